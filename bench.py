@@ -1,0 +1,436 @@
+"""Benchmark of the NVFP4 hot path on B200 -- one JSON line on rank 0.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+
+Workloads (synthetic inputs in the benchmark configurations' shapes):
+  gemv     decode GEMV sweep, M in {1,2,4,8} x (K,N) in {(2048,1536), (768,2048),
+           (4096,14336)}; one step = the 12 calls; GB/s over weight+scale bytes.
+
+`value` is device-timed (CUDA events, max over ranks) with weights resident
+and the step replayed from a CUDA graph; `e2e` times the public Python API
+(nvfp4_linear_forward over ctypes) with the step's activations copied from
+pinned host memory and its outputs copied back.  `--impl reference` times the
+reference's CPU path (the oracle port of nvfp4_matvec, all host threads) on a
+bounded sample of the same workload.  N > 1: one process per GPU (torchrun);
+the GEMV does not shard, so each rank runs an independent replica.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "nvfp4-mojo_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "fused-dequant FP4 GEMM TFLOP/s & HBM GB/s vs peak; MoE layer tok/s at 1–8 GPU"
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+def load_traffic(key):
+    """Per-launch DRAM bytes of the dominant kernel from a committed ncu summary."""
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    d = json.loads(p.read_text())
+    return d.get(key)
+
+
+# ---------------------------------------------------------------------------
+# Clock sampling during the timed region.
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (FileNotFoundError, OSError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        loaded = [s for s in sm if s > 0.5 * max(sm)] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(smax),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# Workload: decode GEMV sweep.
+# ---------------------------------------------------------------------------
+GEMV_SHAPES = [(2048, 1536), (768, 2048), (4096, 14336)]
+GEMV_MS = [1, 2, 4, 8]
+
+
+def gemv_bytes(K, N):
+    return N * K // 2 + N * K // 16 + 4 * N
+
+
+class GemvSweep:
+    name = "gemv"
+    unit = "GB/s"
+    workload = ("decode GEMV sweep: M in {1,2,4,8} x (K,N) in {(2048,1536),(768,2048),"
+                "(4096,14336)}, bf16 activations ~N(0,1), NVFP4 weights (nibbles uniform, "
+                "e4m3 scales U(0.25,4), per-row fp32 scale_2 U(1e-3,1e-2)); bf16 out")
+
+    def __init__(self, device, seed=0):
+        import torch
+        import nvfp4
+        from nvfp4 import synthetic
+
+        self.torch, self.nvfp4 = torch, nvfp4
+        self.dev = device
+        self.sets = 2  # two weight sets alternate per step: reuse distance > L2
+        self.calls = []  # per set: list of (lin, W, SF, X, Y, bytes, is_dominant)
+        for s in range(self.sets):
+            calls = []
+            for (K, N) in GEMV_SHAPES:
+                for M in GEMV_MS:
+                    wd = synthetic.linear_weights_cuda(N, K, seed=seed + 1000 * s + 7 * M + K + N,
+                                                       device=device)
+                    x = torch.randn((M, K), device=device).to(torch.bfloat16)
+                    y = torch.empty((M, N), device=device, dtype=torch.bfloat16)
+                    lin = nvfp4.NvFp4Linear(K, N, weight_scale_2_rows=wd["ws2"])
+                    calls.append((lin, wd["w"], wd["sf"], x, y, gemv_bytes(K, N),
+                                  (K, N) == (4096, 14336)))
+            self.calls.append(calls)
+        self.bytes_per_step = sum(c[5] for c in self.calls[0])
+        self.launches_per_step = len(self.calls[0])
+        self.dominant_bytes = gemv_bytes(4096, 14336)
+        self.dominant_name = "skinny_kernel (decode GEMV, K=4096 N=14336)"
+        self.config = {"workload": self.workload, "shapes_KN": GEMV_SHAPES, "M": GEMV_MS,
+                       "l2": "inputs larger than L2: two weight sets (2 x 143 MB) alternate per step"}
+
+    def run_step(self, i, dom_events=None):
+        from nvfp4 import _lib
+
+        for (lin, W, SF, X, Y, _b, dom) in self.calls[i % self.sets]:
+            if dom and dom_events is not None:
+                e0 = self.torch.cuda.Event(enable_timing=True)
+                e1 = self.torch.cuda.Event(enable_timing=True)
+                e0.record()
+                self.nvfp4.nvfp4_linear_forward(lin, W, SF, X, Y, X.shape[0])
+                e1.record()
+                dom_events.append((e0, e1))
+            else:
+                self.nvfp4.nvfp4_linear_forward(lin, W, SF, X, Y, X.shape[0])
+
+    def units(self, steps):
+        return self.bytes_per_step * steps / 1e9  # GB
+
+    # End to end through the public API: activations H2D from pinned host,
+    # outputs D2H to pinned host, every step.
+    def e2e_setup(self):
+        torch = self.torch
+        self.h_x = [torch.randn(c[3].shape).to(torch.bfloat16).pin_memory() for c in self.calls[0]]
+        self.h_y = [torch.empty(c[4].shape, dtype=torch.bfloat16).pin_memory() for c in self.calls[0]]
+        self.h2d = sum(t.numel() * 2 for t in self.h_x)
+        self.d2h = sum(t.numel() * 2 for t in self.h_y)
+
+    def e2e_step(self, i):
+        calls = self.calls[i % self.sets]
+        for j, (lin, W, SF, X, Y, _b, _d) in enumerate(calls):
+            X.copy_(self.h_x[j], non_blocking=True)
+            self.nvfp4.nvfp4_linear_forward(lin, W, SF, X, Y, X.shape[0])
+            self.h_y[j].copy_(Y, non_blocking=True)
+
+    # CPU baseline: the oracle (nvfp4_matvec restated) on a row sample.
+    def cpu_sample(self, threads, rows_cap=256):
+        from nvfp4 import synthetic
+        from oracle import oracle as O
+
+        work = []
+        for (K, N) in GEMV_SHAPES:
+            n = min(N, rows_cap)
+            wd = synthetic.linear_weights(n, K, seed=5)
+            for M in GEMV_MS:
+                work.append((wd, synthetic.activations(M, K, seed=M), gemv_bytes(K, n)))
+
+        def run():
+            for wd, x, _b in work:
+                O.linear(wd["w"], wd["sf"], x, ws2_rows=wd["ws2"], n_threads=threads)
+
+        nbytes = sum(b for *_x, b in work)
+        desc = (f"all 12 sweep calls on the first {rows_cap} output rows of each shape "
+                f"({nbytes / 1e6:.2f} MB of weights+scales per pass)")
+        return run, nbytes / 1e9, desc
+
+
+WORKLOADS = {"gemv": GemvSweep}
+
+
+# ---------------------------------------------------------------------------
+def dist_setup():
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def max_over_ranks(v, world):
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([v], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def time_cpu(run, units, reps_target_s=10.0, max_reps=50):
+    run()  # warm
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        run()
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= reps_target_s or n >= max_reps:
+            break
+    return units * n / el, n, el
+
+
+def run_reference(args, world, rank):
+    """CPU reference arm: the oracle port of the reference's CPU path."""
+    if rank != 0:
+        return 0
+    from oracle import oracle as O
+
+    wl_cls = WORKLOADS[args.workload]
+    cores = O.host_cores()
+    # Build only what the CPU sample needs (no GPU use).
+    wl = wl_cls.__new__(wl_cls)
+    run, units, desc = wl_cls.cpu_sample(wl, cores)
+    for _ in range(args.warmup):
+        run()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        run()
+    el = time.perf_counter() - t0
+    value = units * args.steps / el
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": wl_cls.unit,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * el / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": wl_cls.workload, "sample": desc},
+        "cpu_baseline": {"value": value, "unit": wl_cls.unit, "cores": cores, "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": value, "unit": wl_cls.unit, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="gemv", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        return run_reference(args, world, rank)
+
+    import torch
+
+    world, rank, local = dist_setup()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    peaks = load_peaks()
+    wl = WORKLOADS[args.workload](device, seed=17 * rank)
+    stream = torch.cuda.Stream(device)
+
+    # Warm-up (also loads the library and JITs nothing: all kernels are prebuilt).
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            wl.run_step(i)
+    torch.cuda.synchronize()
+
+    graphs = None
+    if not args.no_graph:
+        graphs = []
+        for s in range(getattr(wl, "sets", 1)):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                wl.run_step(s)
+            graphs.append(g)
+        torch.cuda.synchronize()
+
+    # Dominant-kernel launch times, measured eagerly inside their own loop on
+    # the launching stream (events inside a graph are not timed).
+    dom_events = []
+    with torch.cuda.stream(stream):
+        for i in range(args.steps):
+            wl.run_step(i, dom_events)
+    torch.cuda.synchronize()
+    dom_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in dom_events) if dom_events else None
+
+    barrier(world)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        for i in range(args.steps):
+            if graphs:
+                graphs[i % len(graphs)].replay()
+            else:
+                wl.run_step(i)
+        ev1.record(stream)
+    torch.cuda.synchronize()
+    # Keep the GPU loaded a little longer so the sampler sees the clocks.
+    t_ms = ev0.elapsed_time(ev1)
+    clk = clocks.stop()
+    barrier(world)
+    t_ms = max_over_ranks(t_ms, world)
+    ms_per_step = t_ms / args.steps
+    value = wl.units(args.steps) * world / (t_ms / 1e3)
+
+    # End to end through the public API with host buffers.
+    wl.e2e_setup()
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            wl.e2e_step(i)
+    torch.cuda.synchronize()
+    barrier(world)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for i in range(args.steps):
+            wl.e2e_step(i)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    e2e_value = wl.units(args.steps) * world / (e2e_ms / 1e3)
+
+    roof = None
+    if dom_ms:
+        achieved = wl.dominant_bytes / (dom_ms / 1e3) / 1e9
+        traffic = load_traffic(wl.name)
+        roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
+                "kernel": wl.dominant_name, "algorithmic_bytes_per_launch": wl.dominant_bytes,
+                "avg_launch_us": dom_ms * 1e3,
+                "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs, copy burst)"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle as O
+
+        cores = O.host_cores()
+        run, units, desc = wl.cpu_sample(cores)
+        v, n, el = time_cpu(run, units)
+        cpu = {"value": v, "unit": wl.unit, "cores": cores, "kind": "port",
+               "sample": f"{desc}; {n} passes in {el:.1f} s, OpenMP over output rows"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": wl.unit, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "config": dict(wl.config, parallelism=(
+                "replicas" if world > 1 else "single GPU"), graph=bool(graphs)),
+            "roofline": roof, "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": wl.unit, "h2d_bytes_per_step": wl.h2d,
+                    "d2h_bytes_per_step": wl.d2h},
+            "clocks": clk, "gpu_launches": wl.launches_per_step * args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        graphs = None
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

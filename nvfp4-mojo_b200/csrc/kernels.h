@@ -1,0 +1,78 @@
+// kernels.h -- host-side launchers of the NVFP4 kernels (internal to libnvfp4).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace nvfp4 {
+
+enum DType : int { kF32 = 0, kBF16 = 1 };
+
+// alpha_n = input_scale[g] * (ws2_rows ? ws2_rows[g][n] : ws2)
+struct AlphaSpec {
+  float input_scale = 1.0f;           // used when input_scales == nullptr
+  const float *input_scales = nullptr;  // per group [G]
+  float ws2 = 1.0f;                   // used when ws2_rows == nullptr
+  const float *ws2_rows = nullptr;      // [G][N]
+  int64_t ws2_group_stride = 0;         // elements
+};
+
+// Grouped NVFP4 weights: group g has rows [N, K/2] at w + g*w_group_stride.
+struct WeightSpec {
+  const uint8_t *w = nullptr;
+  const uint8_t *sf = nullptr;
+  int64_t w_group_stride = 0;   // bytes
+  int64_t sf_group_stride = 0;  // bytes
+  int N = 0;                    // rows (output features)
+  int K = 0;                    // in features
+};
+
+// Full-matrix dequant: out[r, k] = LUT * float(sf) (fp32), or the bf16 of it.
+cudaError_t launch_dequant(const uint8_t *w, const uint8_t *sf, int64_t rows, int64_t K,
+                           void *out, int out_dtype, cudaStream_t s);
+
+// Reference tile form (nvfp4/nvfp4_gemm_gpu.mojo:44-96), fp32 out [tile_m, tile_k].
+cudaError_t launch_dequant_tile(const uint8_t *w, const uint8_t *sf, float *out,
+                                int64_t weight_stride, int64_t scale_stride,
+                                int64_t start_row, int64_t start_col, int64_t tile_m,
+                                int64_t tile_k, cudaStream_t s);
+
+// CUDA-core fp32 linear, any layout by strides (x: [M,K] via xs_m/xs_k,
+// y: [M,N] via ys_m/ys_n).  Faithful to nvfp4_matvec's fp32 arithmetic.
+cudaError_t launch_linear_f32(const WeightSpec &ws, const AlphaSpec &al, const void *x,
+                              int x_dtype, int64_t xs_m, int64_t xs_k, void *y,
+                              int y_dtype, int64_t ys_m, int64_t ys_n, int M,
+                              cudaStream_t s);
+
+// Work item of the grouped skinny kernel: (group, first token slot, tokens).
+struct SkinnyWork {
+  int group;
+  int slot0;
+  int count;
+};
+
+// Tensor-core skinny GEMM (mma.sync m16n8k16, decode in registers).
+// Tokens: for plain linear, slot = token row (x row = slot, y row = slot).
+// For grouped use: `work`/`n_work` list the (group, slot range) items and
+// x_rows / y_rows map a slot to its activation / output row (nullable).
+// silu_gate: W has 2*Nout rows, output n = silu(h[n]) * h[Nout + n].
+struct SkinnyArgs {
+  WeightSpec ws;
+  AlphaSpec al;
+  const uint16_t *x = nullptr;  // bf16 rows of length K, ld x_ld
+  int64_t x_ld = 0;
+  const int32_t *x_rows = nullptr;
+  void *y = nullptr;
+  int y_dtype = kBF16;
+  int64_t y_ld = 0;
+  const int32_t *y_rows = nullptr;
+  int M = 0;                    // tokens (plain mode)
+  const SkinnyWork *work = nullptr;
+  const int *n_work = nullptr;  // device count of work items
+  int work_capacity = 0;        // host upper bound of n_work
+  bool silu_gate = false;
+  int tokens_per_item = 8;      // 8, 16 or 32
+};
+cudaError_t launch_skinny(const SkinnyArgs &a, cudaStream_t s);
+
+}  // namespace nvfp4

@@ -1,0 +1,380 @@
+// linear_kernels.cu -- NVFP4 dequant, decode-GEMV/skinny GEMM and the
+// CUDA-core fp32 linear (sm_100a).
+//
+// Reference behaviour these kernels reproduce:
+//   * dequant: nvfp4/nvfp4_gemm_gpu.mojo:44-96 (load_and_dequant_fp4_tile),
+//     nvfp4/config.mojo:106-121 (unpack_fp4_pair, dequant_fp4);
+//   * linear: nvfp4/deltanet.mojo:549-584 (nvfp4_matvec) and the kernel body
+//     nvfp4/nvfp4_gemm_gpu.mojo:148-182: y = alpha * dequant(W) @ x with fp32
+//     accumulation, alpha = input_scale * weight_scale_2 applied at the end.
+#include "kernels.h"
+#include "nvfp4_common.cuh"
+
+namespace nvfp4 {
+
+// ---------------------------------------------------------------------------
+// Dequant.  One thread per 8 codes (one 32-bit word).  HBM-bound: reads
+// 4 B codes + 1/2 B scale, writes 32 B (fp32) or 16 B (bf16) per thread.
+// ---------------------------------------------------------------------------
+__global__ void dequant_f32_kernel(const uint32_t *__restrict__ w,
+                                   const uint8_t *__restrict__ sf, int64_t n_words,
+                                   int64_t words_per_row, int64_t K, float4 *__restrict__ out) {
+  int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= n_words) return;
+  int64_t row = i / words_per_row, wi = i % words_per_row;
+  uint32_t v = w[i];
+  float s = e4m3_to_f32(sf[row * (K / kGroup) + (wi * 8) / kGroup]);
+  float f[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) f[j] = e2m1_to_f32((v >> (4 * j)) & 15u) * s;
+  out[2 * i] = make_float4(f[0], f[1], f[2], f[3]);
+  out[2 * i + 1] = make_float4(f[4], f[5], f[6], f[7]);
+}
+
+// bf16 output through the exact tensor-core decode (decode8_natural), then
+// * 2^7: this is the operand the GEMM/GEMV kernels feed their MMAs, so its
+// bit-exactness test covers theirs.
+__global__ void dequant_bf16_kernel(const uint32_t *__restrict__ w,
+                                    const uint8_t *__restrict__ sf, int64_t n_words,
+                                    int64_t words_per_row, int64_t K, uint4 *__restrict__ out) {
+  int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= n_words) return;
+  int64_t row = i / words_per_row, wi = i % words_per_row;
+  uint32_t s2 = scale_to_bf16x2_2p119(sf[row * (K / kGroup) + (wi * 8) / kGroup]);
+  uint32_t d[4];
+  decode8_natural(w[i], s2, d);
+  const uint32_t two7 = 0x43004300u;  // bf16x2(128, 128)
+  out[i] = make_uint4(bf16x2_mul(d[0], two7), bf16x2_mul(d[1], two7),
+                      bf16x2_mul(d[2], two7), bf16x2_mul(d[3], two7));
+}
+
+cudaError_t launch_dequant(const uint8_t *w, const uint8_t *sf, int64_t rows, int64_t K,
+                           void *out, int out_dtype, cudaStream_t s) {
+  int64_t words_per_row = K / 8;
+  int64_t n = rows * words_per_row;
+  if (n == 0) return cudaSuccess;
+  int threads = 256;
+  int64_t blocks = (n + threads - 1) / threads;
+  if (out_dtype == kF32)
+    dequant_f32_kernel<<<(unsigned)blocks, threads, 0, s>>>(
+        reinterpret_cast<const uint32_t *>(w), sf, n, words_per_row, K,
+        reinterpret_cast<float4 *>(out));
+  else
+    dequant_bf16_kernel<<<(unsigned)blocks, threads, 0, s>>>(
+        reinterpret_cast<const uint32_t *>(w), sf, n, words_per_row, K,
+        reinterpret_cast<uint4 *>(out));
+  return cudaGetLastError();
+}
+
+// nvfp4/nvfp4_gemm_gpu.mojo:44-96 -- one thread per packed byte of the tile.
+__global__ void dequant_tile_kernel(const uint8_t *__restrict__ w, const uint8_t *__restrict__ sf,
+                                    float *__restrict__ out, int64_t weight_stride,
+                                    int64_t scale_stride, int64_t start_row, int64_t start_col,
+                                    int64_t tile_m, int64_t tile_k) {
+  int64_t half = tile_k / kPack;
+  int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= tile_m * half) return;
+  int64_t m = i / half, k = i % half;
+  int64_t row = start_row + m;
+  uint32_t p = w[row * weight_stride + start_col / kPack + k];
+  float s = e4m3_to_f32(sf[row * scale_stride + (start_col + k * kPack) / kGroup]);
+  out[m * tile_k + 2 * k] = e2m1_to_f32(p & 15u) * s;
+  out[m * tile_k + 2 * k + 1] = e2m1_to_f32((p >> 4) & 15u) * s;
+}
+
+cudaError_t launch_dequant_tile(const uint8_t *w, const uint8_t *sf, float *out,
+                                int64_t weight_stride, int64_t scale_stride,
+                                int64_t start_row, int64_t start_col, int64_t tile_m,
+                                int64_t tile_k, cudaStream_t s) {
+  int64_t n = tile_m * (tile_k / kPack);
+  if (n == 0) return cudaSuccess;
+  int threads = 256;
+  dequant_tile_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, s>>>(
+      w, sf, out, weight_stride, scale_stride, start_row, start_col, tile_m, tile_k);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// CUDA-core fp32 linear: one warp per output row, 8 tokens per warp, lanes
+// stride over the 16-element groups; fp32 products LUT*scale*x exactly as
+// nvfp4_matvec forms them, summed per lane then by warp shuffle.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float load_act(const void *x, int dt, int64_t idx) {
+  if (dt == kF32) return reinterpret_cast<const float *>(x)[idx];
+  return __uint_as_float((uint32_t)reinterpret_cast<const uint16_t *>(x)[idx] << 16);
+}
+
+__device__ __forceinline__ void store_out(void *y, int dt, int64_t idx, float v) {
+  if (dt == kF32)
+    reinterpret_cast<float *>(y)[idx] = v;
+  else
+    reinterpret_cast<uint16_t *>(y)[idx] = f32_to_bf16_bits(v);
+}
+
+__device__ __forceinline__ float alpha_of(const AlphaSpec &al, int g, int n) {
+  float ins = al.input_scales ? al.input_scales[g] : al.input_scale;
+  float w2 = al.ws2_rows ? al.ws2_rows[(int64_t)g * al.ws2_group_stride + n] : al.ws2;
+  return ins * w2;
+}
+
+__global__ void __launch_bounds__(256) linear_f32_kernel(WeightSpec ws, AlphaSpec al,
+                                                         const void *x, int x_dt, int64_t xs_m,
+                                                         int64_t xs_k, void *y, int y_dt,
+                                                         int64_t ys_m, int64_t ys_n, int M) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int n = blockIdx.x * 8 + warp;
+  const int m0 = blockIdx.y * 8;
+  if (n >= ws.N) return;
+  const int K = ws.K;
+  const int groups = K / kGroup;
+  const uint8_t *wr = ws.w + (int64_t)n * (K / kPack);
+  const uint8_t *sr = ws.sf + (int64_t)n * groups;
+  const int mcount = min(8, M - m0);
+  float acc[8];
+#pragma unroll
+  for (int m = 0; m < 8; ++m) acc[m] = 0.0f;
+  for (int gi = lane; gi < groups; gi += 32) {
+    float s = e4m3_to_f32(sr[gi]);
+    const uint8_t *wb = wr + gi * (kGroup / kPack);
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      uint32_t p = wb[b];
+      int64_t k = (int64_t)gi * kGroup + 2 * b;
+      float w0 = e2m1_to_f32(p & 15u) * s;
+      float w1 = e2m1_to_f32((p >> 4) & 15u) * s;
+#pragma unroll
+      for (int m = 0; m < 8; ++m) {
+        if (m < mcount) {
+          int64_t base = (int64_t)(m0 + m) * xs_m;
+          acc[m] += w0 * load_act(x, x_dt, base + k * xs_k);
+          acc[m] += w1 * load_act(x, x_dt, base + (k + 1) * xs_k);
+        }
+      }
+    }
+  }
+  float alpha = alpha_of(al, 0, n);
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    float v = acc[m];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0 && m < mcount) store_out(y, y_dt, (int64_t)(m0 + m) * ys_m + (int64_t)n * ys_n, v * alpha);
+  }
+}
+
+cudaError_t launch_linear_f32(const WeightSpec &ws, const AlphaSpec &al, const void *x,
+                              int x_dtype, int64_t xs_m, int64_t xs_k, void *y, int y_dtype,
+                              int64_t ys_m, int64_t ys_n, int M, cudaStream_t s) {
+  if (M == 0 || ws.N == 0) return cudaSuccess;
+  dim3 grid((ws.N + 7) / 8, (M + 7) / 8);
+  linear_f32_kernel<<<grid, 256, 0, s>>>(ws, al, x, x_dtype, xs_m, xs_k, y, y_dtype, ys_m,
+                                         ys_n, M);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Skinny tensor-core GEMM (decode GEMV for M <= 8; grouped expert GEMMs with
+// few tokens per expert).  HBM-bound on the weights: every weight byte is
+// streamed once per CTA with 128-bit non-allocating loads.
+//
+// CTA = 16 output features x (8*NT) token slots; its warps split K in rounds
+// of 128.  In a round, lane (g = lane/4, c = lane%4) loads 16 bytes (32 codes)
+// of rows g and g+8 at k = k0 + 32c, decodes them in registers to bf16
+// (LUT*scale*2^-7) and issues 8 mma.m16n8k16 per token tile.  The MMA's 16
+// logical k slots are a permutation of physical k; the activation fragments
+// use the same permutation (prmt of the token's 32 activations), so the sum is
+// unchanged.  Partial sums of the warps are reduced in shared memory in a
+// fixed order, then scaled by alpha*2^7 and stored.
+// ---------------------------------------------------------------------------
+template <int NT, bool SILU>
+__global__ void __launch_bounds__(256) skinny_kernel(SkinnyArgs a) {
+  constexpr int NACC = NT * 4 * (SILU ? 2 : 1);
+  __shared__ float red[8][NACC][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const int g = lane >> 2, c = lane & 3;
+
+  int group = 0, slot0, count;
+  if (a.work) {
+    if ((int)blockIdx.y >= *a.n_work) return;
+    SkinnyWork wk = a.work[blockIdx.y];
+    group = wk.group;
+    slot0 = wk.slot0;
+    count = wk.count;
+  } else {
+    slot0 = blockIdx.y * (8 * NT);
+    count = min(8 * NT, a.M - slot0);
+  }
+  const int Nout = SILU ? a.ws.N / 2 : a.ws.N;
+  const int row0 = blockIdx.x * 16;
+  const int K = a.ws.K;
+  const int64_t wld = K / kPack, sld = K / kGroup;
+  const uint8_t *W = a.ws.w + (int64_t)group * a.ws.w_group_stride;
+  const uint8_t *SF = a.ws.sf + (int64_t)group * a.ws.sf_group_stride;
+  // Rows past N are clamped for loading (always valid memory), never stored.
+  const int ra = min(row0 + g, Nout - 1), rb = min(row0 + g + 8, Nout - 1);
+
+  const uint16_t *xrow[NT];
+  bool xval[NT];
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+    int sl = 8 * t + g;
+    xval[t] = sl < count;
+    int slot = slot0 + (xval[t] ? sl : 0);
+    int64_t r = a.x_rows ? a.x_rows[slot] : slot;
+    xrow[t] = a.x + r * a.x_ld;
+  }
+
+  float acc[NT][4], accu[NT][4];
+#pragma unroll
+  for (int t = 0; t < NT; ++t)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[t][i] = accu[t][i] = 0.0f;
+
+  const int rounds = (K + 127) / 128;
+  for (int r = warp; r < rounds; r += nwarps) {
+    const int kc = r * 128 + 32 * c;
+    const bool kval = kc < K;
+    uint4 wa = make_uint4(0, 0, 0, 0), wb = wa, wua = wa, wub = wa;
+    uint32_t sa = 0, sb = 0, sua = 0, sub = 0;
+    if (kval) {
+      wa = ldg_nc_v4(W + ra * wld + kc / 2);
+      wb = ldg_nc_v4(W + rb * wld + kc / 2);
+      sa = *reinterpret_cast<const uint16_t *>(SF + ra * sld + kc / kGroup);
+      sb = *reinterpret_cast<const uint16_t *>(SF + rb * sld + kc / kGroup);
+      if (SILU) {
+        wua = ldg_nc_v4(W + (ra + Nout) * wld + kc / 2);
+        wub = ldg_nc_v4(W + (rb + Nout) * wld + kc / 2);
+        sua = *reinterpret_cast<const uint16_t *>(SF + (ra + Nout) * sld + kc / kGroup);
+        sub = *reinterpret_cast<const uint16_t *>(SF + (rb + Nout) * sld + kc / kGroup);
+      }
+    }
+    uint4 xv[NT][4];
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        xv[t][q] = (kval && xval[t])
+                       ? *reinterpret_cast<const uint4 *>(xrow[t] + kc + 8 * q)
+                       : make_uint4(0, 0, 0, 0);
+
+    const uint32_t wa_[4] = {wa.x, wa.y, wa.z, wa.w}, wb_[4] = {wb.x, wb.y, wb.z, wb.w};
+    const uint32_t wua_[4] = {wua.x, wua.y, wua.z, wua.w}, wub_[4] = {wub.x, wub.y, wub.z, wub.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int sh = (q >> 1) * 8;
+      uint32_t da[4], db[4];
+      {
+        uint32_t s2a = scale_to_bf16x2_2p119((sa >> sh) & 0xffu);
+        uint32_t s2b = scale_to_bf16x2_2p119((sb >> sh) & 0xffu);
+        decode8_raw_pairs(wa_[q], da);
+        decode8_raw_pairs(wb_[q], db);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          da[i] = bf16x2_mul(da[i], s2a);
+          db[i] = bf16x2_mul(db[i], s2b);
+        }
+      }
+      uint32_t dua[4], dub[4];
+      if (SILU) {
+        uint32_t s2a = scale_to_bf16x2_2p119((sua >> sh) & 0xffu);
+        uint32_t s2b = scale_to_bf16x2_2p119((sub >> sh) & 0xffu);
+        decode8_raw_pairs(wua_[q], dua);
+        decode8_raw_pairs(wub_[q], dub);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          dua[i] = bf16x2_mul(dua[i], s2a);
+          dub[i] = bf16x2_mul(dub[i], s2b);
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t A[4] = {da[2 * h], db[2 * h], da[2 * h + 1], db[2 * h + 1]};
+        uint32_t AU[4];
+        if (SILU) {
+          AU[0] = dua[2 * h];
+          AU[1] = dub[2 * h];
+          AU[2] = dua[2 * h + 1];
+          AU[3] = dub[2 * h + 1];
+        }
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          const uint32_t x0 = h ? xv[t][q].y : xv[t][q].x;
+          const uint32_t x1 = h ? xv[t][q].w : xv[t][q].z;
+          const uint32_t b0 = prmt(x0, x1, 0x5410u), b1 = prmt(x0, x1, 0x7632u);
+          mma_bf16_16816(acc[t], A, b0, b1);
+          if (SILU) mma_bf16_16816(accu[t], AU, b0, b1);
+        }
+      }
+    }
+  }
+
+  // Cross-warp reduction in a fixed order.
+#pragma unroll
+  for (int t = 0; t < NT; ++t)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      red[warp][t * 4 + i][lane] = acc[t][i];
+      if (SILU) red[warp][NT * 4 + t * 4 + i][lane] = accu[t][i];
+    }
+  __syncthreads();
+
+  // Output o = token_local * 16 + row_local; consecutive threads write
+  // consecutive features of one token.
+  const int n_out = 16 * 8 * NT;
+  for (int o = threadIdx.x; o < n_out; o += blockDim.x) {
+    const int tl = o >> 4, rl = o & 15;
+    const int t = tl >> 3, tt = tl & 7;
+    const int cc = tt >> 1, lo = tt & 1;
+    const int gg = rl & 7, reg = (rl >> 3) * 2 + lo;
+    const int ln = gg * 4 + cc;
+    const int n = row0 + rl;
+    if (tl >= count || n >= Nout) continue;
+    float v = 0.0f, vu = 0.0f;
+    for (int w = 0; w < nwarps; ++w) {
+      v += red[w][t * 4 + reg][ln];
+      if (SILU) vu += red[w][NT * 4 + t * 4 + reg][ln];
+    }
+    float out;
+    if (SILU) {
+      float hg = v * (alpha_of(a.al, group, n) * kDecodeUnscale);
+      float hu = vu * (alpha_of(a.al, group, n + Nout) * kDecodeUnscale);
+      out = silu_f32(hg) * hu;
+    } else {
+      out = v * (alpha_of(a.al, group, n) * kDecodeUnscale);
+    }
+    const int slot = slot0 + tl;
+    const int64_t yr = a.y_rows ? a.y_rows[slot] : slot;
+    store_out(a.y, a.y_dtype, yr * a.y_ld + n, out);
+  }
+}
+
+cudaError_t launch_skinny(const SkinnyArgs &a, cudaStream_t s) {
+  const int Nout = a.silu_gate ? a.ws.N / 2 : a.ws.N;
+  if (Nout == 0) return cudaSuccess;
+  const int tpi = a.tokens_per_item;
+  const int items = a.work ? a.work_capacity : (a.M + tpi - 1) / tpi;
+  if (items == 0) return cudaSuccess;
+  const int rounds = (a.ws.K + 127) / 128;
+  const int nwarps = rounds < 8 ? rounds : 8;
+  dim3 grid((Nout + 15) / 16, items);
+  dim3 block(32 * nwarps);
+#define NVFP4_SKINNY(NT_)                                                  \
+  do {                                                                     \
+    if (a.silu_gate)                                                       \
+      skinny_kernel<NT_, true><<<grid, block, 0, s>>>(a);                  \
+    else                                                                   \
+      skinny_kernel<NT_, false><<<grid, block, 0, s>>>(a);                 \
+  } while (0)
+  if (tpi == 8)
+    NVFP4_SKINNY(1);
+  else if (tpi == 16)
+    NVFP4_SKINNY(2);
+  else if (tpi == 32)
+    NVFP4_SKINNY(4);
+  else
+    return cudaErrorInvalidValue;
+#undef NVFP4_SKINNY
+  return cudaGetLastError();
+}
+
+}  // namespace nvfp4

@@ -1,0 +1,102 @@
+"""Loader of libnvfp4.so (the C ABI of include/nvfp4.h) via ctypes.
+
+The shared library is built in-tree (``make -C nvfp4-mojo_b200``) and loaded
+from this folder.  There is no fallback: if the library is missing or does
+not load, every compute call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+_HERE = Path(__file__).resolve().parent
+LIB_PATH = Path(os.environ.get("NVFP4_LIB", _HERE / "libnvfp4.so"))
+
+NVFP4_OK = 0
+NVFP4_ERR_INVALID_ARG = -1
+NVFP4_ERR_UNSUPPORTED = -2
+NVFP4_ERR_CUDA = -3
+NVFP4_ERR_WORKSPACE = -4
+NVFP4_ERR_TIMEOUT = -5
+
+DTYPE_F32 = 0
+DTYPE_BF16 = 1
+
+FLAG_W4A4 = 0x1
+FLAG_FORCE_SKINNY = 0x2
+FLAG_FORCE_TC = 0x4
+FLAG_FORCE_F32 = 0x8
+
+_STATUS_NAMES = {
+    NVFP4_ERR_INVALID_ARG: "invalid argument",
+    NVFP4_ERR_UNSUPPORTED: "unsupported",
+    NVFP4_ERR_CUDA: "CUDA error",
+    NVFP4_ERR_WORKSPACE: "workspace too small",
+    NVFP4_ERR_TIMEOUT: "device wait timed out",
+}
+
+
+class Nvfp4Error(RuntimeError):
+    """A libnvfp4 entry point returned a negative status."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(f"libnvfp4: {_STATUS_NAMES.get(status, status)}: {message}")
+        self.status = status
+
+
+class LinearDesc(ctypes.Structure):
+    """struct nvfp4_linear_desc (mirrors NvFp4Linear, nvfp4/config.mojo:64-103)."""
+
+    _fields_ = [
+        ("in_features", ctypes.c_int64),
+        ("out_features", ctypes.c_int64),
+        ("input_scale", ctypes.c_float),
+        ("weight_scale_2", ctypes.c_float),
+        ("weight_scale_2_rows", ctypes.c_void_p),
+    ]
+
+
+_vp = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_int = ctypes.c_int
+_u32 = ctypes.c_uint32
+_f32 = ctypes.c_float
+
+# name -> (restype, argtypes); every symbol include/nvfp4.h declares.
+SIGNATURES = {
+    "nvfp4_abi_version": (_int, []),
+    "nvfp4_last_error_string": (ctypes.c_char_p, []),
+    "nvfp4_linear_forward": (_int, [ctypes.POINTER(LinearDesc), _vp, _vp, _vp, _int, _vp, _int,
+                                    _i64, _u32, _vp]),
+    "nvfp4_gemm_kernel": (_int, [_i64, _i64, _i64, _vp, _vp, _vp, _int, _vp, _int, _f32, _vp]),
+    "nvfp4_matvec": (_int, [ctypes.POINTER(LinearDesc), _vp, _vp, _vp, _vp, _vp]),
+    "nvfp4_dequant_tile": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
+    "nvfp4_dequant": (_int, [_vp, _vp, _i64, _i64, _vp, _int, _vp]),
+}
+
+_lib = None
+
+
+def load():
+    """Load libnvfp4.so once; raises if it is absent or incomplete."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise ImportError(
+            f"libnvfp4.so not found at {LIB_PATH}: build it with "
+            "`make -C nvfp4-mojo_b200` (there is no CPU fallback)")
+    L = ctypes.CDLL(str(LIB_PATH))
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def check(rc: int) -> None:
+    if rc != NVFP4_OK:
+        msg = load().nvfp4_last_error_string().decode(errors="replace")
+        raise Nvfp4Error(rc, msg)

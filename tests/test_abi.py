@@ -1,0 +1,69 @@
+"""The C ABI library loads, exports every symbol include/nvfp4.h declares, and
+its host-side validation rejects bad calls before any CUDA work (CPU only)."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def declared_symbols():
+    names = set()
+    for h in (ROOT / "include").glob("*.h"):
+        src = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        names |= set(re.findall(r"\b(nvfp4_\w+)\s*\(", src))
+    return sorted(names)
+
+
+def test_header_declares_entry_points():
+    syms = declared_symbols()
+    for must in ("nvfp4_linear_forward", "nvfp4_gemm_kernel", "nvfp4_matvec",
+                 "nvfp4_dequant_tile", "nvfp4_dequant", "nvfp4_last_error_string"):
+        assert must in syms
+
+
+def test_library_exports_every_declared_symbol():
+    from nvfp4 import _lib
+
+    L = _lib.load()
+    for name in declared_symbols():
+        assert hasattr(L, name), f"libnvfp4.so does not export {name}"
+        assert name in _lib.SIGNATURES, f"ctypes signature missing for {name}"
+    assert L.nvfp4_abi_version() == 1
+
+
+def test_validation_errors_without_gpu():
+    from nvfp4 import _lib
+
+    L = _lib.load()
+    desc = _lib.LinearDesc(2048, 1536, 1.0, 1.0, None)
+    rc = L.nvfp4_linear_forward(ctypes.byref(desc), None, None, None, 1, None, 1, 4, 0, None)
+    assert rc == _lib.NVFP4_ERR_INVALID_ARG
+    assert b"null" in L.nvfp4_last_error_string()
+    bad = _lib.LinearDesc(2050, 1536, 1.0, 1.0, None)  # K not a multiple of 16
+    rc = L.nvfp4_linear_forward(ctypes.byref(bad), 16, 16, 16, 1, 16, 1, 4, 0, None)
+    assert rc == _lib.NVFP4_ERR_INVALID_ARG
+    assert b"multiple of 16" in L.nvfp4_last_error_string()
+    rc = L.nvfp4_linear_forward(None, 16, 16, 16, 1, 16, 1, 4, 0, None)
+    assert rc == _lib.NVFP4_ERR_INVALID_ARG
+    rc = L.nvfp4_linear_forward(ctypes.byref(desc), 16, 16, 16, 7, 16, 1, 4, 0, None)
+    assert rc == _lib.NVFP4_ERR_INVALID_ARG and b"dtype" in L.nvfp4_last_error_string()
+    rc = L.nvfp4_dequant_tile(16, 16, 16, 1024, 128, 0, 1, 4, 64, None)
+    assert rc == _lib.NVFP4_ERR_INVALID_ARG  # odd start_col
+    with pytest.raises(_lib.Nvfp4Error):
+        _lib.check(_lib.NVFP4_ERR_INVALID_ARG)
+
+
+def test_python_api_refuses_host_tensors():
+    import torch
+    import nvfp4
+
+    lin = nvfp4.NvFp4Linear(64, 32)
+    w = torch.zeros((32, 32), dtype=torch.uint8)
+    sf = torch.zeros((32, 4), dtype=torch.uint8)
+    x = torch.zeros((2, 64), dtype=torch.bfloat16)
+    y = torch.zeros((2, 32), dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        nvfp4.nvfp4_linear_forward(lin, w, sf, x, y, 2)

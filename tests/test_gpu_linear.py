@@ -1,0 +1,193 @@
+"""GPU parity of the NVFP4 dequant / GEMV / linear kernels against the CPU
+oracle, through the C ABI (via the nvfp4 Python mirror).
+
+Tolerances: dequant bit-exact (incl. -0.0 and NaN); GEMV/GEMM
+max|err| <= 2e-2 * RMS(ref) for bf16 operands with fp32 accumulation; the
+fp32-activation path (nvfp4_matvec arithmetic) <= 1e-5 * RMS(ref).
+"""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+TOL_BF16 = 2e-2
+TOL_F32 = 1e-5
+
+
+def rel_err(got, ref):
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    rms = np.sqrt(np.mean(ref * ref))
+    return float(np.abs(got - ref).max() / rms)
+
+
+def dev(a, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    return t if dtype is None else t.to(dtype)
+
+
+def exhaustive_weights():
+    """256 rows (row r uses blockscale code r in every group) x K = 256 with
+    each 16-group holding codes 0..15 in k order (low nibble = even k)."""
+    rows, K = 256, 256
+    codes = np.tile(np.arange(16, dtype=np.uint8), (rows, K // 16))
+    w = (codes[:, 0::2] | (codes[:, 1::2] << 4)).astype(np.uint8)
+    sf = np.repeat(np.arange(256, dtype=np.uint8)[:, None], K // 16, axis=1)
+    return w, sf
+
+
+def bits32(a):
+    a = np.asarray(a, np.float32).copy()
+    nan = np.isnan(a)
+    b = a.view(np.uint32).copy()
+    b[nan] = 0x7FC00000
+    return b
+
+
+def test_dequant_fp32_bit_exact_all_codes(O, cuda):
+    import nvfp4
+
+    w, sf = exhaustive_weights()
+    ref = O.dequant(w, sf)
+    got = nvfp4.dequant(dev(w), dev(sf), torch.float32).cpu().numpy()
+    assert np.array_equal(bits32(got), bits32(ref))
+    assert np.signbit(got[0, 8]) and got[0, 8] == 0.0  # code 8 -> -0.0
+
+
+def test_dequant_bf16_bit_exact_all_codes(O, cuda):
+    """The bf16 form is the tensor-core operand decode (LUT*scale*2^-7, then
+    *2^7): it must equal the exact fp32 dequant rounded to bf16 (which is
+    exact), sign of zero and NaN included."""
+    import nvfp4
+
+    w, sf = exhaustive_weights()
+    ref = torch.from_numpy(O.dequant(w, sf)).to(torch.bfloat16).view(torch.int16).numpy()
+    got = nvfp4.dequant(dev(w), dev(sf), torch.bfloat16).cpu()
+    gb = got.view(torch.int16).numpy().copy()
+    isnan = torch.isnan(got.float()).numpy()
+    assert np.array_equal(isnan, np.isnan(O.dequant(w, sf)))
+    assert np.array_equal(gb[~isnan], ref[~isnan])
+
+
+def test_dequant_tile_matches_reference_form(O, cuda):
+    import nvfp4
+    from nvfp4 import synthetic
+
+    N, K = 1536, 2048
+    wd = synthetic.linear_weights(N, K, seed=0)
+    out = torch.empty((7, 64), dtype=torch.float32, device=cuda)
+    nvfp4.load_and_dequant_fp4_tile(dev(wd["w"]), dev(wd["sf"]), out, K // 2, K // 16,
+                                    5, 48, 7, 64)
+    ref = O.dequant_tile(wd["w"], wd["sf"], K // 2, K // 16, 5, 48, 7, 64)
+    assert np.array_equal(bits32(out.cpu().numpy()), bits32(ref))
+
+
+def test_config0_fp32_linear_and_matvec(O, cuda):
+    """Single NVFP4 linear, fp32 x [4, 2048], W [1536, 1024]: the fp32 path
+    (nvfp4_matvec arithmetic), scalar and per-row weight_scale_2."""
+    import nvfp4
+    from nvfp4 import synthetic
+
+    N, K, M = 1536, 2048, 4
+    wd = synthetic.linear_weights(N, K, seed=0)
+    x = synthetic.activations(M, K, seed=1)
+    W, SF, X = dev(wd["w"]), dev(wd["sf"]), dev(x)
+    lin = nvfp4.NvFp4Linear(K, N, input_scale=1.0, weight_scale_2=1.0,
+                            weight_scale_2_rows=dev(wd["ws2"]))
+    y = torch.empty((M, N), dtype=torch.float32, device=cuda)
+    nvfp4.nvfp4_linear_forward(lin, W, SF, X, y, M)
+    ref = O.linear(wd["w"], wd["sf"], x, ws2_rows=wd["ws2"])
+    assert rel_err(y.cpu().numpy(), ref) <= TOL_F32
+    lin_s = nvfp4.NvFp4Linear(K, N, input_scale=0.5, weight_scale_2=0.003)
+    r = torch.empty(N, dtype=torch.float32, device=cuda)
+    nvfp4.nvfp4_matvec(lin_s, W, SF, X[2].contiguous(), r)
+    ref2 = O.matvec(wd["w"], wd["sf"], x[2], input_scale=0.5, ws2=0.003)
+    assert rel_err(r.cpu().numpy(), ref2) <= TOL_F32
+
+
+@pytest.mark.parametrize("K,N", [(2048, 1536), (768, 2048), (4096, 14336)])
+@pytest.mark.parametrize("M", [1, 2, 4, 8])
+def test_decode_gemv_sweep(O, cuda, K, N, M):
+    """Decode GEMV sweep: bf16 x, tensor-core skinny path, fp32 and bf16 out."""
+    import nvfp4
+    from nvfp4 import synthetic
+
+    wd = synthetic.linear_weights(N, K, seed=100 + K + N)
+    x = synthetic.bf16_round(synthetic.activations(M, K, seed=M))
+    lin = nvfp4.NvFp4Linear(K, N, weight_scale_2_rows=dev(wd["ws2"]))
+    W, SF, X = dev(wd["w"]), dev(wd["sf"]), dev(x, torch.bfloat16)
+    y32 = torch.empty((M, N), dtype=torch.float32, device=cuda)
+    nvfp4.nvfp4_linear_forward(lin, W, SF, X, y32, M, flags=nvfp4._lib.FLAG_FORCE_SKINNY)
+    ybf = nvfp4.nvfp4_linear(lin, W, SF, X)
+    ref = O.linear(wd["w"], wd["sf"], x, ws2_rows=wd["ws2"])
+    # Exact decode + fp32 accumulation: only summation order differs.
+    assert rel_err(y32.cpu().numpy(), ref) <= 1e-5
+    assert rel_err(ybf.float().cpu().numpy(), ref) <= TOL_BF16
+
+
+@pytest.mark.parametrize("M", [3, 13, 17, 33, 64])
+def test_skinny_ragged_shapes(O, cuda, M):
+    """N not a multiple of 16, K = 32 * odd, several token items."""
+    import nvfp4
+    from nvfp4 import synthetic
+
+    N, K = 100, 96 * 3
+    wd = synthetic.linear_weights(N, K, seed=M)
+    x = synthetic.bf16_round(synthetic.activations(M, K, seed=M + 1))
+    lin = nvfp4.NvFp4Linear(K, N, input_scale=1.5, weight_scale_2=0.01)
+    y = torch.full((M, N), float("nan"), dtype=torch.float32, device=cuda)
+    nvfp4.nvfp4_linear_forward(lin, dev(wd["w"]), dev(wd["sf"]), dev(x, torch.bfloat16), y, M)
+    ref = O.linear(wd["w"], wd["sf"], x, input_scale=1.5, ws2=0.01)
+    assert not torch.isnan(y).any()  # every output written
+    assert rel_err(y.cpu().numpy(), ref) <= 1e-5
+
+
+def test_fp32_path_odd_k(O, cuda):
+    """K % 32 == 16 goes to the CUDA-core fp32 path (any K multiple of 16)."""
+    import nvfp4
+    from nvfp4 import synthetic
+
+    N, K, M = 40, 48, 5
+    wd = synthetic.linear_weights(N, K, seed=9)
+    x = synthetic.bf16_round(synthetic.activations(M, K, seed=10))
+    lin = nvfp4.NvFp4Linear(K, N)
+    y = nvfp4.nvfp4_linear(lin, dev(wd["w"]), dev(wd["sf"]), dev(x, torch.bfloat16),
+                           out_dtype=torch.float32)
+    ref = O.linear(wd["w"], wd["sf"], x)
+    assert rel_err(y.cpu().numpy(), ref) <= TOL_F32
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+def test_gemm_kernel_reference_layout(O, cuda, dt):
+    """nvfp4_gemm_kernel: act [K, N_tok] -> out [M_out, N_tok] (reference layout)."""
+    import nvfp4
+    from nvfp4 import synthetic
+
+    M_out, K, N_tok = 256, 512, 6
+    wd = synthetic.linear_weights(M_out, K, seed=21)
+    x = synthetic.bf16_round(synthetic.activations(N_tok, K, seed=22))
+    act = dev(np.ascontiguousarray(x.T), dt)
+    out = torch.empty((M_out, N_tok), dtype=torch.float32, device=cuda)
+    nvfp4.nvfp4_gemm_kernel(dev(wd["w"]), dev(wd["sf"]), act, out, alpha=0.125)
+    ref = O.gemm_kernel(wd["w"], wd["sf"], np.ascontiguousarray(x.T), 0.125)
+    assert rel_err(out.cpu().numpy(), ref) <= TOL_F32
+
+
+def test_nan_scale_propagates_and_empty_batch(O, cuda):
+    import nvfp4
+    from nvfp4 import synthetic
+
+    N, K, M = 32, 128, 2
+    wd = synthetic.linear_weights(N, K, seed=5)
+    wd["sf"][3, 2] = 0x7F  # NaN blockscale in row 3
+    x = synthetic.bf16_round(synthetic.activations(M, K, seed=6))
+    lin = nvfp4.NvFp4Linear(K, N)
+    y = nvfp4.nvfp4_linear(lin, dev(wd["w"]), dev(wd["sf"]), dev(x, torch.bfloat16),
+                           out_dtype=torch.float32).cpu().numpy()
+    assert np.isnan(y[:, 3]).all()
+    assert not np.isnan(np.delete(y, 3, axis=1)).any()
+    empty = torch.empty((0, N), dtype=torch.bfloat16, device=cuda)
+    nvfp4.nvfp4_linear_forward(lin, dev(wd["w"]), dev(wd["sf"]),
+                               torch.empty((0, K), dtype=torch.bfloat16, device=cuda), empty, 0)
+    torch.cuda.synchronize()
