@@ -158,19 +158,18 @@ class GemvSweep:
         self.config = {"workload": self.workload, "shapes_KN": GEMV_SHAPES, "M": GEMV_MS,
                        "l2": "inputs larger than L2: two weight sets (2 x 143 MB) alternate per step"}
 
-    def run_step(self, i, dom_events=None):
-        from nvfp4 import _lib
+    def run_step(self, i):
+        for (lin, W, SF, X, Y, _b, _dom) in self.calls[i % self.sets]:
+            self.nvfp4.nvfp4_linear_forward(lin, W, SF, X, Y, X.shape[0])
 
+    def run_dominant(self, i):
+        """The K=4096, N=14336 launches of one step (M = 1, 2, 4, 8)."""
+        n = 0
         for (lin, W, SF, X, Y, _b, dom) in self.calls[i % self.sets]:
-            if dom and dom_events is not None:
-                e0 = self.torch.cuda.Event(enable_timing=True)
-                e1 = self.torch.cuda.Event(enable_timing=True)
-                e0.record()
+            if dom:
                 self.nvfp4.nvfp4_linear_forward(lin, W, SF, X, Y, X.shape[0])
-                e1.record()
-                dom_events.append((e0, e1))
-            else:
-                self.nvfp4.nvfp4_linear_forward(lin, W, SF, X, Y, X.shape[0])
+                n += 1
+        return n
 
     def units(self, steps):
         return self.bytes_per_step * steps / 1e9  # GB
@@ -340,14 +339,30 @@ def main():
             graphs.append(g)
         torch.cuda.synchronize()
 
-    # Dominant-kernel launch times, measured eagerly inside their own loop on
-    # the launching stream (events inside a graph are not timed).
-    dom_events = []
-    with torch.cuda.stream(stream):
-        for i in range(args.steps):
-            wl.run_step(i, dom_events)
-    torch.cuda.synchronize()
-    dom_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in dom_events) if dom_events else None
+    # Dominant-kernel launch duration: a CUDA graph holding only the dominant
+    # launches of each weight set, replayed back to back on the launching
+    # stream and timed with CUDA events (no host gaps between launches).
+    dom_ms = None
+    if hasattr(wl, "run_dominant"):
+        dg = []
+        for s in range(getattr(wl, "sets", 1)):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                n_dom = wl.run_dominant(s)
+            dg.append(g)
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            for i in range(args.warmup):
+                dg[i % len(dg)].replay()
+            d0 = torch.cuda.Event(enable_timing=True)
+            d1 = torch.cuda.Event(enable_timing=True)
+            d0.record(stream)
+            for i in range(args.steps):
+                dg[i % len(dg)].replay()
+            d1.record(stream)
+        torch.cuda.synchronize()
+        dom_ms = d0.elapsed_time(d1) / (args.steps * n_dom)
+        del dg
 
     barrier(world)
     torch.cuda.synchronize()

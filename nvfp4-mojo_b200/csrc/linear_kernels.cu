@@ -186,10 +186,116 @@ cudaError_t launch_linear_f32(const WeightSpec &ws, const AlphaSpec &al, const v
 // unchanged.  Partial sums of the warps are reduced in shared memory in a
 // fixed order, then scaled by alpha*2^7 and stored.
 // ---------------------------------------------------------------------------
+// Warps per CTA (they split K) and rounds of codes/scales kept in flight per
+// warp ahead of the one being decoded.
+#ifndef NVFP4_SKINNY_WARPS
+#define NVFP4_SKINNY_WARPS 4
+#endif
+#ifndef NVFP4_SKINNY_DEPTH
+#define NVFP4_SKINNY_DEPTH 1
+#endif
+constexpr int kSkinnyWarps = NVFP4_SKINNY_WARPS;
+constexpr int kSkinnyDepth = NVFP4_SKINNY_DEPTH;
+
+// Per-round operands of one lane: 16 bytes of codes and 2 scales for each of
+// its rows (g, g+8, and their `up` rows for the SiLU-gated form), plus the
+// token tiles' 32 activations each.
 template <int NT, bool SILU>
-__global__ void __launch_bounds__(256) skinny_kernel(SkinnyArgs a) {
+struct SkinnyRound {
+  static constexpr int R = SILU ? 4 : 2;
+  uint4 w[R];
+  uint32_t s[R];
+  int kc;
+};
+
+// Full rounds (k0 + 128 <= K): unpredicated loads.  Token slots past the
+// item's count read the first slot's row; their columns are never stored.
+template <int NT, bool SILU>
+__device__ __forceinline__ void skinny_load(SkinnyRound<NT, SILU> &d,
+                                            const uint8_t *const (&wp)[SkinnyRound<NT, SILU>::R],
+                                            const uint8_t *const (&sp)[SkinnyRound<NT, SILU>::R],
+                                            const uint16_t *const (&xrow)[NT], int kc) {
+#pragma unroll
+  for (int i = 0; i < SkinnyRound<NT, SILU>::R; ++i) {
+    d.w[i] = ldg_nc_v4(wp[i] + kc / 2);
+    d.s[i] = (uint32_t)__ldg(reinterpret_cast<const unsigned short *>(sp[i] + kc / kGroup));
+  }
+  d.kc = kc;
+  (void)xrow;
+}
+
+// Tail round (K % 128 != 0): lanes whose 32-element chunk is past K load
+// nothing and contribute zero codes with unit scales.
+template <int NT, bool SILU>
+__device__ __forceinline__ void skinny_load_tail(SkinnyRound<NT, SILU> &d,
+                                                 const uint8_t *const (&wp)[SkinnyRound<NT, SILU>::R],
+                                                 const uint8_t *const (&sp)[SkinnyRound<NT, SILU>::R],
+                                                 const uint16_t *const (&xrow)[NT], int kc,
+                                                 bool kval) {
+  if (kval) {
+    skinny_load(d, wp, sp, xrow, kc);
+  } else {
+#pragma unroll
+    for (int i = 0; i < SkinnyRound<NT, SILU>::R; ++i) {
+      d.w[i] = make_uint4(0, 0, 0, 0);
+      d.s[i] = 0x3838u;  // e4m3 1.0, 1.0
+    }
+    d.kc = -1;  // activations read as zero
+  }
+}
+
+template <int NT, bool SILU, bool TAIL = false>
+__device__ __forceinline__ void skinny_compute(const SkinnyRound<NT, SILU> &d,
+                                               const uint16_t *const (&xrow)[NT],
+                                               float (&acc)[NT][4], float (&accu)[NT][4]) {
+  constexpr int R = SkinnyRound<NT, SILU>::R;
+  // Activations are small and shared by every CTA on the SM: L1-resident.
+  uint4 xv[NT][4];
+#pragma unroll
+  for (int t = 0; t < NT; ++t)
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      xv[t][q] = (!TAIL || d.kc >= 0) ? __ldg(reinterpret_cast<const uint4 *>(xrow[t] + d.kc + 8 * q))
+                                      : make_uint4(0, 0, 0, 0);
+  uint32_t sc[R][2];
+#pragma unroll
+  for (int i = 0; i < R; ++i) scale_pair_to_bf16x2(d.s[i], sc[i][0], sc[i][1]);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int gsel = q >> 1;
+    uint32_t dec[R][4];
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+      const uint32_t wq = q == 0 ? d.w[i].x : q == 1 ? d.w[i].y : q == 2 ? d.w[i].z : d.w[i].w;
+      decode8_raw_pairs(wq, dec[i]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) dec[i][j] = bf16x2_mul(dec[i][j], sc[i][gsel]);
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t A[4] = {dec[0][2 * h], dec[1][2 * h], dec[0][2 * h + 1], dec[1][2 * h + 1]};
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        const uint32_t x0 = h ? xv[t][q].y : xv[t][q].x;
+        const uint32_t x1 = h ? xv[t][q].w : xv[t][q].z;
+        const uint32_t b0 = prmt(x0, x1, 0x5410u), b1 = prmt(x0, x1, 0x7632u);
+        mma_bf16_16816(acc[t], A, b0, b1);
+        if (SILU) {
+          const uint32_t AU[4] = {dec[2 % R][2 * h], dec[3 % R][2 * h], dec[2 % R][2 * h + 1],
+                                  dec[3 % R][2 * h + 1]};
+          mma_bf16_16816(accu[t], AU, b0, b1);
+        }
+      }
+    }
+  }
+}
+
+template <int NT, bool SILU>
+__global__ void __launch_bounds__(32 * kSkinnyWarps,
+                                  (NT == 1 && !SILU) ? 7 : (NT == 4 ? 2 : (SILU ? 3 : 4)) * 4 / kSkinnyWarps)
+    skinny_kernel(SkinnyArgs a) {
   constexpr int NACC = NT * 4 * (SILU ? 2 : 1);
-  __shared__ float red[8][NACC][32];
+  __shared__ float red[kSkinnyWarps][NACC][32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const int g = lane >> 2, c = lane & 3;
 
@@ -212,15 +318,22 @@ __global__ void __launch_bounds__(256) skinny_kernel(SkinnyArgs a) {
   const uint8_t *SF = a.ws.sf + (int64_t)group * a.ws.sf_group_stride;
   // Rows past N are clamped for loading (always valid memory), never stored.
   const int ra = min(row0 + g, Nout - 1), rb = min(row0 + g + 8, Nout - 1);
+  const int rows[4] = {ra, rb, ra + Nout, rb + Nout};
+  constexpr int R = SkinnyRound<NT, SILU>::R;
+  const uint8_t *wp[R];
+  const uint8_t *sp[R];
+#pragma unroll
+  for (int i = 0; i < R; ++i) {
+    wp[i] = W + rows[i] * wld;
+    sp[i] = SF + rows[i] * sld;
+  }
 
   const uint16_t *xrow[NT];
-  bool xval[NT];
 #pragma unroll
   for (int t = 0; t < NT; ++t) {
-    int sl = 8 * t + g;
-    xval[t] = sl < count;
-    int slot = slot0 + (xval[t] ? sl : 0);
-    int64_t r = a.x_rows ? a.x_rows[slot] : slot;
+    const int sl = 8 * t + g;
+    const int slot = slot0 + (sl < count ? sl : 0);
+    const int64_t r = a.x_rows ? a.x_rows[slot] : slot;
     xrow[t] = a.x + r * a.x_ld;
   }
 
@@ -230,82 +343,38 @@ __global__ void __launch_bounds__(256) skinny_kernel(SkinnyArgs a) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[t][i] = accu[t][i] = 0.0f;
 
-  const int rounds = (K + 127) / 128;
-  for (int r = warp; r < rounds; r += nwarps) {
-    const int kc = r * 128 + 32 * c;
-    const bool kval = kc < K;
-    uint4 wa = make_uint4(0, 0, 0, 0), wb = wa, wua = wa, wub = wa;
-    uint32_t sa = 0, sb = 0, sua = 0, sub = 0;
-    if (kval) {
-      wa = ldg_nc_v4(W + ra * wld + kc / 2);
-      wb = ldg_nc_v4(W + rb * wld + kc / 2);
-      sa = *reinterpret_cast<const uint16_t *>(SF + ra * sld + kc / kGroup);
-      sb = *reinterpret_cast<const uint16_t *>(SF + rb * sld + kc / kGroup);
-      if (SILU) {
-        wua = ldg_nc_v4(W + (ra + Nout) * wld + kc / 2);
-        wub = ldg_nc_v4(W + (rb + Nout) * wld + kc / 2);
-        sua = *reinterpret_cast<const uint16_t *>(SF + (ra + Nout) * sld + kc / kGroup);
-        sub = *reinterpret_cast<const uint16_t *>(SF + (rb + Nout) * sld + kc / kGroup);
-      }
-    }
-    uint4 xv[NT][4];
+  // Software pipeline over this warp's full rounds r = warp + i * nwarps with a
+  // ring of kSkinnyDepth + 1 register buffers: rounds i+1 .. i+depth are in
+  // flight while round i decodes and multiplies.  The ring loop is unrolled
+  // so every buffer index is static.
+  constexpr int NB = kSkinnyDepth + 1;
+  const int full = K / 128;
+  SkinnyRound<NT, SILU> buf[NB];
 #pragma unroll
-    for (int t = 0; t < NT; ++t)
+  for (int i = 0; i < kSkinnyDepth; ++i) {
+    const int rr = warp + i * nwarps;
+    if (rr < full) skinny_load(buf[i], wp, sp, xrow, rr * 128 + 32 * c);
+  }
+  bool done = false;
+  for (int base = 0; !done; base += NB) {
 #pragma unroll
-      for (int q = 0; q < 4; ++q)
-        xv[t][q] = (kval && xval[t])
-                       ? *reinterpret_cast<const uint4 *>(xrow[t] + kc + 8 * q)
-                       : make_uint4(0, 0, 0, 0);
-
-    const uint32_t wa_[4] = {wa.x, wa.y, wa.z, wa.w}, wb_[4] = {wb.x, wb.y, wb.z, wb.w};
-    const uint32_t wua_[4] = {wua.x, wua.y, wua.z, wua.w}, wub_[4] = {wub.x, wub.y, wub.z, wub.w};
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int sh = (q >> 1) * 8;
-      uint32_t da[4], db[4];
-      {
-        uint32_t s2a = scale_to_bf16x2_2p119((sa >> sh) & 0xffu);
-        uint32_t s2b = scale_to_bf16x2_2p119((sb >> sh) & 0xffu);
-        decode8_raw_pairs(wa_[q], da);
-        decode8_raw_pairs(wb_[q], db);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          da[i] = bf16x2_mul(da[i], s2a);
-          db[i] = bf16x2_mul(db[i], s2b);
-        }
-      }
-      uint32_t dua[4], dub[4];
-      if (SILU) {
-        uint32_t s2a = scale_to_bf16x2_2p119((sua >> sh) & 0xffu);
-        uint32_t s2b = scale_to_bf16x2_2p119((sub >> sh) & 0xffu);
-        decode8_raw_pairs(wua_[q], dua);
-        decode8_raw_pairs(wub_[q], dub);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          dua[i] = bf16x2_mul(dua[i], s2a);
-          dub[i] = bf16x2_mul(dub[i], s2b);
-        }
-      }
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const uint32_t A[4] = {da[2 * h], db[2 * h], da[2 * h + 1], db[2 * h + 1]};
-        uint32_t AU[4];
-        if (SILU) {
-          AU[0] = dua[2 * h];
-          AU[1] = dub[2 * h];
-          AU[2] = dua[2 * h + 1];
-          AU[3] = dub[2 * h + 1];
-        }
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-          const uint32_t x0 = h ? xv[t][q].y : xv[t][q].x;
-          const uint32_t x1 = h ? xv[t][q].w : xv[t][q].z;
-          const uint32_t b0 = prmt(x0, x1, 0x5410u), b1 = prmt(x0, x1, 0x7632u);
-          mma_bf16_16816(acc[t], A, b0, b1);
-          if (SILU) mma_bf16_16816(accu[t], AU, b0, b1);
+    for (int j = 0; j < NB; ++j) {
+      if (!done) {
+        const int rr = warp + (base + j) * nwarps;
+        if (rr >= full) {
+          done = true;
+        } else {
+          const int rl = rr + kSkinnyDepth * nwarps;
+          if (rl < full) skinny_load(buf[(j + kSkinnyDepth) % NB], wp, sp, xrow, rl * 128 + 32 * c);
+          skinny_compute(buf[j], xrow, acc, accu);
         }
       }
     }
+  }
+  if ((K % 128) != 0 && warp == (full % nwarps)) {
+    const int kc = full * 128 + 32 * c;
+    skinny_load_tail(buf[0], wp, sp, xrow, kc, kc < K);
+    skinny_compute<NT, SILU, true>(buf[0], xrow, acc, accu);
   }
 
   // Cross-warp reduction in a fixed order.
@@ -355,7 +424,7 @@ cudaError_t launch_skinny(const SkinnyArgs &a, cudaStream_t s) {
   const int items = a.work ? a.work_capacity : (a.M + tpi - 1) / tpi;
   if (items == 0) return cudaSuccess;
   const int rounds = (a.ws.K + 127) / 128;
-  const int nwarps = rounds < 8 ? rounds : 8;
+  const int nwarps = rounds < kSkinnyWarps ? rounds : kSkinnyWarps;
   dim3 grid((Nout + 15) / 16, items);
   dim3 block(32 * nwarps);
 #define NVFP4_SKINNY(NT_)                                                  \

@@ -48,6 +48,27 @@ __device__ __forceinline__ uint32_t scale_to_bf16x2_2p119(uint32_t b) {
   return h | (h << 16);
 }
 
+// Two e4m3 blockscales (low byte = first group) -> bf16x2 of float(s)*2^119
+// broadcast to both halves, for each.  Fast path: the hardware e4m3x2 -> f16x2
+// conversion is exact and every finite non-zero e4m3 is an f16 normal, so the
+// bf16 pattern is ((|h| >> 3) + (231 << 7)) | sign.  Zero and NaN scales (the
+// only inputs that leave that range) take the exact scalar path.
+__device__ __forceinline__ void scale_pair_to_bf16x2(uint32_t u16, uint32_t &s0, uint32_t &s1) {
+  // Zero (|b| == 0) and NaN (|b| == 0x7F) scales are the only codes outside
+  // the fast path: (|b| - 1) >= 0x7E as unsigned catches both.
+  const uint32_t b0 = u16 & 0x7Fu, b1 = (u16 >> 8) & 0x7Fu;
+  if (__builtin_expect(((b0 - 1u) >= 0x7Eu) | ((b1 - 1u) >= 0x7Eu), 0)) {
+    s0 = scale_to_bf16x2_2p119(u16 & 0xffu);
+    s1 = scale_to_bf16x2_2p119((u16 >> 8) & 0xffu);
+    return;
+  }
+  uint32_t h;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"((unsigned short)u16));
+  const uint32_t r = (((h & 0x7FFF7FFFu) >> 3) + 0x73807380u) | (h & 0x80008000u);
+  asm("prmt.b32 %0, %1, %1, 0x1010;" : "=r"(s0) : "r"(r));
+  asm("prmt.b32 %0, %1, %1, 0x3232;" : "=r"(s1) : "r"(r));
+}
+
 // Four bf16x2 words of LUT*2^-126 from one 32-bit word of 8 packed codes
 // e0..e7 (e_j = nibble j = k offset j).  out[i] = (lo: e_i, hi: e_{i+4}).
 __device__ __forceinline__ void decode8_raw_pairs(uint32_t w, uint32_t out[4]) {
