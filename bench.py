@@ -212,7 +212,93 @@ class GemvSweep:
         return run, nbytes / 1e9, desc
 
 
-WORKLOADS = {"gemv": GemvSweep}
+# ---------------------------------------------------------------------------
+# Workload: prefill W4A16 GEMM sweep (tcgen05).
+# ---------------------------------------------------------------------------
+PREFILL_MS = [512, 2048, 8192]
+PREFILL_K, PREFILL_N = 4096, 14336
+
+
+class PrefillSweep:
+    name = "prefill"
+    unit = "TFLOP/s"
+    workload = ("prefill W4A16 GEMM sweep: bf16 x [M, 4096] ~N(0,1), M in {512, 2048, 8192} x "
+                "NVFP4 W [14336, 4096] (u8 [14336, 2048], e4m3 [14336, 256], fp32 scale_2 "
+                "[14336]); fp32 accumulate, bf16 out; 2*M*N*K flop per GEMM")
+
+    def __init__(self, device, seed=0):
+        import torch
+        import nvfp4
+        from nvfp4 import synthetic
+
+        self.torch, self.nvfp4 = torch, nvfp4
+        self.sets = 2
+        K, N = PREFILL_K, PREFILL_N
+        self.calls = []
+        for s in range(self.sets):
+            wd = synthetic.linear_weights_cuda(N, K, seed=seed + 31 * s, device=device)
+            lin = nvfp4.NvFp4Linear(K, N, weight_scale_2_rows=wd["ws2"])
+            calls = []
+            for M in PREFILL_MS:
+                x = torch.randn((M, K), device=device).to(torch.bfloat16)
+                y = torch.empty((M, N), device=device, dtype=torch.bfloat16)
+                calls.append((lin, wd["w"], wd["sf"], x, y, 2.0 * M * N * K, M == 8192))
+            self.calls.append(calls)
+        self.flop_per_step = sum(c[5] for c in self.calls[0])
+        self.launches_per_step = len(self.calls[0])
+        self.dominant_bytes = 2.0 * 8192 * N * K  # flop of the dominant launch
+        self.dominant_name = "w4a16_tc_kernel (tcgen05, M=8192 K=4096 N=14336)"
+        self.bound = "tensor"
+        self.config = {"workload": self.workload, "M": PREFILL_MS, "K": K, "N": N,
+                       "l2": "inputs larger than L2: two weight sets alternate per step "
+                             "(2 x 33 MB weights + 88 MB activations per set)"}
+
+    def run_step(self, i):
+        for (lin, W, SF, X, Y, _f, _d) in self.calls[i % self.sets]:
+            self.nvfp4.nvfp4_linear_forward(lin, W, SF, X, Y, X.shape[0])
+
+    def run_dominant(self, i):
+        n = 0
+        for (lin, W, SF, X, Y, _f, dom) in self.calls[i % self.sets]:
+            if dom:
+                self.nvfp4.nvfp4_linear_forward(lin, W, SF, X, Y, X.shape[0])
+                n += 1
+        return n
+
+    def units(self, steps):
+        return self.flop_per_step * steps / 1e12  # TFLOP
+
+    def e2e_setup(self):
+        torch = self.torch
+        self.h_x = [torch.randn(c[3].shape).to(torch.bfloat16).pin_memory() for c in self.calls[0]]
+        self.h_y = [torch.empty(c[4].shape, dtype=torch.bfloat16).pin_memory() for c in self.calls[0]]
+        self.h2d = sum(t.numel() * 2 for t in self.h_x)
+        self.d2h = sum(t.numel() * 2 for t in self.h_y)
+
+    def e2e_step(self, i):
+        for j, (lin, W, SF, X, Y, _f, _d) in enumerate(self.calls[i % self.sets]):
+            X.copy_(self.h_x[j], non_blocking=True)
+            self.nvfp4.nvfp4_linear_forward(lin, W, SF, X, Y, X.shape[0])
+            self.h_y[j].copy_(Y, non_blocking=True)
+
+    def cpu_sample(self, threads, rows=8, cols=256):
+        from nvfp4 import synthetic
+        from oracle import oracle as O
+
+        K, N = PREFILL_K, PREFILL_N
+        wd = synthetic.linear_weights(cols, K, seed=5)
+        x = synthetic.activations(rows, K, seed=6)
+
+        def run():
+            O.linear(wd["w"], wd["sf"], x, ws2_rows=wd["ws2"], n_threads=threads)
+
+        flop = 2.0 * rows * cols * K
+        desc = (f"{rows} tokens x {cols} output features of the K=4096 GEMM per pass "
+                f"({flop / 1e6:.1f} MFLOP; the oracle's cost is linear in tokens x features)")
+        return run, flop / 1e12, desc
+
+
+WORKLOADS = {"gemv": GemvSweep, "prefill": PrefillSweep}
 
 
 # ---------------------------------------------------------------------------
@@ -408,13 +494,23 @@ def main():
 
     roof = None
     if dom_ms:
-        achieved = wl.dominant_bytes / (dom_ms / 1e3) / 1e9
         traffic = load_traffic(wl.name)
-        roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
-                "kernel": wl.dominant_name, "algorithmic_bytes_per_launch": wl.dominant_bytes,
-                "avg_launch_us": dom_ms * 1e3,
-                "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs, copy burst)"}
+        if getattr(wl, "bound", "hbm") == "tensor":
+            achieved = wl.dominant_bytes / (dom_ms / 1e3) / 1e12
+            roof = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
+                    "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
+                    "traffic": traffic, "kernel": wl.dominant_name,
+                    "algorithmic_flop_per_launch": wl.dominant_bytes,
+                    "avg_launch_us": dom_ms * 1e3,
+                    "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json bf16_tflops, "
+                                   "cuBLAS bf16 burst)"}
+        else:
+            achieved = wl.dominant_bytes / (dom_ms / 1e3) / 1e9
+            roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                    "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
+                    "kernel": wl.dominant_name, "algorithmic_bytes_per_launch": wl.dominant_bytes,
+                    "avg_launch_us": dom_ms * 1e3,
+                    "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs, copy burst)"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

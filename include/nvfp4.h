@@ -84,6 +84,15 @@ int nvfp4_abi_version(void);
 const char *nvfp4_last_error_string(void);
 
 /*
+ * Status word of the tensor-core kernels, read (synchronously) and cleared:
+ * 0 = no failure; > 0 = a kernel abandoned a bounded wait (1 TMA stage,
+ * 2 decoded operands, 3 stage release, 4 accumulator) and returned early,
+ * its output then being undefined; < 0 = the status could not be read.
+ * No reference counterpart (the reference has no GPU kernel that runs).
+ */
+int nvfp4_device_status(void);
+
+/*
  * Replaces nvfp4_linear_forward (nvfp4/nvfp4_gemm_gpu.mojo:185-224), whose
  * launch the reference leaves as a placeholder (:219-224).
  * activations [batch_seq_len, in_features] (act_dtype bf16 or f32), output

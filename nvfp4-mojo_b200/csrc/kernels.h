@@ -17,6 +17,14 @@ struct AlphaSpec {
   int64_t ws2_group_stride = 0;         // elements
 };
 
+#ifdef __CUDACC__
+__device__ __forceinline__ float alpha_of(const AlphaSpec &al, int g, int n) {
+  const float ins = al.input_scales ? al.input_scales[g] : al.input_scale;
+  const float w2 = al.ws2_rows ? al.ws2_rows[(int64_t)g * al.ws2_group_stride + n] : al.ws2;
+  return ins * w2;
+}
+#endif
+
 // Grouped NVFP4 weights: group g has rows [N, K/2] at w + g*w_group_stride.
 struct WeightSpec {
   const uint8_t *w = nullptr;
@@ -74,5 +82,13 @@ struct SkinnyArgs {
   int tokens_per_item = 8;      // 8, 16 or 32
 };
 cudaError_t launch_skinny(const SkinnyArgs &a, cudaStream_t s);
+
+// tcgen05 W4A16 GEMM (token-major x [M, K] bf16 with row stride x_ld).
+bool tc_gemm_supported(int K, const void *w, const void *x, int64_t x_ld);
+cudaError_t launch_w4a16_tc(const WeightSpec &ws, const AlphaSpec &al, const uint16_t *x,
+                            int64_t x_ld, void *y, int y_dtype, int64_t y_ld, int M,
+                            cudaStream_t st);
+// Returns and clears the device status word of the tensor-core kernels.
+int read_gemm_device_status();
 
 }  // namespace nvfp4

@@ -111,12 +111,6 @@ __device__ __forceinline__ void store_out(void *y, int dt, int64_t idx, float v)
     reinterpret_cast<uint16_t *>(y)[idx] = f32_to_bf16_bits(v);
 }
 
-__device__ __forceinline__ float alpha_of(const AlphaSpec &al, int g, int n) {
-  float ins = al.input_scales ? al.input_scales[g] : al.input_scale;
-  float w2 = al.ws2_rows ? al.ws2_rows[(int64_t)g * al.ws2_group_stride + n] : al.ws2;
-  return ins * w2;
-}
-
 __global__ void __launch_bounds__(256) linear_f32_kernel(WeightSpec ws, AlphaSpec al,
                                                          const void *x, int x_dt, int64_t xs_m,
                                                          int64_t xs_k, void *y, int y_dt,

@@ -53,9 +53,17 @@ static int run_linear(const WeightSpec &ws, const AlphaSpec &al, const void *x, 
   const bool skinny_ok = token_major && x_dt == kBF16 && (ws.K % 32) == 0 &&
                          aligned(ws.w, 16) && aligned(ws.sf, 2) && aligned(x, 16) &&
                          (xs_m % 8) == 0;
-  if (flags & NVFP4_FLAG_FORCE_TC)
-    return fail(NVFP4_ERR_UNSUPPORTED, "tcgen05 GEMM path not available in this build");
-  if (!force_f32 && skinny_ok && (M <= 64 || (flags & NVFP4_FLAG_FORCE_SKINNY))) {
+  const bool tc_ok = token_major && x_dt == kBF16 && !force_f32 &&
+                     tc_gemm_supported(ws.K, ws.w, x, xs_m);
+  if ((flags & NVFP4_FLAG_FORCE_TC) && !tc_ok)
+    return fail(NVFP4_ERR_UNSUPPORTED,
+                "tcgen05 GEMM path needs bf16 token-major activations, K %% 64 == 0 and "
+                "16-byte aligned weights/activations");
+  if (tc_ok && ((flags & NVFP4_FLAG_FORCE_TC) || (M > 64 && !(flags & NVFP4_FLAG_FORCE_SKINNY))))
+    return check_launch(launch_w4a16_tc(ws, al, reinterpret_cast<const uint16_t *>(x), xs_m, y,
+                                        y_dt, ys_m, (int)M, st),
+                        "tcgen05 GEMM launch");
+  if (!force_f32 && skinny_ok && (M <= 64 || !tc_ok || (flags & NVFP4_FLAG_FORCE_SKINNY))) {
     SkinnyArgs a;
     a.ws = ws;
     a.al = al;
@@ -165,6 +173,12 @@ extern "C" int nvfp4_dequant_tile(const uint8_t *w, const uint8_t *sf, float *ou
                                           start_col, tile_m, tile_k,
                                           static_cast<cudaStream_t>(stream)),
                       "dequant tile launch");
+}
+
+extern "C" int nvfp4_device_status(void) {
+  const int v = read_gemm_device_status();
+  if (v < 0) return fail(NVFP4_ERR_CUDA, "could not read the device status word");
+  return v;
 }
 
 extern "C" int nvfp4_dequant(const uint8_t *w, const uint8_t *sf, int64_t rows, int64_t K,

@@ -73,6 +73,7 @@ SIGNATURES = {
     "nvfp4_matvec": (_int, [ctypes.POINTER(LinearDesc), _vp, _vp, _vp, _vp, _vp]),
     "nvfp4_dequant_tile": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
     "nvfp4_dequant": (_int, [_vp, _vp, _i64, _i64, _vp, _int, _vp]),
+    "nvfp4_device_status": (_int, []),
 }
 
 _lib = None

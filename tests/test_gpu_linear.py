@@ -191,3 +191,54 @@ def test_nan_scale_propagates_and_empty_batch(O, cuda):
     nvfp4.nvfp4_linear_forward(lin, dev(wd["w"]), dev(wd["sf"]),
                                torch.empty((0, K), dtype=torch.bfloat16, device=cuda), empty, 0)
     torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("N,K,M", [(256, 512, 65), (256, 512, 256), (200, 256, 300),
+                                   (384, 1024, 513), (128, 768, 97), (1024, 256, 2560)])
+def test_tc_gemm_small_shapes(O, cuda, N, K, M):
+    """tcgen05 W4A16 GEMM (forced): ragged N, M not a multiple of the tile,
+    a single blockscale chunk (K = 256), an odd number of chunks (K = 768),
+    and more tiles than SMs (persistent CTAs, both accumulator buffers); fp32
+    out checked against the oracle."""
+    import nvfp4
+    from nvfp4 import synthetic
+
+    wd = synthetic.linear_weights(N, K, seed=N + K + M)
+    x = synthetic.bf16_round(synthetic.activations(M, K, seed=M))
+    lin = nvfp4.NvFp4Linear(K, N, input_scale=0.5, weight_scale_2_rows=dev(wd["ws2"]))
+    y = torch.full((M, N), float("nan"), dtype=torch.float32, device=cuda)
+    nvfp4.nvfp4_linear_forward(lin, dev(wd["w"]), dev(wd["sf"]), dev(x, torch.bfloat16), y, M,
+                               flags=nvfp4._lib.FLAG_FORCE_TC)
+    torch.cuda.synchronize()
+    assert nvfp4._lib.load().nvfp4_device_status() == 0
+    ref = O.linear(wd["w"], wd["sf"], x, input_scale=0.5, ws2_rows=wd["ws2"])
+    got = y.cpu().numpy()
+    assert not np.isnan(got).any()
+    assert rel_err(got, ref) <= 1e-5
+
+
+@pytest.mark.parametrize("M", [512, 2048, 8192])
+def test_prefill_w4a16_config2_sampled(O, cuda, M):
+    """Prefill W4A16 at the benchmark shape (K=4096, N=14336): bf16 out,
+    oracle on a sample of tokens x output features."""
+    import nvfp4
+    from nvfp4 import synthetic
+
+    N, K = 14336, 4096
+    wd = synthetic.linear_weights(N, K, seed=2)
+    x = synthetic.bf16_round(synthetic.activations(M, K, seed=3))
+    lin = nvfp4.NvFp4Linear(K, N, weight_scale_2_rows=dev(wd["ws2"]))
+    y = nvfp4.nvfp4_linear(lin, dev(wd["w"]), dev(wd["sf"]), dev(x, torch.bfloat16))
+    torch.cuda.synchronize()
+    assert nvfp4._lib.load().nvfp4_device_status() == 0
+    rng = np.random.default_rng(M)
+    rows = np.sort(rng.choice(M, 24, replace=False))
+    cols = np.sort(rng.choice(N, 256, replace=False))
+    ref = O.linear(wd["w"], wd["sf"], x, ws2_rows=wd["ws2"], rows=rows, cols=cols, n_threads=8)
+    got = y.float().cpu().numpy()[np.ix_(rows, cols)]
+    assert rel_err(got, ref) <= TOL_BF16
+    # fp32 output agrees with the oracle to fp32 summation-order error (the
+    # oracle sums K = 4096 terms sequentially; 200x tighter than the bf16 bar).
+    y32 = torch.empty((M, N), dtype=torch.float32, device=cuda)
+    nvfp4.nvfp4_linear_forward(lin, dev(wd["w"]), dev(wd["sf"]), dev(x, torch.bfloat16), y32, M)
+    assert rel_err(y32.cpu().numpy()[np.ix_(rows, cols)], ref) <= 1e-4
