@@ -298,7 +298,88 @@ class PrefillSweep:
         return run, flop / 1e12, desc
 
 
-WORKLOADS = {"gemv": GemvSweep, "prefill": PrefillSweep}
+# ---------------------------------------------------------------------------
+# Workload: one MoE FFN layer (128 experts, top-8, H=2048, I=768).
+# ---------------------------------------------------------------------------
+MOE_E, MOE_K, MOE_H, MOE_I = 128, 8, 2048, 768
+
+
+def moe_expert_bytes(H=MOE_H, I=MOE_I):
+    # gate_up [2I, H] + down [H, I]: codes, scales, per-row fp32 scale_2
+    return (2 * I * H // 2 + 2 * I * H // 16 + 4 * 2 * I) + (H * I // 2 + H * I // 16 + 4 * H)
+
+
+class MoELayerBench:
+    name = "moe"
+    unit = "tokens/s"
+
+    def __init__(self, device, seed=0, tokens=4096, layers=4):
+        import torch
+        from nvfp4 import synthetic
+        from nvfp4.moe import MoELayer, MoEWeights
+
+        self.torch = torch
+        self.T = tokens
+        self.workload = (f"one MoE FFN layer, 128 experts, top-8 (softmax, renormalised), hidden "
+                         f"2048, expert intermediate 768, NVFP4 gate_up [1536, 2048] and down "
+                         f"[2048, 768] per expert; T = {tokens} bf16 tokens ~N(0,1)")
+        # Distinct layers (weights 342 MB each) cycle so that inputs exceed L2.
+        self.layers = []
+        for l in range(layers):
+            wd = synthetic.moe_weights_cuda(MOE_E, MOE_H, MOE_I, seed=seed + 97 * l, device=device)
+            self.layers.append(MoELayer(MoEWeights.from_dict(wd, device), top_k=MOE_K))
+        self.x = torch.randn((tokens, MOE_H), device=device).to(torch.bfloat16)
+        self.y = torch.empty_like(self.x)
+        for L in self.layers:
+            L.workspace(tokens, device)
+        self.sets = len(self.layers)
+        self.launches_per_step = 7  # router x2, slot index, permute, gate_up, down, combine
+        # Distinct experts touched: expectation under uniform routing.
+        touched = MOE_E * (1.0 - (1.0 - MOE_K / MOE_E) ** tokens)
+        self.dominant_bytes = touched * moe_expert_bytes()
+        self.dominant_name = f"MoE layer (T={tokens}): expert weight bytes of the experts touched"
+        self.config = {"workload": self.workload, "T": tokens, "experts": MOE_E, "top_k": MOE_K,
+                       "hidden": MOE_H, "intermediate": MOE_I,
+                       "l2": f"inputs larger than L2: {layers} distinct layers (342 MB of expert "
+                             f"weights each) cycle per step"}
+
+    def run_step(self, i):
+        self.layers[i % self.sets](self.x, out=self.y)
+
+    def run_dominant(self, i):
+        self.layers[i % self.sets](self.x, out=self.y)
+        return 1
+
+    def units(self, steps):
+        return self.T * steps  # tokens
+
+    def e2e_setup(self):
+        torch = self.torch
+        self.h_x = torch.randn(self.x.shape).to(torch.bfloat16).pin_memory()
+        self.h_y = torch.empty(self.y.shape, dtype=torch.bfloat16).pin_memory()
+        self.h2d = self.h_x.numel() * 2
+        self.d2h = self.h_y.numel() * 2
+
+    def e2e_step(self, i):
+        self.x.copy_(self.h_x, non_blocking=True)
+        self.layers[i % self.sets](self.x, out=self.y)
+        self.h_y.copy_(self.y, non_blocking=True)
+
+    def cpu_sample(self, threads, n_tok=64):
+        from nvfp4 import synthetic
+        from oracle import oracle as O
+
+        wd = synthetic.moe_weights(MOE_E, MOE_H, MOE_I, seed=5)
+        x = synthetic.activations(n_tok, MOE_H, seed=6)
+
+        def run():
+            O.moe(x, wd, top_k=MOE_K, n_threads=threads)
+
+        desc = f"{n_tok} tokens through one layer (oracle cost is linear in tokens)"
+        return run, float(n_tok), desc
+
+
+WORKLOADS = {"gemv": GemvSweep, "prefill": PrefillSweep, "moe": MoELayerBench}
 
 
 # ---------------------------------------------------------------------------
@@ -392,6 +473,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--tokens", type=int, default=4096, help="MoE workload: tokens per step")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -406,7 +488,8 @@ def main():
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     peaks = load_peaks()
-    wl = WORKLOADS[args.workload](device, seed=17 * rank)
+    kw = {"tokens": args.tokens} if args.workload == "moe" else {}
+    wl = WORKLOADS[args.workload](device, seed=17 * rank, **kw)
     stream = torch.cuda.Stream(device)
 
     # Warm-up (also loads the library and JITs nothing: all kernels are prebuilt).

@@ -143,6 +143,76 @@ int nvfp4_dequant_tile(const uint8_t *packed_weights, const uint8_t *blockscales
 int nvfp4_dequant(const uint8_t *packed_weights, const uint8_t *blockscales, int64_t rows,
                   int64_t K, void *output, int out_dtype, void *stream);
 
+/* ------------------------------------------------------------------------
+ * MoE expert path.  No counterpart in the reference, which only defines the
+ * per-expert NVFP4 weight layout (nvfp4/weight_loader.mojo:767-793,
+ * :873-887: expert gate/up/down linears and the router `mlp.gate.weight`)
+ * and SiLU (nvfp4/deltanet.mojo:66-80).  Experts are stacked: expert e's
+ * fused gate_up linear is rows [e*2I, (e+1)*2I) (gate rows first, then up),
+ * its down linear rows [e*H, (e+1)*H); each in the layout above.
+ * ---------------------------------------------------------------------- */
+typedef struct nvfp4_moe_desc {
+  int32_t num_experts;   /* E (local experts, <= 256) */
+  int32_t top_k;         /* k (<= 32) */
+  int32_t hidden;        /* H (multiple of 128) */
+  int32_t intermediate;  /* I (multiple of 128) */
+  int32_t renormalize;   /* nonzero: the k routing weights are renormalised to sum 1 */
+} nvfp4_moe_desc;
+
+typedef struct nvfp4_moe_weights {
+  const float *router;                /* [H, E] fp32 (logits = x @ router) */
+  const uint8_t *gate_up;             /* [E, 2I, H/2] packed E2M1 */
+  const uint8_t *gate_up_scale;       /* [E, 2I, H/16] e4m3 */
+  const float *gate_up_scale_2;       /* [E, 2I] fp32, or NULL (1.0) */
+  const float *gate_up_input_scale;   /* [E] fp32, or NULL (1.0) */
+  const uint8_t *down;                /* [E, H, I/2] */
+  const uint8_t *down_scale;          /* [E, H, I/16] */
+  const float *down_scale_2;          /* [E, H], or NULL */
+  const float *down_input_scale;      /* [E], or NULL */
+} nvfp4_moe_weights;
+
+/* Bytes of caller-provided device workspace nvfp4_moe_forward needs for T tokens. */
+size_t nvfp4_moe_workspace_size(const nvfp4_moe_desc *desc, int64_t T);
+/* Bytes of workspace nvfp4_moe_experts needs for R rows. */
+size_t nvfp4_moe_experts_workspace_size(const nvfp4_moe_desc *desc, int64_t R);
+
+/*
+ * One MoE FFN layer: y[T, H] = sum_j w_j * expert_{e_j}(x) (+ residual if
+ * non-NULL, bf16 [T, H]); x bf16 [T, H]; y bf16 or fp32 (y_dtype).
+ * Workspace: device memory of at least nvfp4_moe_workspace_size() bytes,
+ * 256-byte aligned, owned by the caller; its contents on entry do not
+ * matter.  If topk_ids / topk_w are non-NULL they receive the routing
+ * decisions (int32 / fp32 [T, k]).
+ */
+int nvfp4_moe_forward(const nvfp4_moe_desc *desc, const nvfp4_moe_weights *weights,
+                      const void *x, const void *residual, void *y, int y_dtype, int64_t T,
+                      int32_t *topk_ids, float *topk_w, void *workspace,
+                      size_t workspace_bytes, void *stream);
+
+/* Router alone: topk_ids int32 [T, k], topk_w fp32 [T, k]; logits fp32
+ * [T, E] is caller memory the router writes (and the caller may read). */
+int nvfp4_moe_route(const nvfp4_moe_desc *desc, const float *router, const void *x, int64_t T,
+                    int32_t *topk_ids, float *topk_w, float *logits, void *stream);
+
+/*
+ * Expert FFNs over R rows, each assigned one expert: y_rows[r] ([R, H],
+ * y_dtype fp32 or bf16) = down_e(silu(gate_e(x)) * up_e(x)) with e =
+ * row_expert[r] and x = x[x_row_index[r]] (or x[r] when x_row_index is
+ * NULL); x is bf16 [*, H]; rows whose expert id is outside [0, E) are left
+ * untouched.  The building block of the expert-parallel layer (rows
+ * received from other ranks).
+ */
+int nvfp4_moe_experts(const nvfp4_moe_desc *desc, const nvfp4_moe_weights *weights,
+                      const void *x, const int32_t *x_row_index, const int32_t *row_expert,
+                      int64_t R, void *y_rows, int y_dtype, void *workspace,
+                      size_t workspace_bytes, void *stream);
+
+/* y[t] = sum_j topk_w[t, j] * y_slots[t*k + j] (+ residual[t]): fp32 sums in
+ * j order; residual bf16; y_slots and y fp32 or bf16 (slot_dtype, y_dtype). */
+int nvfp4_moe_combine(const void *y_slots, int slot_dtype, const float *topk_w,
+                      const void *residual, void *y, int y_dtype, int64_t T, int32_t k,
+                      int32_t hidden, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -68,12 +68,14 @@ struct SkinnyArgs {
   WeightSpec ws;
   AlphaSpec al;
   const uint16_t *x = nullptr;  // bf16 rows of length K, ld x_ld
+  const uint16_t *x_lo = nullptr;  // optional bf16 low parts (x = x + x_lo), same layout
   int64_t x_ld = 0;
   const int32_t *x_rows = nullptr;
   void *y = nullptr;
   int y_dtype = kBF16;
   int64_t y_ld = 0;
   const int32_t *y_rows = nullptr;
+  uint16_t *y_lo = nullptr;     // silu_gate only: bf16 low parts of the outputs
   int M = 0;                    // tokens (plain mode)
   const SkinnyWork *work = nullptr;
   const int *n_work = nullptr;  // device count of work items

@@ -238,19 +238,27 @@ __device__ __forceinline__ void skinny_load_tail(SkinnyRound<NT, SILU> &d,
   }
 }
 
-template <int NT, bool SILU, bool TAIL = false>
+template <int NT, bool SILU, bool SPLIT, bool TAIL = false>
 __device__ __forceinline__ void skinny_compute(const SkinnyRound<NT, SILU> &d,
                                                const uint16_t *const (&xrow)[NT],
+                                               const uint16_t *const (&xrow_lo)[NT],
                                                float (&acc)[NT][4], float (&accu)[NT][4]) {
   constexpr int R = SkinnyRound<NT, SILU>::R;
   // Activations are small and shared by every CTA on the SM: L1-resident.
-  uint4 xv[NT][4];
+  // SPLIT: the activations are hi + lo bf16 parts (x = hi + lo to ~2^-16);
+  // both multiply the same decoded weights into the same accumulator.
+  uint4 xv[NT][4], xl[SPLIT ? NT : 1][4];
 #pragma unroll
   for (int t = 0; t < NT; ++t)
 #pragma unroll
-    for (int q = 0; q < 4; ++q)
+    for (int q = 0; q < 4; ++q) {
       xv[t][q] = (!TAIL || d.kc >= 0) ? __ldg(reinterpret_cast<const uint4 *>(xrow[t] + d.kc + 8 * q))
                                       : make_uint4(0, 0, 0, 0);
+      if (SPLIT)
+        xl[SPLIT ? t : 0][q] = (!TAIL || d.kc >= 0)
+                                   ? __ldg(reinterpret_cast<const uint4 *>(xrow_lo[t] + d.kc + 8 * q))
+                                   : make_uint4(0, 0, 0, 0);
+    }
   uint32_t sc[R][2];
 #pragma unroll
   for (int i = 0; i < R; ++i) scale_pair_to_bf16x2(d.s[i], sc[i][0], sc[i][1]);
@@ -274,6 +282,11 @@ __device__ __forceinline__ void skinny_compute(const SkinnyRound<NT, SILU> &d,
         const uint32_t x1 = h ? xv[t][q].w : xv[t][q].z;
         const uint32_t b0 = prmt(x0, x1, 0x5410u), b1 = prmt(x0, x1, 0x7632u);
         mma_bf16_16816(acc[t], A, b0, b1);
+        if (SPLIT) {
+          const uint32_t l0 = h ? xl[SPLIT ? t : 0][q].y : xl[SPLIT ? t : 0][q].x;
+          const uint32_t l1 = h ? xl[SPLIT ? t : 0][q].w : xl[SPLIT ? t : 0][q].z;
+          mma_bf16_16816(acc[t], A, prmt(l0, l1, 0x5410u), prmt(l0, l1, 0x7632u));
+        }
         if (SILU) {
           const uint32_t AU[4] = {dec[2 % R][2 * h], dec[3 % R][2 * h], dec[2 % R][2 * h + 1],
                                   dec[3 % R][2 * h + 1]};
@@ -284,9 +297,10 @@ __device__ __forceinline__ void skinny_compute(const SkinnyRound<NT, SILU> &d,
   }
 }
 
-template <int NT, bool SILU>
+template <int NT, bool SILU, bool SPLIT>
 __global__ void __launch_bounds__(32 * kSkinnyWarps,
-                                  (NT == 1 && !SILU) ? 7 : (NT == 4 ? 2 : (SILU ? 3 : 4)) * 4 / kSkinnyWarps)
+                                  (NT == 1 && !SILU && !SPLIT) ? 7
+                                  : (NT == 4 ? 2 : ((SILU || SPLIT) ? 3 : 4)) * 4 / kSkinnyWarps)
     skinny_kernel(SkinnyArgs a) {
   constexpr int NACC = NT * 4 * (SILU ? 2 : 1);
   __shared__ float red[kSkinnyWarps][NACC][32];
@@ -323,12 +337,14 @@ __global__ void __launch_bounds__(32 * kSkinnyWarps,
   }
 
   const uint16_t *xrow[NT];
+  const uint16_t *xrow_lo[NT];
 #pragma unroll
   for (int t = 0; t < NT; ++t) {
     const int sl = 8 * t + g;
     const int slot = slot0 + (sl < count ? sl : 0);
     const int64_t r = a.x_rows ? a.x_rows[slot] : slot;
     xrow[t] = a.x + r * a.x_ld;
+    xrow_lo[t] = SPLIT ? a.x_lo + r * a.x_ld : nullptr;
   }
 
   float acc[NT][4], accu[NT][4];
@@ -360,7 +376,7 @@ __global__ void __launch_bounds__(32 * kSkinnyWarps,
         } else {
           const int rl = rr + kSkinnyDepth * nwarps;
           if (rl < full) skinny_load(buf[(j + kSkinnyDepth) % NB], wp, sp, xrow, rl * 128 + 32 * c);
-          skinny_compute(buf[j], xrow, acc, accu);
+          skinny_compute<NT, SILU, SPLIT>(buf[j], xrow, xrow_lo, acc, accu);
         }
       }
     }
@@ -368,7 +384,7 @@ __global__ void __launch_bounds__(32 * kSkinnyWarps,
   if ((K % 128) != 0 && warp == (full % nwarps)) {
     const int kc = full * 128 + 32 * c;
     skinny_load_tail(buf[0], wp, sp, xrow, kc, kc < K);
-    skinny_compute<NT, SILU, true>(buf[0], xrow, acc, accu);
+    skinny_compute<NT, SILU, SPLIT, true>(buf[0], xrow, xrow_lo, acc, accu);
   }
 
   // Cross-warp reduction in a fixed order.
@@ -407,7 +423,14 @@ __global__ void __launch_bounds__(32 * kSkinnyWarps,
     }
     const int slot = slot0 + tl;
     const int64_t yr = a.y_rows ? a.y_rows[slot] : slot;
-    store_out(a.y, a.y_dtype, yr * a.y_ld + n, out);
+    if (a.y_lo) {
+      // bf16 hi part and the bf16 of the remainder: hi + lo == out to ~2^-16.
+      const uint16_t hb = f32_to_bf16_bits(out);
+      reinterpret_cast<uint16_t *>(a.y)[yr * a.y_ld + n] = hb;
+      a.y_lo[yr * a.y_ld + n] = f32_to_bf16_bits(out - __uint_as_float((uint32_t)hb << 16));
+    } else {
+      store_out(a.y, a.y_dtype, yr * a.y_ld + n, out);
+    }
   }
 }
 
@@ -424,9 +447,11 @@ cudaError_t launch_skinny(const SkinnyArgs &a, cudaStream_t s) {
 #define NVFP4_SKINNY(NT_)                                                  \
   do {                                                                     \
     if (a.silu_gate)                                                       \
-      skinny_kernel<NT_, true><<<grid, block, 0, s>>>(a);                  \
+      skinny_kernel<NT_, true, false><<<grid, block, 0, s>>>(a);           \
+    else if (a.x_lo)                                                       \
+      skinny_kernel<NT_, false, true><<<grid, block, 0, s>>>(a);           \
     else                                                                   \
-      skinny_kernel<NT_, false><<<grid, block, 0, s>>>(a);                 \
+      skinny_kernel<NT_, false, false><<<grid, block, 0, s>>>(a);          \
   } while (0)
   if (tpi == 8)
     NVFP4_SKINNY(1);

@@ -1,0 +1,32 @@
+// moe.h -- device-side plan of the grouped expert GEMMs (internal).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "kernels.h"
+
+namespace nvfp4 {
+
+// Rows sorted by expert: sorted position p holds row dst_row[p], whose
+// activations are row src_row[p] of the input; expert e owns positions
+// [offsets[e], offsets[e+1]).  work[0..n_work) are the grouped-GEMM items.
+struct MoePlan {
+  int32_t *offsets;  // [E + 1]
+  int32_t *n_work;   // [1]
+  int32_t *n_rows;   // [1] rows with a valid expert id
+  SkinnyWork *work;  // [capacity]
+  int32_t *src_row;  // [R]
+  int32_t *dst_row;  // [R]
+};
+
+cudaError_t launch_router(const uint16_t *x, const float *router, float *logits, int T, int H,
+                          int E, int k, int renormalize, int32_t *ids, float *w, cudaStream_t st);
+cudaError_t launch_moe_permute(const int32_t *row_expert, const int32_t *x_row_index, int R, int E,
+                               int tpi, const MoePlan &plan, cudaStream_t st);
+cudaError_t launch_slot_token(int32_t *idx, int R, int k, cudaStream_t st);
+cudaError_t launch_moe_combine(const void *ys, int ys_dtype, const float *w,
+                               const uint16_t *residual, void *y, int y_dtype, int T, int k, int H,
+                               cudaStream_t st);
+
+}  // namespace nvfp4

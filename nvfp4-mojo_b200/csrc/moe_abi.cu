@@ -1,0 +1,275 @@
+// moe_abi.cu -- extern "C" MoE entry points (include/nvfp4.h): validation,
+// workspace layout and the launch sequence of one MoE layer.
+#include "../../include/nvfp4.h"
+#include "abi_util.h"
+#include "kernels.h"
+#include "moe.h"
+
+namespace nvfp4 {
+namespace {
+
+constexpr size_t kAlign = 256;
+
+size_t up(size_t v) { return (v + kAlign - 1) & ~(kAlign - 1); }
+
+// Token slots per grouped-GEMM work item, from the mean rows per expert.
+int choose_tpi(int64_t R, int E) {
+  const int64_t avg = (R + E - 1) / E;
+  return avg <= 8 ? 8 : (avg <= 16 ? 16 : 32);
+}
+
+int64_t work_capacity(int64_t R, int E, int tpi) { return (R + tpi - 1) / tpi + E; }
+
+struct ExpertsLayout {
+  size_t offsets, n_work, n_rows, work, src_row, dst_row, inter, inter_lo, total;
+};
+
+ExpertsLayout experts_layout(const nvfp4_moe_desc &d, int64_t R) {
+  ExpertsLayout L;
+  const int tpi = choose_tpi(R, d.num_experts);
+  size_t o = 0;
+  L.offsets = o;
+  o = up(o + sizeof(int32_t) * (d.num_experts + 1));
+  L.n_work = o;
+  o = up(o + sizeof(int32_t));
+  L.n_rows = o;
+  o = up(o + sizeof(int32_t));
+  L.work = o;
+  o = up(o + sizeof(SkinnyWork) * work_capacity(R, d.num_experts, tpi));
+  L.src_row = o;
+  o = up(o + sizeof(int32_t) * R);
+  L.dst_row = o;
+  o = up(o + sizeof(int32_t) * R);
+  L.inter = o;
+  o = up(o + sizeof(uint16_t) * R * d.intermediate);
+  L.inter_lo = o;
+  o = up(o + sizeof(uint16_t) * R * d.intermediate);
+  L.total = o;
+  return L;
+}
+
+struct ForwardLayout {
+  size_t ids, w, logits, slot_tok, y_slot, experts, total;
+};
+
+ForwardLayout forward_layout(const nvfp4_moe_desc &d, int64_t T) {
+  ForwardLayout L;
+  const int64_t R = T * d.top_k;
+  size_t o = 0;
+  L.ids = o;
+  o = up(o + sizeof(int32_t) * R);
+  L.w = o;
+  o = up(o + sizeof(float) * R);
+  L.logits = o;
+  o = up(o + sizeof(float) * T * d.num_experts);
+  L.slot_tok = o;
+  o = up(o + sizeof(int32_t) * R);
+  L.y_slot = o;
+  o = up(o + sizeof(float) * R * d.hidden);
+  L.experts = o;
+  o = up(o + experts_layout(d, R).total);
+  L.total = o;
+  return L;
+}
+
+int check_desc(const nvfp4_moe_desc *d) {
+  if (!d) return fail(NVFP4_ERR_INVALID_ARG, "null MoE descriptor");
+  if (d->num_experts <= 0 || d->num_experts > 256)
+    return fail(NVFP4_ERR_INVALID_ARG, "num_experts must be in [1, 256]");
+  if (d->top_k <= 0 || d->top_k > 32 || d->top_k > d->num_experts)
+    return fail(NVFP4_ERR_INVALID_ARG, "top_k must be in [1, min(32, num_experts)]");
+  if (d->hidden <= 0 || d->hidden % 128 || d->intermediate <= 0 || d->intermediate % 128)
+    return fail(NVFP4_ERR_INVALID_ARG, "hidden and intermediate must be positive multiples of 128");
+  return NVFP4_OK;
+}
+
+int check_weights(const nvfp4_moe_weights *w) {
+  if (!w || !w->gate_up || !w->gate_up_scale || !w->down || !w->down_scale)
+    return fail(NVFP4_ERR_INVALID_ARG, "null expert weight pointer");
+  if (!aligned(w->gate_up, 16) || !aligned(w->down, 16) || !aligned(w->gate_up_scale, 2) ||
+      !aligned(w->down_scale, 2))
+    return fail(NVFP4_ERR_INVALID_ARG, "expert weights must be 16-byte (scales 2-byte) aligned");
+  return NVFP4_OK;
+}
+
+int run_experts(const nvfp4_moe_desc &d, const nvfp4_moe_weights &w, const uint16_t *x,
+                const int32_t *x_row_index, const int32_t *row_expert, int64_t R,
+                void *y_rows, int y_dtype, uint8_t *ws, cudaStream_t st) {
+  if (R == 0) return NVFP4_OK;
+  const ExpertsLayout L = experts_layout(d, R);
+  const int E = d.num_experts, H = d.hidden, I = d.intermediate;
+  const int tpi = choose_tpi(R, E);
+  MoePlan plan;
+  plan.offsets = reinterpret_cast<int32_t *>(ws + L.offsets);
+  plan.n_work = reinterpret_cast<int32_t *>(ws + L.n_work);
+  plan.n_rows = reinterpret_cast<int32_t *>(ws + L.n_rows);
+  plan.work = reinterpret_cast<SkinnyWork *>(ws + L.work);
+  plan.src_row = reinterpret_cast<int32_t *>(ws + L.src_row);
+  plan.dst_row = reinterpret_cast<int32_t *>(ws + L.dst_row);
+  // The SiLU*up activations are kept as bf16 hi + lo parts so the down
+  // projection sees them to ~2^-16 (one bf16 rounding would cost up to 2^-9
+  // relative per element on the MMA operand).
+  uint16_t *inter = reinterpret_cast<uint16_t *>(ws + L.inter);
+  uint16_t *inter_lo = reinterpret_cast<uint16_t *>(ws + L.inter_lo);
+  int rc = check_launch(launch_moe_permute(row_expert, x_row_index, (int)R, E, tpi, plan, st),
+                        "MoE permutation launch");
+  if (rc) return rc;
+
+  SkinnyArgs gu;
+  gu.ws.w = w.gate_up;
+  gu.ws.sf = w.gate_up_scale;
+  gu.ws.w_group_stride = (int64_t)2 * I * (H / 2);
+  gu.ws.sf_group_stride = (int64_t)2 * I * (H / 16);
+  gu.ws.N = 2 * I;
+  gu.ws.K = H;
+  gu.al.input_scales = w.gate_up_input_scale;
+  gu.al.ws2_rows = w.gate_up_scale_2;
+  gu.al.ws2_group_stride = 2 * I;
+  gu.x = x;
+  gu.x_ld = H;
+  gu.x_rows = plan.src_row;
+  gu.y = inter;
+  gu.y_lo = inter_lo;
+  gu.y_dtype = kBF16;
+  gu.y_ld = I;
+  gu.work = plan.work;
+  gu.n_work = plan.n_work;
+  gu.work_capacity = (int)work_capacity(R, E, tpi);
+  gu.silu_gate = true;
+  gu.tokens_per_item = tpi;
+  rc = check_launch(launch_skinny(gu, st), "MoE gate_up launch");
+  if (rc) return rc;
+
+  SkinnyArgs dn = gu;
+  dn.ws.w = w.down;
+  dn.ws.sf = w.down_scale;
+  dn.ws.w_group_stride = (int64_t)H * (I / 2);
+  dn.ws.sf_group_stride = (int64_t)H * (I / 16);
+  dn.ws.N = H;
+  dn.ws.K = I;
+  dn.al = AlphaSpec();
+  dn.al.input_scales = w.down_input_scale;
+  dn.al.ws2_rows = w.down_scale_2;
+  dn.al.ws2_group_stride = H;
+  dn.x = inter;
+  dn.x_lo = inter_lo;
+  dn.y_lo = nullptr;
+  dn.x_ld = I;
+  dn.x_rows = nullptr;
+  dn.y = y_rows;
+  dn.y_dtype = y_dtype;
+  dn.y_ld = H;
+  dn.y_rows = plan.dst_row;
+  dn.silu_gate = false;
+  return check_launch(launch_skinny(dn, st), "MoE down launch");
+}
+
+}  // namespace
+}  // namespace nvfp4
+
+using namespace nvfp4;
+
+extern "C" size_t nvfp4_moe_workspace_size(const nvfp4_moe_desc *d, int64_t T) {
+  if (check_desc(d) || T < 0) return 0;
+  return forward_layout(*d, T).total;
+}
+
+extern "C" size_t nvfp4_moe_experts_workspace_size(const nvfp4_moe_desc *d, int64_t R) {
+  if (check_desc(d) || R < 0) return 0;
+  return experts_layout(*d, R).total;
+}
+
+extern "C" int nvfp4_moe_route(const nvfp4_moe_desc *d, const float *router, const void *x,
+                               int64_t T, int32_t *ids, float *w, float *logits, void *stream) {
+  int rc = check_desc(d);
+  if (rc) return rc;
+  if (T < 0 || T > (1 << 24)) return fail(NVFP4_ERR_INVALID_ARG, "bad token count");
+  if (T == 0) return NVFP4_OK;
+  if (!router || !x || !ids || !w || !logits)
+    return fail(NVFP4_ERR_INVALID_ARG, "null router, activation or output pointer");
+  return check_launch(launch_router(static_cast<const uint16_t *>(x), router, logits, (int)T,
+                                    d->hidden, d->num_experts, d->top_k, d->renormalize, ids, w,
+                                    static_cast<cudaStream_t>(stream)),
+                      "router launch");
+}
+
+extern "C" int nvfp4_moe_experts(const nvfp4_moe_desc *d, const nvfp4_moe_weights *w,
+                                 const void *x, const int32_t *x_row_index,
+                                 const int32_t *row_expert, int64_t R, void *y_rows, int y_dtype,
+                                 void *ws, size_t ws_bytes, void *stream) {
+  int rc = check_desc(d);
+  if (rc) return rc;
+  if ((rc = check_weights(w))) return rc;
+  if (R < 0 || R > (1 << 24)) return fail(NVFP4_ERR_INVALID_ARG, "bad row count");
+  if (R == 0) return NVFP4_OK;
+  if (!x || !row_expert || !y_rows || !ws)
+    return fail(NVFP4_ERR_INVALID_ARG, "null activation, expert id, output or workspace pointer");
+  if (y_dtype != NVFP4_DTYPE_F32 && y_dtype != NVFP4_DTYPE_BF16)
+    return fail(NVFP4_ERR_INVALID_ARG, "bad output dtype");
+  if (!aligned(x, 16) || !aligned(ws, kAlign))
+    return fail(NVFP4_ERR_INVALID_ARG, "x must be 16-byte and workspace 256-byte aligned");
+  if (ws_bytes < experts_layout(*d, R).total)
+    return fail(NVFP4_ERR_WORKSPACE, "workspace of %zu bytes, %zu needed", ws_bytes,
+                experts_layout(*d, R).total);
+  return run_experts(*d, *w, static_cast<const uint16_t *>(x), x_row_index, row_expert, R, y_rows,
+                     y_dtype, static_cast<uint8_t *>(ws), static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int nvfp4_moe_combine(const void *y_slots, int slot_dtype, const float *topk_w,
+                                 const void *residual, void *y, int y_dtype, int64_t T, int32_t k,
+                                 int32_t H, void *stream) {
+  if (T < 0 || k <= 0 || H <= 0 || H % 8) return fail(NVFP4_ERR_INVALID_ARG, "bad combine shape");
+  if ((slot_dtype != NVFP4_DTYPE_F32 && slot_dtype != NVFP4_DTYPE_BF16) ||
+      (y_dtype != NVFP4_DTYPE_F32 && y_dtype != NVFP4_DTYPE_BF16))
+    return fail(NVFP4_ERR_INVALID_ARG, "bad slot or output dtype");
+  if (T == 0) return NVFP4_OK;
+  if (!y_slots || !topk_w || !y) return fail(NVFP4_ERR_INVALID_ARG, "null combine pointer");
+  if (!aligned(y_slots, 16) || !aligned(y, 16) || (residual && !aligned(residual, 16)))
+    return fail(NVFP4_ERR_INVALID_ARG, "combine buffers must be 16-byte aligned");
+  return check_launch(launch_moe_combine(y_slots, slot_dtype, topk_w,
+                                         static_cast<const uint16_t *>(residual), y, y_dtype,
+                                         (int)T, k, H, static_cast<cudaStream_t>(stream)),
+                      "combine launch");
+}
+
+extern "C" int nvfp4_moe_forward(const nvfp4_moe_desc *d, const nvfp4_moe_weights *w,
+                                 const void *x, const void *residual, void *y, int y_dtype,
+                                 int64_t T,
+                                 int32_t *topk_ids, float *topk_w, void *ws, size_t ws_bytes,
+                                 void *stream) {
+  int rc = check_desc(d);
+  if (rc) return rc;
+  if ((rc = check_weights(w))) return rc;
+  if (!w->router) return fail(NVFP4_ERR_INVALID_ARG, "null router pointer");
+  if (T < 0 || T * d->top_k > (1 << 24)) return fail(NVFP4_ERR_INVALID_ARG, "bad token count");
+  if (T == 0) return NVFP4_OK;
+  if (!x || !y || !ws) return fail(NVFP4_ERR_INVALID_ARG, "null activation, output or workspace");
+  if (y_dtype != NVFP4_DTYPE_F32 && y_dtype != NVFP4_DTYPE_BF16)
+    return fail(NVFP4_ERR_INVALID_ARG, "bad output dtype");
+  if (!aligned(x, 16) || !aligned(y, 16) || (residual && !aligned(residual, 16)) ||
+      !aligned(ws, kAlign))
+    return fail(NVFP4_ERR_INVALID_ARG, "x/y/residual must be 16-byte and workspace 256-byte aligned");
+  const ForwardLayout L = forward_layout(*d, T);
+  if (ws_bytes < L.total)
+    return fail(NVFP4_ERR_WORKSPACE, "workspace of %zu bytes, %zu needed", ws_bytes, L.total);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t *base = static_cast<uint8_t *>(ws);
+  int32_t *ids = topk_ids ? topk_ids : reinterpret_cast<int32_t *>(base + L.ids);
+  float *tw = topk_w ? topk_w : reinterpret_cast<float *>(base + L.w);
+  float *logits = reinterpret_cast<float *>(base + L.logits);
+  int32_t *slot_tok = reinterpret_cast<int32_t *>(base + L.slot_tok);
+  float *y_slot = reinterpret_cast<float *>(base + L.y_slot);
+  const int64_t R = T * d->top_k;
+  rc = check_launch(launch_router(static_cast<const uint16_t *>(x), w->router, logits, (int)T,
+                                  d->hidden, d->num_experts, d->top_k, d->renormalize, ids, tw, st),
+                    "router launch");
+  if (rc) return rc;
+  rc = check_launch(launch_slot_token(slot_tok, (int)R, d->top_k, st), "slot index launch");
+  if (rc) return rc;
+  rc = run_experts(*d, *w, static_cast<const uint16_t *>(x), slot_tok, ids, R, y_slot, kF32,
+                   base + L.experts, st);
+  if (rc) return rc;
+  return check_launch(launch_moe_combine(y_slot, kF32, tw, static_cast<const uint16_t *>(residual),
+                                         y, y_dtype, (int)T, d->top_k, d->hidden, st),
+                      "combine launch");
+}

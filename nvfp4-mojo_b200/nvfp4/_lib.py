@@ -57,6 +57,24 @@ class LinearDesc(ctypes.Structure):
     ]
 
 
+class MoEDesc(ctypes.Structure):
+    """struct nvfp4_moe_desc."""
+
+    _fields_ = [("num_experts", ctypes.c_int32), ("top_k", ctypes.c_int32),
+                ("hidden", ctypes.c_int32), ("intermediate", ctypes.c_int32),
+                ("renormalize", ctypes.c_int32)]
+
+
+class MoEWeightPtrs(ctypes.Structure):
+    """struct nvfp4_moe_weights (device pointers)."""
+
+    _fields_ = [("router", ctypes.c_void_p), ("gate_up", ctypes.c_void_p),
+                ("gate_up_scale", ctypes.c_void_p), ("gate_up_scale_2", ctypes.c_void_p),
+                ("gate_up_input_scale", ctypes.c_void_p), ("down", ctypes.c_void_p),
+                ("down_scale", ctypes.c_void_p), ("down_scale_2", ctypes.c_void_p),
+                ("down_input_scale", ctypes.c_void_p)]
+
+
 _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
 _int = ctypes.c_int
@@ -74,6 +92,15 @@ SIGNATURES = {
     "nvfp4_dequant_tile": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
     "nvfp4_dequant": (_int, [_vp, _vp, _i64, _i64, _vp, _int, _vp]),
     "nvfp4_device_status": (_int, []),
+    "nvfp4_moe_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(MoEDesc), _i64]),
+    "nvfp4_moe_experts_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(MoEDesc), _i64]),
+    "nvfp4_moe_forward": (_int, [ctypes.POINTER(MoEDesc), ctypes.POINTER(MoEWeightPtrs), _vp, _vp,
+                                 _vp, _int, _i64, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
+    "nvfp4_moe_route": (_int, [ctypes.POINTER(MoEDesc), _vp, _vp, _i64, _vp, _vp, _vp, _vp]),
+    "nvfp4_moe_experts": (_int, [ctypes.POINTER(MoEDesc), ctypes.POINTER(MoEWeightPtrs), _vp, _vp,
+                                 _vp, _i64, _vp, _int, _vp, ctypes.c_size_t, _vp]),
+    "nvfp4_moe_combine": (_int, [_vp, _int, _vp, _vp, _vp, _int, _i64, ctypes.c_int32,
+                                 ctypes.c_int32, _vp]),
 }
 
 _lib = None

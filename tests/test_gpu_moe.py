@@ -1,0 +1,157 @@
+"""GPU parity of the NVFP4 MoE layer (router, top-k, grouped gate_up with
+SiLU*up, grouped down, combine) against the CPU oracle, through the C ABI.
+
+Tolerances.  fp32 output: max|err| <= 1e-3 * RMS(ref) -- the SiLU*up
+activations feed the down projection as bf16 hi + lo parts, so only
+summation order and the 2^-16 split residue remain.  bf16 output: per element
+|err| <= 2e-2 * RMS(ref) + 2^-8 * |ref|, the bf16-operand bound plus the
+output's own rounding (half an ulp of bf16 is up to 2^-8 of the value, and
+these synthetic layers have max|y| / RMS(y) up to ~9).
+Router near-ties: where the oracle's k-th and (k+1)-th probabilities differ
+by less than 1e-5, summation-order differences may legitimately swap the
+selection; such tokens replay the GPU's choice in the oracle (force_ids) and
+are counted.  Every other token must select exactly the oracle's experts.
+"""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-2
+TIE_GAP = 1e-5
+
+
+def rel_err(got, ref):
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    return float(np.abs(got - ref).max() / np.sqrt(np.mean(ref * ref)))
+
+
+def near_ties(probs, k):
+    s = -np.sort(-probs, axis=1)
+    return (s[:, k - 1] - s[:, k]) < TIE_GAP
+
+
+def setup(E, H, I, T, seed):
+    from nvfp4 import synthetic
+    from nvfp4.moe import MoEWeights
+
+    wd = synthetic.moe_weights(E, H, I, seed=seed)
+    x = synthetic.bf16_round(synthetic.activations(T, H, seed=seed + 1))
+    w = MoEWeights.from_dict(wd)
+    return wd, x, w
+
+
+def check_layer(O, wd, x, w, k, tokens=None, residual=None):
+    from nvfp4.moe import MoELayer
+
+    T, H = x.shape
+    layer = MoELayer(w, top_k=k)
+    X = torch.from_numpy(x).cuda().to(torch.bfloat16)
+    ids = torch.empty((T, k), dtype=torch.int32, device="cuda")
+    tw = torch.empty((T, k), dtype=torch.float32, device="cuda")
+    Rz = None if residual is None else torch.from_numpy(residual).cuda().to(torch.bfloat16)
+    y = layer(X, residual=Rz, topk_ids=ids, topk_w=tw).float().cpu().numpy()
+    y32 = layer(X, residual=Rz, out=torch.empty((T, H), dtype=torch.float32, device="cuda"))
+    y32 = y32.cpu().numpy()
+    ids = ids.cpu().numpy()
+    tok = np.arange(T) if tokens is None else np.asarray(tokens)
+    _, probs = O.router(x[tok], wd["router"])
+    ties = near_ties(probs, k)
+    ref, ref_ids, _ = O.moe(x, wd, top_k=k, tokens=tok, n_threads=8)
+    mismatch = [i for i in range(len(tok)) if not np.array_equal(ref_ids[i], ids[tok[i]])]
+    assert all(ties[i] for i in mismatch), f"routing differs away from near-ties: {mismatch[:5]}"
+    if mismatch:
+        ref, _, _ = O.moe(x, wd, top_k=k, tokens=tok, force_ids=ids[tok], n_threads=8)
+    if residual is not None:
+        ref = ref + residual[tok]
+    rms = np.sqrt(np.mean(ref.astype(np.float64) ** 2))
+    excess = np.abs(y[tok] - ref) - (TOL * rms + 2.0 ** -8 * np.abs(ref))
+    err = rel_err(y[tok], ref)
+    assert excess.max() <= 0.0, (err, len(mismatch))
+    err32 = rel_err(y32[tok], ref)
+    assert err32 <= 1e-3, (err32, len(mismatch))
+    return err, len(mismatch)
+
+
+@pytest.mark.parametrize("T", [1, 5, 64, 300])
+def test_moe_small(O, cuda, T):
+    wd, x, w = setup(E=8, H=256, I=128, T=T, seed=T)
+    check_layer(O, wd, x, w, k=2)
+
+
+@pytest.mark.parametrize("T", [1, 16, 256])
+def test_moe_config3(O, cuda, T):
+    """One MoE FFN layer: 128 experts, top-8, hidden 2048, intermediate 768."""
+    wd, x, w = setup(E=128, H=2048, I=768, T=T, seed=100 + T)
+    check_layer(O, wd, x, w, k=8)
+
+
+def test_moe_config3_large_sampled(O, cuda):
+    """T = 4096 tokens, oracle on a sample of tokens; with a residual add."""
+    T = 4096
+    wd, x, w = setup(E=128, H=2048, I=768, T=T, seed=7)
+    res = np.random.default_rng(8).standard_normal((T, 2048)).astype(np.float32)
+    res = torch.from_numpy(res).to(torch.bfloat16).float().numpy()
+    tok = np.sort(np.random.default_rng(9).choice(T, 48, replace=False))
+    check_layer(O, wd, x, w, k=8, tokens=tok, residual=res)
+
+
+def test_route_matches_oracle(O, cuda):
+    from nvfp4.moe import moe_route
+
+    wd, x, w = setup(E=128, H=2048, I=768, T=512, seed=3)
+    ids, tw, logits = moe_route(w, torch.from_numpy(x).cuda().to(torch.bfloat16), top_k=8)
+    ref_logits, probs = O.router(x, wd["router"])
+    assert rel_err(logits.cpu().numpy(), ref_logits) <= 1e-5
+    ids = ids.cpu().numpy()
+    ties = near_ties(probs, 8)
+    for t in range(x.shape[0]):
+        order = sorted(range(128), key=lambda e: (-probs[t, e], e))[:8]
+        if not ties[t]:
+            assert list(ids[t]) == order
+    s = tw.cpu().numpy().sum(1)
+    assert np.allclose(s, 1.0, atol=1e-5)
+
+
+def test_experts_rows_and_invalid_ids(O, cuda):
+    """moe_experts over explicit rows; rows with expert id -1 stay untouched."""
+    from nvfp4.moe import moe_experts
+
+    E, H, I, R = 16, 256, 128, 40
+    wd, x, w = setup(E=E, H=H, I=I, T=R, seed=21)
+    rng = np.random.default_rng(22)
+    ids = rng.integers(0, E, R).astype(np.int32)
+    ids[[3, 17]] = -1
+    out = torch.full((R, H), 7.0, dtype=torch.float32, device="cuda")
+    moe_experts(w, torch.from_numpy(x).cuda().to(torch.bfloat16),
+                torch.from_numpy(ids).cuda(), out=out, top_k=2)
+    got = out.float().cpu().numpy()
+    assert np.all(got[[3, 17]] == 7.0)
+    for r in range(R):
+        if ids[r] < 0:
+            continue
+        e = ids[r]
+        h = O.matvec(wd["gu_w"][e], wd["gu_sf"][e], x[r], ws2_rows=wd["gu_ws2"][e])
+        a = np.array([O.silu(float(v)) for v in h[:I]], np.float32) * h[I:]
+        y = O.matvec(wd["dn_w"][e], wd["dn_sf"][e], a, ws2_rows=wd["dn_ws2"][e])
+        assert rel_err(got[r], y) <= TOL, r
+
+
+def test_workspace_too_small_is_an_error(cuda):
+    import ctypes
+
+    from nvfp4 import _lib
+    from nvfp4.moe import MoELayer
+
+    _, x, w = setup(E=8, H=256, I=128, T=4, seed=1)
+    layer = MoELayer(w, top_k=2)
+    X = torch.from_numpy(x).cuda().to(torch.bfloat16)
+    y = torch.empty_like(X)
+    ws = torch.empty(64, dtype=torch.uint8, device="cuda")
+    rc = _lib.load().nvfp4_moe_forward(ctypes.byref(layer.desc), ctypes.byref(layer.ptrs),
+                                        X.data_ptr(), None, y.data_ptr(), _lib.DTYPE_BF16, 4,
+                                        None, None,
+                                        ws.data_ptr(), ws.numel(), None)
+    assert rc == _lib.NVFP4_ERR_WORKSPACE
