@@ -379,7 +379,103 @@ class MoELayerBench:
         return run, float(n_tok), desc
 
 
-WORKLOADS = {"gemv": GemvSweep, "prefill": PrefillSweep, "moe": MoELayerBench}
+# ---------------------------------------------------------------------------
+# Workload: 48-layer stack of the MoE layer, expert-parallel over the ranks.
+# ---------------------------------------------------------------------------
+class EPStackBench:
+    name = "ep"
+    unit = "tokens/s"
+    graphable = False  # the per-layer slot counts are read on the host (exchange sizes)
+    scaling = "strong"  # the global token batch is fixed; experts and tokens split over GPUs
+
+    def __init__(self, device, seed=0, tokens=64, layers=48):
+        import torch
+        import torch.distributed as dist
+        from nvfp4.ep import EPMoELayer
+        from nvfp4.moe import MoEWeights
+
+        self.torch = torch
+        world = dist.get_world_size() if dist.is_initialized() else 1
+        rank = dist.get_rank() if dist.is_initialized() else 0
+        if tokens % world:
+            raise ValueError("global token count must divide by the number of GPUs")
+        self.T = tokens
+        self.T_local = tokens // world
+        epr = MOE_E // world
+        self.workload = (f"{layers}-layer stack of pre-norm MoE blocks h += MoE(RMSNorm(h)) (128 "
+                         f"experts, top-8, hidden 2048, intermediate 768, NVFP4 experts; the "
+                         f"residual add is fused in the combine); "
+                         f"expert-parallel over {world} GPU(s) ({epr} experts each) with NCCL "
+                         f"all-to-all dispatch/combine; {tokens} bf16 tokens ~N(0,1) per step "
+                         f"({self.T_local} per GPU)")
+        self.layers = []
+        for l in range(layers):
+            g = torch.Generator(device=device)
+            g.manual_seed(1000 + l)  # router identical on every rank
+            router = torch.randn((MOE_H, MOE_E), generator=g, device=device) * 0.02
+            wd = synthetic_local_experts(epr, seed=seed + 7919 * l + 104729 * rank, device=device)
+            wd["router"] = router
+            local = MoEWeights.from_dict(wd, device)
+            self.layers.append(EPMoELayer(local, router, top_k=MOE_K, num_experts=MOE_E))
+        self.x = torch.randn((self.T_local, MOE_H), device=device).to(torch.bfloat16)
+        self.sets = 1
+        self.launches_per_step = layers * 10
+        self.dominant_bytes = None
+        self.config = {"workload": self.workload, "layers": layers, "global_tokens": tokens,
+                       "experts_per_gpu": epr, "parallelism": f"ep{world}",
+                       "l2": f"inputs larger than L2: {layers} layers x {342 // world} MB of "
+                             f"expert weights per GPU per step"}
+
+    def run_step(self, i):
+        torch = self.torch
+        h = self.x
+        for L in self.layers:
+            hf = h.float()
+            hn = (hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + 1e-6)).to(torch.bfloat16)
+            h = L(hn, residual=h)
+        self.out = h
+
+    def units(self, steps):
+        return self.T_local * steps  # per rank; the job total is this times the world size
+
+    def e2e_setup(self):
+        torch = self.torch
+        self.h_x = torch.randn(self.x.shape).to(torch.bfloat16).pin_memory()
+        self.h_y = torch.empty(self.x.shape, dtype=torch.bfloat16).pin_memory()
+        self.h2d = self.h_x.numel() * 2
+        self.d2h = self.h_y.numel() * 2
+
+    def e2e_step(self, i):
+        self.x.copy_(self.h_x, non_blocking=True)
+        self.run_step(i)
+        self.h_y.copy_(self.out, non_blocking=True)
+
+    def cpu_sample(self, threads, n_tok=8):
+        from nvfp4 import synthetic
+        from oracle import oracle as O
+
+        wd = synthetic.moe_weights(MOE_E, MOE_H, MOE_I, seed=5)
+        x = synthetic.activations(n_tok, MOE_H, seed=6)
+
+        def run():
+            O.moe(x, wd, top_k=MOE_K, n_threads=threads)
+
+        desc = (f"{n_tok} tokens through one layer, reported per layer-token and divided by "
+                f"the layer count (oracle cost is linear in tokens and layers)")
+        return run, float(n_tok) / len(self.layers), desc
+
+
+def synthetic_local_experts(epr, seed, device):
+    """NVFP4 expert weights of `epr` experts (distributions of nvfp4.synthetic)."""
+    from nvfp4 import synthetic
+
+    d = synthetic.moe_weights_cuda(epr, MOE_H, MOE_I, seed=seed, device=device)
+    d.pop("router")
+    return d
+
+
+WORKLOADS = {"gemv": GemvSweep, "prefill": PrefillSweep, "moe": MoELayerBench,
+             "ep": EPStackBench}
 
 
 # ---------------------------------------------------------------------------
@@ -473,9 +569,13 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
-    ap.add_argument("--tokens", type=int, default=4096, help="MoE workload: tokens per step")
+    ap.add_argument("--tokens", type=int, default=None,
+                    help="MoE: tokens per step (default 4096); EP stack: global tokens (default 64)")
+    ap.add_argument("--layers", type=int, default=48, help="EP stack: number of MoE layers")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.tokens is None:
+        args.tokens = 64 if args.workload == "ep" else 4096
 
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -488,7 +588,9 @@ def main():
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     peaks = load_peaks()
-    kw = {"tokens": args.tokens} if args.workload == "moe" else {}
+    kw = {"tokens": args.tokens} if args.workload in ("moe", "ep") else {}
+    if args.workload == "ep":
+        kw["layers"] = args.layers
     wl = WORKLOADS[args.workload](device, seed=17 * rank, **kw)
     stream = torch.cuda.Stream(device)
 
@@ -499,7 +601,7 @@ def main():
     torch.cuda.synchronize()
 
     graphs = None
-    if not args.no_graph:
+    if not args.no_graph and getattr(wl, "graphable", True):
         graphs = []
         for s in range(getattr(wl, "sets", 1)):
             g = torch.cuda.CUDAGraph()
@@ -576,7 +678,7 @@ def main():
     e2e_value = wl.units(args.steps) * world / (e2e_ms / 1e3)
 
     roof = None
-    if dom_ms:
+    if dom_ms and wl.dominant_bytes:
         traffic = load_traffic(wl.name)
         if getattr(wl, "bound", "hbm") == "tensor":
             achieved = wl.dominant_bytes / (dom_ms / 1e3) / 1e12
@@ -609,9 +711,10 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": wl.unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic", "config": dict(wl.config, parallelism=(
-                "replicas" if world > 1 else "single GPU"), graph=bool(graphs)),
+            "higher_is_better": True, "scaling": getattr(wl, "scaling", "weak"),
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "config": dict({"parallelism": (
+                "replicas" if world > 1 else "single GPU")}, **wl.config, graph=bool(graphs)),
             "roofline": roof, "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": wl.unit, "h2d_bytes_per_step": wl.h2d,
                     "d2h_bytes_per_step": wl.d2h},

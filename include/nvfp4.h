@@ -207,11 +207,29 @@ int nvfp4_moe_experts(const nvfp4_moe_desc *desc, const nvfp4_moe_weights *weigh
                       int64_t R, void *y_rows, int y_dtype, void *workspace,
                       size_t workspace_bytes, void *stream);
 
-/* y[t] = sum_j topk_w[t, j] * y_slots[t*k + j] (+ residual[t]): fp32 sums in
- * j order; residual bf16; y_slots and y fp32 or bf16 (slot_dtype, y_dtype). */
+/* y[t] = sum_j topk_w[t, j] * y_slots[row(t*k + j)] (+ residual[t]) with
+ * row(s) = slot_pos ? slot_pos[s] : s: fp32 sums in j order; residual bf16;
+ * y_slots and y fp32 or bf16 (slot_dtype, y_dtype). */
 int nvfp4_moe_combine(const void *y_slots, int slot_dtype, const float *topk_w,
-                      const void *residual, void *y, int y_dtype, int64_t T, int32_t k,
-                      int32_t hidden, void *stream);
+                      const int32_t *slot_pos, const void *residual, void *y, int y_dtype,
+                      int64_t T, int32_t k, int32_t hidden, void *stream);
+
+/*
+ * Expert-parallel dispatch plan (the exchange itself is NCCL all-to-all over
+ * NVLink, driven by the host): slot s = t*k + j with global expert
+ * e = topk_ids[s] goes to rank e / experts_per_rank as local expert
+ * e % experts_per_rank.  Writes send_counts [world], and in send order
+ * (grouped by rank; slot order within a rank) send_token [T*k] and
+ * send_expert [T*k]; slot_pos [T*k] = send position of each slot.
+ */
+int nvfp4_ep_dispatch_plan(const int32_t *topk_ids, int64_t T, int32_t k,
+                           int32_t experts_per_rank, int32_t world, int32_t *send_counts,
+                           int32_t *send_token, int32_t *send_expert, int32_t *slot_pos,
+                           void *stream);
+
+/* dst[i] = src[row_index[i]] for n rows of row_bytes bytes (multiple of 16). */
+int nvfp4_gather_rows(const void *src, const int32_t *row_index, int64_t n, int64_t row_bytes,
+                      void *dst, void *stream);
 
 #ifdef __cplusplus
 }

@@ -185,11 +185,11 @@ cudaError_t launch_linear_f32(const WeightSpec &ws, const AlphaSpec &al, const v
 #ifndef NVFP4_SKINNY_WARPS
 #define NVFP4_SKINNY_WARPS 4
 #endif
-#ifndef NVFP4_SKINNY_DEPTH
-#define NVFP4_SKINNY_DEPTH 1
+#ifndef NVFP4_SKINNY_PIPE
+#define NVFP4_SKINNY_PIPE 4
 #endif
 constexpr int kSkinnyWarps = NVFP4_SKINNY_WARPS;
-constexpr int kSkinnyDepth = NVFP4_SKINNY_DEPTH;
+constexpr int kSkinnyPipe = NVFP4_SKINNY_PIPE;
 
 // Per-round operands of one lane: 16 bytes of codes and 2 scales for each of
 // its rows (g, g+8, and their `up` rows for the SiLU-gated form), plus the
@@ -242,7 +242,8 @@ template <int NT, bool SILU, bool SPLIT, bool TAIL = false>
 __device__ __forceinline__ void skinny_compute(const SkinnyRound<NT, SILU> &d,
                                                const uint16_t *const (&xrow)[NT],
                                                const uint16_t *const (&xrow_lo)[NT],
-                                               float (&acc)[NT][4], float (&accu)[NT][4]) {
+                                               float (&acc)[NT][4], float (&accu)[NT][4],
+                                               const uint32_t *slut) {
   constexpr int R = SkinnyRound<NT, SILU>::R;
   // Activations are small and shared by every CTA on the SM: L1-resident.
   // SPLIT: the activations are hi + lo bf16 parts (x = hi + lo to ~2^-16);
@@ -259,9 +260,13 @@ __device__ __forceinline__ void skinny_compute(const SkinnyRound<NT, SILU> &d,
                                    ? __ldg(reinterpret_cast<const uint4 *>(xrow_lo[t] + d.kc + 8 * q))
                                    : make_uint4(0, 0, 0, 0);
     }
+  // e4m3 -> bf16x2 (scale * 2^119) through the CTA's 256-entry table.
   uint32_t sc[R][2];
 #pragma unroll
-  for (int i = 0; i < R; ++i) scale_pair_to_bf16x2(d.s[i], sc[i][0], sc[i][1]);
+  for (int i = 0; i < R; ++i) {
+    sc[i][0] = slut[d.s[i] & 0xffu];
+    sc[i][1] = slut[(d.s[i] >> 8) & 0xffu];
+  }
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     const int gsel = q >> 1;
@@ -303,9 +308,18 @@ __global__ void __launch_bounds__(32 * kSkinnyWarps,
                                   : (NT == 4 ? 2 : ((SILU || SPLIT) ? 3 : 4)) * 4 / kSkinnyWarps)
     skinny_kernel(SkinnyArgs a) {
   constexpr int NACC = NT * 4 * (SILU ? 2 : 1);
-  __shared__ float red[kSkinnyWarps][NACC][32];
+  constexpr int RR = SILU ? 4 : 2;
+  // The cp.async ring and, after the main loop, the cross-warp reduction
+  // share one buffer.
+  constexpr int RING_BYTES = kSkinnyWarps * kSkinnyPipe * (RR * 512 + RR * 128);
+  constexpr int RED_BYTES = kSkinnyWarps * NACC * 32 * 4;
+  __shared__ uint32_t slut[256];
+  __shared__ __align__(16) uint8_t skinny_smem[RING_BYTES > RED_BYTES ? RING_BYTES : RED_BYTES];
+  float(*red)[NACC][32] = reinterpret_cast<float(*)[NACC][32]>(skinny_smem);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const int g = lane >> 2, c = lane & 3;
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) slut[i] = scale_to_bf16x2_2p119(i);
+  __syncthreads();
 
   int group = 0, slot0, count;
   if (a.work) {
@@ -353,41 +367,69 @@ __global__ void __launch_bounds__(32 * kSkinnyWarps,
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[t][i] = accu[t][i] = 0.0f;
 
-  // Software pipeline over this warp's full rounds r = warp + i * nwarps with a
-  // ring of kSkinnyDepth + 1 register buffers: rounds i+1 .. i+depth are in
-  // flight while round i decodes and multiplies.  The ring loop is unrolled
-  // so every buffer index is static.
-  constexpr int NB = kSkinnyDepth + 1;
+  // Software pipeline over this warp's full rounds r = warp + i * nwarps:
+  // cp.async streams each lane's 16-byte code chunks (and the 4 scale bytes
+  // holding its two blockscales) into a per-warp shared-memory ring that is
+  // kSkinnyPipe rounds deep, so the HBM latency is covered without holding
+  // the data in registers.  Each lane reads back only what it copied itself.
+  constexpr int PD = kSkinnyPipe;
+  constexpr int WSTAGE = R * 512;       // bytes of codes per round per warp
+  constexpr int SSTAGE = R * 32 * 4;    // bytes of scales per round per warp
+  uint8_t *wring = skinny_smem + warp * PD * (WSTAGE + SSTAGE);
+  uint8_t *sring = wring + PD * WSTAGE;
+  const uint32_t wr0 = smem_addr(wring) + g * 64 + c * 16;
+  const uint32_t sr0 = smem_addr(sring) + lane * 4;
   const int full = K / 128;
-  SkinnyRound<NT, SILU> buf[NB];
+  const int cbyte = 4 * (c >> 1);         // this lane's 4-byte scale word within the 8
+  const int cshift = 16 * (c & 1);        // and its two bytes within that word
 #pragma unroll
-  for (int i = 0; i < kSkinnyDepth; ++i) {
+  for (int i = 0; i < PD; ++i) {
     const int rr = warp + i * nwarps;
-    if (rr < full) skinny_load(buf[i], wp, sp, xrow, rr * 128 + 32 * c);
-  }
-  bool done = false;
-  for (int base = 0; !done; base += NB) {
+    if (rr < full) {
+      const int kc = rr * 128 + 32 * c;
 #pragma unroll
-    for (int j = 0; j < NB; ++j) {
-      if (!done) {
-        const int rr = warp + (base + j) * nwarps;
-        if (rr >= full) {
-          done = true;
-        } else {
-          const int rl = rr + kSkinnyDepth * nwarps;
-          if (rl < full) skinny_load(buf[(j + kSkinnyDepth) % NB], wp, sp, xrow, rl * 128 + 32 * c);
-          skinny_compute<NT, SILU, SPLIT>(buf[j], xrow, xrow_lo, acc, accu);
-        }
+      for (int q = 0; q < R; ++q) {
+        cp_async_16(wr0 + i * WSTAGE + q * 512, wp[q] + kc / 2);
+        cp_async_4(sr0 + i * SSTAGE + q * 128, sp[q] + rr * 8 + cbyte);
       }
     }
+    cp_async_commit();
   }
+  int stage = 0;
+  for (int i = 0;; ++i) {
+    const int rr = warp + i * nwarps;
+    if (rr >= full) break;
+    cp_async_wait<PD - 1>();
+    SkinnyRound<NT, SILU> d;
+#pragma unroll
+    for (int q = 0; q < R; ++q) {
+      d.w[q] = lds_v4(wr0 + stage * WSTAGE + q * 512);
+      d.s[q] = (lds_u32(sr0 + stage * SSTAGE + q * 128) >> cshift) & 0xffffu;
+    }
+    d.kc = rr * 128 + 32 * c;
+    skinny_compute<NT, SILU, SPLIT>(d, xrow, xrow_lo, acc, accu, slut);
+    const int rl = rr + PD * nwarps;
+    if (rl < full) {
+      const int kc = rl * 128 + 32 * c;
+#pragma unroll
+      for (int q = 0; q < R; ++q) {
+        cp_async_16(wr0 + stage * WSTAGE + q * 512, wp[q] + kc / 2);
+        cp_async_4(sr0 + stage * SSTAGE + q * 128, sp[q] + rl * 8 + cbyte);
+      }
+    }
+    cp_async_commit();
+    stage = stage + 1 == PD ? 0 : stage + 1;
+  }
+  cp_async_wait<0>();
+  SkinnyRound<NT, SILU> buf[1];
   if ((K % 128) != 0 && warp == (full % nwarps)) {
     const int kc = full * 128 + 32 * c;
     skinny_load_tail(buf[0], wp, sp, xrow, kc, kc < K);
-    skinny_compute<NT, SILU, SPLIT, true>(buf[0], xrow, xrow_lo, acc, accu);
+    skinny_compute<NT, SILU, SPLIT, true>(buf[0], xrow, xrow_lo, acc, accu, slut);
   }
 
-  // Cross-warp reduction in a fixed order.
+  // Cross-warp reduction in a fixed order (the ring's memory is reused).
+  __syncthreads();
 #pragma unroll
   for (int t = 0; t < NT; ++t)
 #pragma unroll

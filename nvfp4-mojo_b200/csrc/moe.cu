@@ -21,64 +21,58 @@
 namespace nvfp4 {
 
 // ---------------------------------------------------------------------------
-// Router: logits[t, e] = sum_h x[t, h] * router[h, e] (fp32), then per token
-// softmax, top-k and renormalisation.  A CTA owns 16 tokens and all experts
-// (E <= 256); router rows are staged through shared memory in chunks of 32.
+// Router: logits[t, e] = sum_h x[t, h] * router[h, e] (fp32 FMA).  A CTA owns
+// 32 experts x 8 tokens; its 8 warps split H, lane = expert (router rows are
+// expert-contiguous, so a warp reads 128 coalesced bytes per h), the 8
+// tokens' activations come from shared memory as fp32 [H][8]; partial sums of
+// the warps are added in a fixed order.
 // ---------------------------------------------------------------------------
-constexpr int kRouterTok = 16;
-constexpr int kRouterChunk = 32;
+constexpr int kRouterTok = 8;
+constexpr int kRouterWarps = 8;
 
-__global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t *__restrict__ x,
-                                                            const float *__restrict__ router,
-                                                            float *__restrict__ logits, int T,
-                                                            int H, int E) {
-  __shared__ float rs[kRouterChunk][256];
-  __shared__ float xs[kRouterTok][kRouterChunk];
-  const int t0 = blockIdx.x * kRouterTok;
-  const int tid = threadIdx.x;
-  // Thread computes experts e = tid % 64 + 64 * c (c < 4) for tokens
-  // tid / 64 + 4 * i (i < 4).
-  const int e_lane = tid & 63, t_lane = tid >> 6;
-  float acc[4][4];
+__global__ void __launch_bounds__(32 * kRouterWarps)
+    router_logits_kernel(const uint16_t *__restrict__ x, const float *__restrict__ router,
+                         float *__restrict__ logits, int T, int H, int E) {
+  extern __shared__ float4 rsm[];  // xs [H][8] fp32, then red [warps][8][32]
+  float *xs = reinterpret_cast<float *>(rsm);
+  float *red = xs + (size_t)H * kRouterTok;
+  const int e0 = blockIdx.x * 32, t0 = blockIdx.y * kRouterTok;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int i = threadIdx.x; i < H * kRouterTok; i += blockDim.x) {
+    const int h = i / kRouterTok, tt = i % kRouterTok;
+    const int t = t0 + tt;
+    xs[i] = t < T ? __uint_as_float((uint32_t)x[(int64_t)t * H + h] << 16) : 0.0f;
+  }
+  __syncthreads();
+  const int e = min(e0 + lane, E - 1);
+  const int hs = H / kRouterWarps, hb = warp * hs;
+  float acc[kRouterTok];
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
-#pragma unroll
-    for (int c = 0; c < 4; ++c) acc[i][c] = 0.0f;
-  for (int h0 = 0; h0 < H; h0 += kRouterChunk) {
-    for (int idx = tid; idx < kRouterChunk * E; idx += 256) {
-      const int hh = idx / E, e = idx % E;
-      rs[hh][e] = (h0 + hh < H) ? router[(int64_t)(h0 + hh) * E + e] : 0.0f;
-    }
-    for (int idx = tid; idx < kRouterTok * kRouterChunk; idx += 256) {
-      const int tt = idx / kRouterChunk, hh = idx % kRouterChunk;
-      const int t = t0 + tt;
-      xs[tt][hh] = (t < T && h0 + hh < H)
-                       ? __uint_as_float((uint32_t)x[(int64_t)t * H + h0 + hh] << 16)
-                       : 0.0f;
-    }
-    __syncthreads();
-#pragma unroll 4
-    for (int hh = 0; hh < kRouterChunk; ++hh) {
-      float r[4], xv[4];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) r[c] = rs[hh][e_lane + 64 * c];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) xv[i] = xs[t_lane + 4 * i][hh];
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) acc[i][c] = fmaf(xv[i], r[c], acc[i][c]);
-    }
-    __syncthreads();
+  for (int i = 0; i < kRouterTok; ++i) acc[i] = 0.0f;
+  const float *rp = router + (int64_t)hb * E + e;
+#pragma unroll 8
+  for (int h = 0; h < hs; ++h) {
+    const float r = __ldg(rp + (int64_t)h * E);
+    const float4 xa = *reinterpret_cast<const float4 *>(xs + (hb + h) * kRouterTok);
+    const float4 xb = *reinterpret_cast<const float4 *>(xs + (hb + h) * kRouterTok + 4);
+    acc[0] = fmaf(xa.x, r, acc[0]);
+    acc[1] = fmaf(xa.y, r, acc[1]);
+    acc[2] = fmaf(xa.z, r, acc[2]);
+    acc[3] = fmaf(xa.w, r, acc[3]);
+    acc[4] = fmaf(xb.x, r, acc[4]);
+    acc[5] = fmaf(xb.y, r, acc[5]);
+    acc[6] = fmaf(xb.z, r, acc[6]);
+    acc[7] = fmaf(xb.w, r, acc[7]);
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int t = t0 + t_lane + 4 * i;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const int e = e_lane + 64 * c;
-      if (t < T && e < E) logits[(int64_t)t * E + e] = acc[i][c];
-    }
+  for (int i = 0; i < kRouterTok; ++i) red[(warp * kRouterTok + i) * 32 + lane] = acc[i];
+  __syncthreads();
+  if (threadIdx.x < kRouterTok * 32) {
+    const int tt = threadIdx.x >> 5, l = threadIdx.x & 31;
+    float v = 0.0f;
+    for (int w = 0; w < kRouterWarps; ++w) v += red[(w * kRouterTok + tt) * 32 + l];
+    const int t = t0 + tt, ee = e0 + l;
+    if (t < T && ee < E) logits[(int64_t)t * E + ee] = v;
   }
 }
 
@@ -112,11 +106,16 @@ __global__ void router_topk_kernel(const float *__restrict__ logits, int T, int 
 #pragma unroll
   for (int i = 0; i < 8; ++i) p[i] = p[i] / sum;
 
+  // NaN probabilities rank below every number (and are still selectable, so
+  // k valid ids are always produced); taken experts are marked -inf.
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    if (p[i] != p[i]) p[i] = -1.0e30f;
   float wsum = 0.0f, wsel = 0.0f;
   int id_sel = 0;
   for (int j = 0; j < k; ++j) {
     // Best of this lane (lowest expert index among equals), then across lanes.
-    float bv = -1.0f;
+    float bv = -INFINITY;
     int bi = 0x7fffffff;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -138,11 +137,12 @@ __global__ void router_topk_kernel(const float *__restrict__ logits, int T, int 
     if ((bi & 31) == lane) {
 #pragma unroll
       for (int i = 0; i < 8; ++i)
-        if (lane + 32 * i == bi) p[i] = -2.0f;  // taken
+        if (lane + 32 * i == bi) p[i] = -INFINITY;  // taken
     }
-    wsum += bv;
+    const float wv = bv < -1.0e29f ? __int_as_float(0x7fc00000) : bv;  // NaN stays NaN
+    wsum += wv;
     if (lane == j) {
-      wsel = bv;
+      wsel = wv;
       id_sel = bi;
     }
   }
@@ -156,8 +156,14 @@ cudaError_t launch_router(const uint16_t *x, const float *router, float *logits,
                           int E, int k, int renormalize, int32_t *ids, float *w,
                           cudaStream_t st) {
   if (T == 0) return cudaSuccess;
-  router_logits_kernel<<<(T + kRouterTok - 1) / kRouterTok, 256, 0, st>>>(x, router, logits, T,
-                                                                          H, E);
+  const size_t smem = sizeof(float) * ((size_t)H * kRouterTok + kRouterWarps * kRouterTok * 32);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(router_logits_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  dim3 grid((E + 31) / 32, (T + kRouterTok - 1) / kRouterTok);
+  router_logits_kernel<<<grid, 32 * kRouterWarps, smem, st>>>(x, router, logits, T, H, E);
   router_topk_kernel<<<(T * 32 + 255) / 256, 256, 0, st>>>(logits, T, E, k, renormalize, ids, w);
   return cudaGetLastError();
 }
@@ -235,6 +241,100 @@ cudaError_t launch_slot_token(int32_t *idx, int R, int k, cudaStream_t st) {
 }
 
 // ---------------------------------------------------------------------------
+// Expert-parallel dispatch plan.  Slot r (= token r / k, choice r % k) goes to
+// rank dst = id / experts_per_rank as local expert id % experts_per_rank.
+// Output: per-rank counts, the send order (slots grouped by destination rank,
+// in slot order within a rank: a stable counting sort) as token index and
+// local expert id per send position, and slot_pos[r] = send position of slot r
+// (so the returned expert outputs can be combined in slot order).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) ep_plan_kernel(const int32_t *__restrict__ ids, int R,
+                                                      int k, int epr, int world,
+                                                      int32_t *__restrict__ counts,
+                                                      int32_t *__restrict__ send_token,
+                                                      int32_t *__restrict__ send_expert,
+                                                      int32_t *__restrict__ slot_pos) {
+  __shared__ int cnt[64], off[64];
+  __shared__ int chunk_cnt[32][64];  // per-warp counts of the current chunk
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid < 64) cnt[tid] = 0;
+  __syncthreads();
+  for (int r = tid; r < R; r += blockDim.x) {
+    const int d = ids[r] / epr;
+    if (d >= 0 && d < world) atomicAdd(&cnt[d], 1);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int acc = 0;
+    for (int d = 0; d < world; ++d) {
+      off[d] = acc;
+      counts[d] = cnt[d];
+      acc += cnt[d];
+    }
+  }
+  __syncthreads();
+  // Stable placement, one 1024-slot chunk at a time: rank of the slot among
+  // same-destination slots = (earlier warps' counts) + (earlier lanes' count).
+  for (int base = 0; base < R; base += blockDim.x) {
+    const int r = base + tid;
+    const int id = r < R ? ids[r] : -1;
+    const int d = (id >= 0) ? id / epr : -1;
+    const bool ok = d >= 0 && d < world;
+    int mine = 0, before = 0;
+    for (int dd = 0; dd < world; ++dd) {
+      const unsigned m = __ballot_sync(0xffffffffu, ok && d == dd);
+      if (lane == 0) chunk_cnt[warp][dd] = __popc(m);
+      if (ok && d == dd) before = __popc(m & ((1u << lane) - 1u));
+    }
+    __syncthreads();
+    if (ok) {
+      mine = 0;
+      for (int w = 0; w < warp; ++w) mine += chunk_cnt[w][d];
+      const int p = off[d] + mine + before;
+      send_token[p] = r / k;
+      send_expert[p] = id % epr;
+      slot_pos[r] = p;
+    } else if (r < R) {
+      slot_pos[r] = -1;  // expert id outside [0, world * epr): not dispatched
+    }
+    __syncthreads();
+    if (tid < world) {
+      int tot = 0;
+      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) tot += chunk_cnt[w][tid];
+      off[tid] += tot;
+    }
+    __syncthreads();
+  }
+}
+
+cudaError_t launch_ep_plan(const int32_t *ids, int R, int k, int epr, int world, int32_t *counts,
+                           int32_t *send_token, int32_t *send_expert, int32_t *slot_pos,
+                           cudaStream_t st) {
+  ep_plan_kernel<<<1, 1024, 0, st>>>(ids, R, k, epr, world, counts, send_token, send_expert,
+                                     slot_pos);
+  return cudaGetLastError();
+}
+
+// dst[i, :] = src[idx[i], :] for rows of `bytes` bytes (16-byte vectors).
+__global__ void gather_rows_kernel(const uint4 *__restrict__ src, const int32_t *__restrict__ idx,
+                                   int64_t n, int vec, uint4 *__restrict__ dst) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= n * vec) return;
+  const int64_t row = i / vec, v = i % vec;
+  dst[i] = src[(int64_t)idx[row] * vec + v];
+}
+
+cudaError_t launch_gather_rows(const void *src, const int32_t *idx, int64_t n, int64_t row_bytes,
+                               void *dst, cudaStream_t st) {
+  const int vec = (int)(row_bytes / 16);
+  const int64_t total = n * vec;
+  if (total == 0) return cudaSuccess;
+  gather_rows_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
+      static_cast<const uint4 *>(src), idx, n, vec, static_cast<uint4 *>(dst));
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
 // Combine: y[t, :] = sum_j w[t, j] * ys[t*k + j, :] (+ residual[t, :]), fp32
 // sums in j order, residual added last, one bf16 rounding at the end.  Slot
 // outputs are fp32 (or bf16).  8 features per thread.
@@ -262,7 +362,8 @@ __device__ __forceinline__ void load8<uint16_t>(const uint16_t *p, float (&v)[8]
 template <typename SlotT, typename OutT>
 __global__ void moe_combine_kernel(const SlotT *__restrict__ ys, const float *__restrict__ w,
                                    const uint16_t *__restrict__ residual,
-                                   OutT *__restrict__ y, int T, int k, int H) {
+                                   const int32_t *__restrict__ slot_pos, OutT *__restrict__ y,
+                                   int T, int k, int H) {
   const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;  // vector index
   const int hv = H / 8;
   if (i >= (int64_t)T * hv) return;
@@ -272,8 +373,10 @@ __global__ void moe_combine_kernel(const SlotT *__restrict__ ys, const float *__
   for (int q = 0; q < 8; ++q) s[q] = 0.0f;
   for (int j = 0; j < k; ++j) {
     const float wj = w[(int64_t)t * k + j];
+    const int64_t row = slot_pos ? slot_pos[(int64_t)t * k + j] : (int64_t)t * k + j;
+    if (row < 0) continue;  // slot that was not dispatched contributes nothing
     float v[8];
-    load8<SlotT>(ys + ((int64_t)t * k + j) * H + 8 * h8, v);
+    load8<SlotT>(ys + row * H + 8 * h8, v);
 #pragma unroll
     for (int q = 0; q < 8; ++q) s[q] = fmaf(wj, v[q], s[q]);
   }
@@ -296,21 +399,21 @@ __global__ void moe_combine_kernel(const SlotT *__restrict__ ys, const float *__
 }
 
 cudaError_t launch_moe_combine(const void *ys, int ys_dtype, const float *w,
-                               const uint16_t *residual, void *y, int y_dtype, int T, int k, int H,
-                               cudaStream_t st) {
+                               const uint16_t *residual, const int32_t *slot_pos, void *y,
+                               int y_dtype, int T, int k, int H, cudaStream_t st) {
   const int64_t n = (int64_t)T * (H / 8);
   if (n == 0) return cudaSuccess;
   const unsigned blocks = (unsigned)((n + 255) / 256);
   const float *yf = static_cast<const float *>(ys);
   const uint16_t *yb = static_cast<const uint16_t *>(ys);
   if (ys_dtype == kF32 && y_dtype == kF32)
-    moe_combine_kernel<float, float><<<blocks, 256, 0, st>>>(yf, w, residual, static_cast<float *>(y), T, k, H);
+    moe_combine_kernel<float, float><<<blocks, 256, 0, st>>>(yf, w, residual, slot_pos, static_cast<float *>(y), T, k, H);
   else if (ys_dtype == kF32)
-    moe_combine_kernel<float, uint16_t><<<blocks, 256, 0, st>>>(yf, w, residual, static_cast<uint16_t *>(y), T, k, H);
+    moe_combine_kernel<float, uint16_t><<<blocks, 256, 0, st>>>(yf, w, residual, slot_pos, static_cast<uint16_t *>(y), T, k, H);
   else if (y_dtype == kF32)
-    moe_combine_kernel<uint16_t, float><<<blocks, 256, 0, st>>>(yb, w, residual, static_cast<float *>(y), T, k, H);
+    moe_combine_kernel<uint16_t, float><<<blocks, 256, 0, st>>>(yb, w, residual, slot_pos, static_cast<float *>(y), T, k, H);
   else
-    moe_combine_kernel<uint16_t, uint16_t><<<blocks, 256, 0, st>>>(yb, w, residual, static_cast<uint16_t *>(y), T, k, H);
+    moe_combine_kernel<uint16_t, uint16_t><<<blocks, 256, 0, st>>>(yb, w, residual, slot_pos, static_cast<uint16_t *>(y), T, k, H);
   return cudaGetLastError();
 }
 

@@ -80,15 +80,17 @@ int check_desc(const nvfp4_moe_desc *d) {
     return fail(NVFP4_ERR_INVALID_ARG, "top_k must be in [1, min(32, num_experts)]");
   if (d->hidden <= 0 || d->hidden % 128 || d->intermediate <= 0 || d->intermediate % 128)
     return fail(NVFP4_ERR_INVALID_ARG, "hidden and intermediate must be positive multiples of 128");
+  if (d->hidden > 6144)
+    return fail(NVFP4_ERR_INVALID_ARG, "hidden > 6144 exceeds the router's shared-memory tile");
   return NVFP4_OK;
 }
 
 int check_weights(const nvfp4_moe_weights *w) {
   if (!w || !w->gate_up || !w->gate_up_scale || !w->down || !w->down_scale)
     return fail(NVFP4_ERR_INVALID_ARG, "null expert weight pointer");
-  if (!aligned(w->gate_up, 16) || !aligned(w->down, 16) || !aligned(w->gate_up_scale, 2) ||
-      !aligned(w->down_scale, 2))
-    return fail(NVFP4_ERR_INVALID_ARG, "expert weights must be 16-byte (scales 2-byte) aligned");
+  if (!aligned(w->gate_up, 16) || !aligned(w->down, 16) || !aligned(w->gate_up_scale, 4) ||
+      !aligned(w->down_scale, 4))
+    return fail(NVFP4_ERR_INVALID_ARG, "expert weights must be 16-byte (scales 4-byte) aligned");
   return NVFP4_OK;
 }
 
@@ -216,8 +218,8 @@ extern "C" int nvfp4_moe_experts(const nvfp4_moe_desc *d, const nvfp4_moe_weight
 }
 
 extern "C" int nvfp4_moe_combine(const void *y_slots, int slot_dtype, const float *topk_w,
-                                 const void *residual, void *y, int y_dtype, int64_t T, int32_t k,
-                                 int32_t H, void *stream) {
+                                 const int32_t *slot_pos, const void *residual, void *y,
+                                 int y_dtype, int64_t T, int32_t k, int32_t H, void *stream) {
   if (T < 0 || k <= 0 || H <= 0 || H % 8) return fail(NVFP4_ERR_INVALID_ARG, "bad combine shape");
   if ((slot_dtype != NVFP4_DTYPE_F32 && slot_dtype != NVFP4_DTYPE_BF16) ||
       (y_dtype != NVFP4_DTYPE_F32 && y_dtype != NVFP4_DTYPE_BF16))
@@ -227,9 +229,36 @@ extern "C" int nvfp4_moe_combine(const void *y_slots, int slot_dtype, const floa
   if (!aligned(y_slots, 16) || !aligned(y, 16) || (residual && !aligned(residual, 16)))
     return fail(NVFP4_ERR_INVALID_ARG, "combine buffers must be 16-byte aligned");
   return check_launch(launch_moe_combine(y_slots, slot_dtype, topk_w,
-                                         static_cast<const uint16_t *>(residual), y, y_dtype,
-                                         (int)T, k, H, static_cast<cudaStream_t>(stream)),
+                                         static_cast<const uint16_t *>(residual), slot_pos, y,
+                                         y_dtype, (int)T, k, H, static_cast<cudaStream_t>(stream)),
                       "combine launch");
+}
+
+extern "C" int nvfp4_ep_dispatch_plan(const int32_t *topk_ids, int64_t T, int32_t k,
+                                      int32_t experts_per_rank, int32_t world,
+                                      int32_t *send_counts, int32_t *send_token,
+                                      int32_t *send_expert, int32_t *slot_pos, void *stream) {
+  if (T < 0 || k <= 0 || k > 32 || experts_per_rank <= 0 || world <= 0 || world > 64 ||
+      T * k > (1 << 24))
+    return fail(NVFP4_ERR_INVALID_ARG, "bad dispatch-plan shape");
+  if (!topk_ids || !send_counts || !send_token || !send_expert || !slot_pos)
+    return fail(NVFP4_ERR_INVALID_ARG, "null dispatch-plan pointer");
+  return check_launch(launch_ep_plan(topk_ids, (int)(T * k), k, experts_per_rank, world,
+                                     send_counts, send_token, send_expert, slot_pos,
+                                     static_cast<cudaStream_t>(stream)),
+                      "dispatch plan launch");
+}
+
+extern "C" int nvfp4_gather_rows(const void *src, const int32_t *row_index, int64_t n,
+                                 int64_t row_bytes, void *dst, void *stream) {
+  if (n < 0 || row_bytes <= 0 || row_bytes % 16) return fail(NVFP4_ERR_INVALID_ARG, "bad gather shape");
+  if (n == 0) return NVFP4_OK;
+  if (!src || !row_index || !dst) return fail(NVFP4_ERR_INVALID_ARG, "null gather pointer");
+  if (!aligned(src, 16) || !aligned(dst, 16))
+    return fail(NVFP4_ERR_INVALID_ARG, "gather buffers must be 16-byte aligned");
+  return check_launch(launch_gather_rows(src, row_index, n, row_bytes, dst,
+                                         static_cast<cudaStream_t>(stream)),
+                      "gather launch");
 }
 
 extern "C" int nvfp4_moe_forward(const nvfp4_moe_desc *d, const nvfp4_moe_weights *w,
@@ -270,6 +299,6 @@ extern "C" int nvfp4_moe_forward(const nvfp4_moe_desc *d, const nvfp4_moe_weight
                    base + L.experts, st);
   if (rc) return rc;
   return check_launch(launch_moe_combine(y_slot, kF32, tw, static_cast<const uint16_t *>(residual),
-                                         y, y_dtype, (int)T, d->top_k, d->hidden, st),
+                                         nullptr, y, y_dtype, (int)T, d->top_k, d->hidden, st),
                       "combine launch");
 }

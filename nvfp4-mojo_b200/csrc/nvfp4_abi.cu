@@ -50,8 +50,10 @@ static int run_linear(const WeightSpec &ws, const AlphaSpec &al, const void *x, 
   if (M > INT32_MAX / 2) return fail(NVFP4_ERR_INVALID_ARG, "too many tokens: %lld", (long long)M);
   const bool token_major = (xs_k == 1 && ys_n == 1);
   const bool force_f32 = flags & NVFP4_FLAG_FORCE_F32;
-  const bool skinny_ok = token_major && x_dt == kBF16 && (ws.K % 32) == 0 &&
-                         aligned(ws.w, 16) && aligned(ws.sf, 2) && aligned(x, 16) &&
+  // Decode GEMV: 16-byte code chunks and 4-byte scale words stream through
+  // cp.async, hence K % 64 (scale rows of whole 4-byte words) and alignment.
+  const bool skinny_ok = token_major && x_dt == kBF16 && (ws.K % 64) == 0 &&
+                         aligned(ws.w, 16) && aligned(ws.sf, 4) && aligned(x, 16) &&
                          (xs_m % 8) == 0;
   const bool tc_ok = token_major && x_dt == kBF16 && !force_f32 &&
                      tc_gemm_supported(ws.K, ws.w, x, xs_m);
@@ -78,7 +80,7 @@ static int run_linear(const WeightSpec &ws, const AlphaSpec &al, const void *x, 
   }
   if ((flags & NVFP4_FLAG_FORCE_SKINNY) && !skinny_ok)
     return fail(NVFP4_ERR_UNSUPPORTED,
-                "decode GEMV path needs bf16 token-major activations, K %% 32 == 0 and "
+                "decode GEMV path needs bf16 token-major activations, K %% 64 == 0 and "
                 "16-byte aligned weights/activations");
   return check_launch(
       launch_linear_f32(ws, al, x, x_dt, xs_m, xs_k, y, y_dt, ys_m, ys_n, (int)M, st),

@@ -99,8 +99,11 @@ SIGNATURES = {
     "nvfp4_moe_route": (_int, [ctypes.POINTER(MoEDesc), _vp, _vp, _i64, _vp, _vp, _vp, _vp]),
     "nvfp4_moe_experts": (_int, [ctypes.POINTER(MoEDesc), ctypes.POINTER(MoEWeightPtrs), _vp, _vp,
                                  _vp, _i64, _vp, _int, _vp, ctypes.c_size_t, _vp]),
-    "nvfp4_moe_combine": (_int, [_vp, _int, _vp, _vp, _vp, _int, _i64, ctypes.c_int32,
+    "nvfp4_moe_combine": (_int, [_vp, _int, _vp, _vp, _vp, _vp, _int, _i64, ctypes.c_int32,
                                  ctypes.c_int32, _vp]),
+    "nvfp4_ep_dispatch_plan": (_int, [_vp, _i64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                      _vp, _vp, _vp, _vp, _vp]),
+    "nvfp4_gather_rows": (_int, [_vp, _vp, _i64, _i64, _vp, _vp]),
 }
 
 _lib = None

@@ -1,0 +1,128 @@
+"""Expert-parallel NVFP4 MoE layer over NCCL (torch.distributed).
+
+One process per GPU; rank r of a world of G owns experts
+[r * E/G, (r+1) * E/G) (their stacked NVFP4 weights) and a replica of the
+fp32 router.  Per layer, on every rank:
+
+  1. route its own tokens (softmax top-k over all E experts);
+  2. plan the dispatch on the device: slots grouped by destination rank;
+  3. exchange per-rank slot counts (all-to-all, 4 bytes per peer);
+  4. gather the token rows in send order and exchange them with the local
+     expert ids (all-to-all over NVLink);
+  5. run the local experts on the received rows (grouped NVFP4 GEMMs);
+  6. return the fp32 expert outputs (reverse all-to-all);
+  7. combine them in slot order with the routing weights (+ residual).
+
+Steps 1, 2, 4 (gather), 5 and 7 are libnvfp4 CUDA kernels; steps 3, 4 and 6
+are NCCL collectives.  The kernel calls go through a backend object so the
+exchange logic can be exercised with CPU ranks (gloo) in tests.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+from .moe import MoEWeights, make_desc, moe_combine, moe_experts, moe_route, _ptr
+from .nvfp4_gemm_gpu import _stream
+
+
+class CudaBackend:
+    """The libnvfp4 kernels (the product path)."""
+
+    def __init__(self, local: MoEWeights, router: torch.Tensor, top_k: int, renormalize=True):
+        self.local = local
+        self.router_w = MoEWeights(router, local.gate_up, local.gate_up_scale,
+                                   local.gate_up_scale_2, local.down, local.down_scale,
+                                   local.down_scale_2)
+        self.E_total = router.shape[1]
+        self.top_k = top_k
+        self.renormalize = renormalize
+        self._ws = None
+
+    def route(self, x):
+        desc = _lib.MoEDesc(self.E_total, self.top_k, self.local.hidden, self.local.intermediate,
+                            int(self.renormalize))
+        T = x.shape[0]
+        ids = torch.empty((T, self.top_k), dtype=torch.int32, device=x.device)
+        tw = torch.empty((T, self.top_k), dtype=torch.float32, device=x.device)
+        logits = torch.empty((T, self.E_total), dtype=torch.float32, device=x.device)
+        import ctypes
+        rc = _lib.load().nvfp4_moe_route(ctypes.byref(desc), _ptr(self.router_w.router), _ptr(x),
+                                         T, _ptr(ids), _ptr(tw), _ptr(logits), _stream(None))
+        _lib.check(rc)
+        return ids, tw
+
+    def plan(self, ids, epr, world):
+        T, k = ids.shape
+        R = T * k
+        dev = ids.device
+        counts = torch.empty(world, dtype=torch.int32, device=dev)
+        send_token = torch.empty(R, dtype=torch.int32, device=dev)
+        send_expert = torch.empty(R, dtype=torch.int32, device=dev)
+        slot_pos = torch.empty(R, dtype=torch.int32, device=dev)
+        rc = _lib.load().nvfp4_ep_dispatch_plan(_ptr(ids), T, k, epr, world, _ptr(counts),
+                                                _ptr(send_token), _ptr(send_expert),
+                                                _ptr(slot_pos), _stream(None))
+        _lib.check(rc)
+        return counts, send_token, send_expert, slot_pos
+
+    def gather(self, x, idx):
+        out = torch.empty((idx.numel(), x.shape[1]), dtype=x.dtype, device=x.device)
+        rc = _lib.load().nvfp4_gather_rows(_ptr(x), _ptr(idx), idx.numel(),
+                                           x.shape[1] * x.element_size(), _ptr(out), _stream(None))
+        _lib.check(rc)
+        return out
+
+    def experts(self, rows, local_ids):
+        return moe_experts(self.local, rows, local_ids, top_k=self.top_k, out_dtype=torch.float32)
+
+    def combine(self, y_send, tw, slot_pos, residual):
+        return moe_combine(y_send, tw, residual=residual, slot_pos=slot_pos)
+
+
+class EPMoELayer:
+    """Expert-parallel MoE layer; `backend` defaults to the CUDA kernels."""
+
+    def __init__(self, local: Optional[MoEWeights], router: torch.Tensor, top_k: int = 8,
+                 num_experts: Optional[int] = None, group=None, backend=None,
+                 renormalize: bool = True):
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.E = num_experts if num_experts is not None else router.shape[1]
+        if self.E % self.world:
+            raise ValueError("num_experts must be divisible by the world size")
+        self.epr = self.E // self.world
+        self.top_k = top_k
+        self.backend = backend or CudaBackend(local, router, top_k, renormalize)
+
+    def _a2a(self, out, inp, out_splits, in_splits):
+        if self.world == 1:
+            out.copy_(inp)
+            return
+        dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
+
+    def forward(self, x: torch.Tensor, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+        be = self.backend
+        ids, tw = be.route(x)
+        counts, send_token, send_expert, slot_pos = be.plan(ids, self.epr, self.world)
+        recv_counts = torch.empty_like(counts)
+        self._a2a(recv_counts, counts, None, None)
+        send_sizes = counts.tolist()
+        recv_sizes = recv_counts.tolist()
+        n_recv = sum(recv_sizes)
+        n_send = sum(send_sizes)  # slots with a valid expert id
+        send_token, send_expert = send_token[:n_send], send_expert[:n_send]
+        send_x = be.gather(x, send_token)
+        recv_x = torch.empty((n_recv, x.shape[1]), dtype=x.dtype, device=x.device)
+        recv_e = torch.empty(n_recv, dtype=torch.int32, device=x.device)
+        self._a2a(recv_x, send_x, recv_sizes, send_sizes)
+        self._a2a(recv_e, send_expert, recv_sizes, send_sizes)
+        y_recv = be.experts(recv_x, recv_e)
+        y_send = torch.empty((send_x.shape[0], x.shape[1]), dtype=y_recv.dtype, device=x.device)
+        self._a2a(y_send, y_recv, send_sizes, recv_sizes)
+        return be.combine(y_send, tw, slot_pos, residual)
+
+    __call__ = forward

@@ -178,13 +178,14 @@ def moe_experts(weights: MoEWeights, x: torch.Tensor, row_expert: torch.Tensor,
 
 
 def moe_combine(y_slots: torch.Tensor, topk_w: torch.Tensor, residual=None, out=None,
-                stream=None) -> torch.Tensor:
+                slot_pos: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
     T, k = topk_w.shape
     H = y_slots.shape[-1]
     y = out if out is not None else torch.empty((T, H), dtype=torch.bfloat16,
                                                 device=y_slots.device)
     dts = {torch.float32: _lib.DTYPE_F32, torch.bfloat16: _lib.DTYPE_BF16}
-    rc = _sig().nvfp4_moe_combine(_ptr(y_slots), dts[y_slots.dtype], _ptr(topk_w), _ptr(residual),
-                                  _ptr(y), dts[y.dtype], T, k, H, _stream(stream))
+    rc = _sig().nvfp4_moe_combine(_ptr(y_slots), dts[y_slots.dtype], _ptr(topk_w),
+                                  _ptr(slot_pos), _ptr(residual), _ptr(y), dts[y.dtype], T, k, H,
+                                  _stream(stream))
     _lib.check(rc)
     return y

@@ -128,11 +128,12 @@ def test_decode_gemv_sweep(O, cuda, K, N, M):
 
 @pytest.mark.parametrize("M", [3, 13, 17, 33, 64])
 def test_skinny_ragged_shapes(O, cuda, M):
-    """N not a multiple of 16, K = 32 * odd, several token items."""
+    """N not a multiple of 16, K % 128 == 64 (a partial last round), several
+    token items."""
     import nvfp4
     from nvfp4 import synthetic
 
-    N, K = 100, 96 * 3
+    N, K = 100, 64 * 5
     wd = synthetic.linear_weights(N, K, seed=M)
     x = synthetic.bf16_round(synthetic.activations(M, K, seed=M + 1))
     lin = nvfp4.NvFp4Linear(K, N, input_scale=1.5, weight_scale_2=0.01)
@@ -144,7 +145,7 @@ def test_skinny_ragged_shapes(O, cuda, M):
 
 
 def test_fp32_path_odd_k(O, cuda):
-    """K % 32 == 16 goes to the CUDA-core fp32 path (any K multiple of 16)."""
+    """K % 64 != 0 goes to the CUDA-core fp32 path (any K multiple of 16)."""
     import nvfp4
     from nvfp4 import synthetic
 
