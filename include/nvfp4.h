@@ -189,6 +189,27 @@ int nvfp4_moe_forward(const nvfp4_moe_desc *desc, const nvfp4_moe_weights *weigh
                       int32_t *topk_ids, float *topk_w, void *workspace,
                       size_t workspace_bytes, void *stream);
 
+/*
+ * No counterpart in the reference.  nvfp4_moe_forward for callers that cannot
+ * allocate device memory: a caller with no device allocator of its own (such
+ * as foreign-function host code that only holds the pointers it was given) or
+ * a serving loop that must not call cudaMalloc once it runs (it synchronises
+ * the device and is not allowed during stream capture).  The workspace is a
+ * static device array of NVFP4_NOALLOC_SCRATCH_BYTES inside the library,
+ * which every GPU that loads the library holds until the process exits; the
+ * call allocates nothing.  Layers whose workspace would exceed it
+ * (nvfp4_moe_workspace_size(desc, T) > NVFP4_NOALLOC_SCRATCH_BYTES) are
+ * rejected with NVFP4_ERR_WORKSPACE.  The first call on each device looks up
+ * the array's device address (with that device current): make it before any
+ * stream capture.  All calls on a device share the array, so calls that
+ * overlap on the GPU race and must be serialised by the caller; nothing in it
+ * has to start at zero.  Arguments as nvfp4_moe_forward, minus the workspace.
+ */
+#define NVFP4_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+int nvfp4_moe_forward_noalloc(const nvfp4_moe_desc *desc, const nvfp4_moe_weights *weights,
+                              const void *x, const void *residual, void *y, int y_dtype,
+                              int64_t T, int32_t *topk_ids, float *topk_w, void *stream);
+
 /* Router alone: topk_ids int32 [T, k], topk_w fp32 [T, k]; logits fp32
  * [T, E] is caller memory the router writes (and the caller may read). */
 int nvfp4_moe_route(const nvfp4_moe_desc *desc, const float *router, const void *x, int64_t T,
