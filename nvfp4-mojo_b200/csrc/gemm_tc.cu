@@ -298,9 +298,9 @@ static EncodeTiledFn encode_fn() {
 }
 
 // 2-D row-major tensor map: rows x cols elements, box box_rows x box_cols.
-static bool make_map(CUtensorMap *m, CUtensorMapDataType dt, int esize, const void *base,
-                     int64_t rows, int64_t cols, int64_t ld_elems, int box_cols, int box_rows,
-                     CUtensorMapSwizzle sw) {
+bool make_tmap_2d(CUtensorMap *m, CUtensorMapDataType dt, int esize, const void *base,
+                  int64_t rows, int64_t cols, int64_t ld_elems, int box_cols, int box_rows,
+                  CUtensorMapSwizzle sw) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
@@ -318,7 +318,7 @@ bool tc_gemm_supported(int K, const void *w, const void *x, int64_t x_ld) {
          (x_ld % 8) == 0 && encode_fn() != nullptr;
 }
 
-static int sm_count() {
+int tc_sm_count() {
   static int n = 0;
   if (!n) {
     int dev = 0;
@@ -335,11 +335,11 @@ static cudaError_t launch_tc_bn(const WeightSpec &ws, const AlphaSpec &al, const
                                 cudaStream_t st) {
   using L = TcSmem<BN>;
   CUtensorMap tmX, tmW, tmS;
-  if (!make_map(&tmX, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, M, ws.K, x_ld, kTcBK, BN,
+  if (!make_tmap_2d(&tmX, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, M, ws.K, x_ld, kTcBK, BN,
                 CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ws.w, ws.N, ws.K / 2, ws.K / 2,
+      !make_tmap_2d(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ws.w, ws.N, ws.K / 2, ws.K / 2,
                 kTcBK / 2, kTcBM, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-      !make_map(&tmS, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ws.sf, ws.N, ws.K / 16, ws.K / 16, 16,
+      !make_tmap_2d(&tmS, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ws.sf, ws.N, ws.K / 16, ws.K / 16, 16,
                 kTcBM, CU_TENSOR_MAP_SWIZZLE_NONE))
     return cudaErrorInvalidValue;
   static bool attr = false;
@@ -358,7 +358,7 @@ static cudaError_t launch_tc_bn(const WeightSpec &ws, const AlphaSpec &al, const
   a.y_dtype = y_dtype;
   a.y_ld = y_ld;
   const int tiles = ((ws.N + kTcBM - 1) / kTcBM) * ((M + BN - 1) / BN);
-  const int grid = tiles < sm_count() ? tiles : sm_count();
+  const int grid = tiles < tc_sm_count() ? tiles : tc_sm_count();
   w4a16_tc_kernel<BN><<<grid, kTcThreads, L::alloc, st>>>(tmX, tmW, tmS, a);
   return cudaGetLastError();
 }
@@ -368,7 +368,7 @@ cudaError_t launch_w4a16_tc(const WeightSpec &ws, const AlphaSpec &al, const uin
                             cudaStream_t st) {
   // Smaller token tiles when 256-token tiles would leave SMs idle.
   const int tiles256 = ((ws.N + kTcBM - 1) / kTcBM) * ((M + 255) / 256);
-  if (tiles256 < 4 * sm_count())
+  if (tiles256 < 4 * tc_sm_count())
     return launch_tc_bn<128>(ws, al, x, x_ld, y, y_dtype, y_ld, M, st);
   return launch_tc_bn<256>(ws, al, x, x_ld, y, y_dtype, y_ld, M, st);
 }

@@ -220,6 +220,12 @@ __global__ void __launch_bounds__(1024) moe_permute_kernel(const int32_t *__rest
       plan.dst_row[p] = r;
     }
   }
+  // Positions past the valid rows (ids outside [0, E)) stay in bounds for a
+  // whole-array gather and belong to no work item.
+  for (int p = off[E] + tid; p < R; p += blockDim.x) {
+    plan.src_row[p] = 0;
+    plan.dst_row[p] = -1;
+  }
 }
 
 cudaError_t launch_moe_permute(const int32_t *row_expert, const int32_t *x_row_index, int R,

@@ -20,6 +20,27 @@ struct MoePlan {
   int32_t *dst_row;  // [R]
 };
 
+// Grouped tensor-core expert GEMM (moe_tc.cu).
+struct MoeTcLaunch {
+  const uint8_t *w = nullptr;   // stacked expert codes [E * Nw, K/2]
+  const uint8_t *sf = nullptr;  // [E * Nw, K/16]
+  int E = 0, Nw = 0, K = 0;
+  const uint16_t *b0 = nullptr;  // activations in sorted-row order [R, K] (bf16)
+  const uint16_t *b1 = nullptr;  // low parts (down projection) or null
+  int64_t R = 0;
+  const SkinnyWork *work = nullptr;
+  const int *n_work = nullptr;
+  AlphaSpec al;                 // ws2_rows with stride Nw per expert
+  uint16_t *inter = nullptr, *inter_lo = nullptr;  // gate_up outputs [R, Nw/2]
+  void *y = nullptr;            // down output rows (scattered by dst_row)
+  int y_dtype = kF32;
+  const int32_t *dst_row = nullptr;
+  int y_ld = 0;
+};
+cudaError_t launch_moe_tc(const MoeTcLaunch &L, bool gate_up, cudaStream_t st);
+bool moe_tc_supported(int H, int I);
+int moe_tc_rows_per_item();
+
 cudaError_t launch_router(const uint16_t *x, const float *router, float *logits, int T, int H,
                           int E, int k, int renormalize, int32_t *ids, float *w, cudaStream_t st);
 cudaError_t launch_moe_permute(const int32_t *row_expert, const int32_t *x_row_index, int R, int E,

@@ -12,21 +12,28 @@ constexpr size_t kAlign = 256;
 
 size_t up(size_t v) { return (v + kAlign - 1) & ~(kAlign - 1); }
 
-// Token slots per grouped-GEMM work item, from the mean rows per expert.
-int choose_tpi(int64_t R, int E) {
-  const int64_t avg = (R + E - 1) / E;
+// Grouped-GEMM path: tcgen05 tiles when experts get many rows on average
+// (prefill), the register-decode skinny kernel otherwise (decode).
+bool use_tc(const nvfp4_moe_desc &d, int64_t R) {
+  return R >= 64LL * d.num_experts && moe_tc_supported(d.hidden, d.intermediate);
+}
+
+// Rows per grouped-GEMM work item.
+int choose_tpi(const nvfp4_moe_desc &d, int64_t R) {
+  if (use_tc(d, R)) return moe_tc_rows_per_item();
+  const int64_t avg = (R + d.num_experts - 1) / d.num_experts;
   return avg <= 8 ? 8 : (avg <= 16 ? 16 : 32);
 }
 
 int64_t work_capacity(int64_t R, int E, int tpi) { return (R + tpi - 1) / tpi + E; }
 
 struct ExpertsLayout {
-  size_t offsets, n_work, n_rows, work, src_row, dst_row, inter, inter_lo, total;
+  size_t offsets, n_work, n_rows, work, src_row, dst_row, inter, inter_lo, x_perm, total;
 };
 
 ExpertsLayout experts_layout(const nvfp4_moe_desc &d, int64_t R) {
   ExpertsLayout L;
-  const int tpi = choose_tpi(R, d.num_experts);
+  const int tpi = choose_tpi(d, R);
   size_t o = 0;
   L.offsets = o;
   o = up(o + sizeof(int32_t) * (d.num_experts + 1));
@@ -44,6 +51,8 @@ ExpertsLayout experts_layout(const nvfp4_moe_desc &d, int64_t R) {
   o = up(o + sizeof(uint16_t) * R * d.intermediate);
   L.inter_lo = o;
   o = up(o + sizeof(uint16_t) * R * d.intermediate);
+  L.x_perm = o;  // tensor-core path: activation rows gathered in sorted order
+  if (use_tc(d, R)) o = up(o + sizeof(uint16_t) * R * d.hidden);
   L.total = o;
   return L;
 }
@@ -100,7 +109,7 @@ int run_experts(const nvfp4_moe_desc &d, const nvfp4_moe_weights &w, const uint1
   if (R == 0) return NVFP4_OK;
   const ExpertsLayout L = experts_layout(d, R);
   const int E = d.num_experts, H = d.hidden, I = d.intermediate;
-  const int tpi = choose_tpi(R, E);
+  const int tpi = choose_tpi(d, R);
   MoePlan plan;
   plan.offsets = reinterpret_cast<int32_t *>(ws + L.offsets);
   plan.n_work = reinterpret_cast<int32_t *>(ws + L.n_work);
@@ -116,6 +125,47 @@ int run_experts(const nvfp4_moe_desc &d, const nvfp4_moe_weights &w, const uint1
   int rc = check_launch(launch_moe_permute(row_expert, x_row_index, (int)R, E, tpi, plan, st),
                         "MoE permutation launch");
   if (rc) return rc;
+
+  if (use_tc(d, R)) {
+    uint16_t *x_perm = reinterpret_cast<uint16_t *>(ws + L.x_perm);
+    rc = check_launch(launch_gather_rows(x, plan.src_row, R, (int64_t)H * 2, x_perm, st),
+                      "MoE activation gather launch");
+    if (rc) return rc;
+    MoeTcLaunch g;
+    g.w = w.gate_up;
+    g.sf = w.gate_up_scale;
+    g.E = E;
+    g.Nw = 2 * I;
+    g.K = H;
+    g.b0 = x_perm;
+    g.R = R;
+    g.work = plan.work;
+    g.n_work = plan.n_work;
+    g.al.input_scales = w.gate_up_input_scale;
+    g.al.ws2_rows = w.gate_up_scale_2;
+    g.inter = inter;
+    g.inter_lo = inter_lo;
+    rc = check_launch(launch_moe_tc(g, true, st), "MoE gate_up (tensor core) launch");
+    if (rc) return rc;
+    MoeTcLaunch dn;
+    dn.w = w.down;
+    dn.sf = w.down_scale;
+    dn.E = E;
+    dn.Nw = H;
+    dn.K = I;
+    dn.b0 = inter;
+    dn.b1 = inter_lo;
+    dn.R = R;
+    dn.work = plan.work;
+    dn.n_work = plan.n_work;
+    dn.al.input_scales = w.down_input_scale;
+    dn.al.ws2_rows = w.down_scale_2;
+    dn.y = y_rows;
+    dn.y_dtype = y_dtype;
+    dn.dst_row = plan.dst_row;
+    dn.y_ld = H;
+    return check_launch(launch_moe_tc(dn, false, st), "MoE down (tensor core) launch");
+  }
 
   SkinnyArgs gu;
   gu.ws.w = w.gate_up;

@@ -155,3 +155,19 @@ def test_workspace_too_small_is_an_error(cuda):
                                         None, None,
                                         ws.data_ptr(), ws.numel(), None)
     assert rc == _lib.NVFP4_ERR_WORKSPACE
+
+
+def test_moe_tensor_core_path_small(O, cuda):
+    """Many rows per expert (R >= 64 E) with H, I multiples of 256: the grouped
+    tcgen05 GEMMs (gate_up with two accumulators and fused SiLU*up, down on the
+    hi + lo activation parts), items of up to 128 rows, ragged last items."""
+    wd, x, w = setup(E=8, H=512, I=256, T=400, seed=31)
+    check_layer(O, wd, x, w, k=2)
+
+
+def test_moe_tensor_core_path_config3(O, cuda):
+    """Config-3 layer at T = 1024 (R = 8192 = 64 E: tensor-core path), sampled."""
+    T = 1024
+    wd, x, w = setup(E=128, H=2048, I=768, T=T, seed=33)
+    tok = np.sort(np.random.default_rng(34).choice(T, 64, replace=False))
+    check_layer(O, wd, x, w, k=8, tokens=tok)
