@@ -21,35 +21,42 @@
 namespace nvfp4 {
 
 // ---------------------------------------------------------------------------
-// Router: logits[t, e] = sum_h x[t, h] * router[h, e] (fp32 FMA).  A CTA owns
-// 32 experts x 8 tokens; its 8 warps split H, lane = expert (router rows are
-// expert-contiguous, so a warp reads 128 coalesced bytes per h), the 8
-// tokens' activations come from shared memory as fp32 [H][8]; partial sums of
-// the warps are added in a fixed order.
+// Router: logits[t, e] = sum_h x[t, h] * router[h, e].
+//
+// Few tokens (decode): CUDA-core fp32 FMA, split over H so that enough CTAs
+// run: CTA (32 experts, 8 tokens, H slice z) writes partial sums
+// part[z][t][e]; lane = expert (router rows are expert-contiguous: 128
+// coalesced bytes per h per warp), warps split the slice, their sums are added
+// in a fixed order.  The top-k kernel adds the slices in z order.
+// Many tokens (prefill): tensor cores, TF32 with the router split into
+// hi + lo TF32 parts (x is bf16, exact in TF32), two MMAs per k step, so the
+// logits carry fp32-level accuracy (~2^-21 relative residue of the split);
+// also split over H when the token tiles alone do not cover the GPU.
 // ---------------------------------------------------------------------------
 constexpr int kRouterTok = 8;
 constexpr int kRouterWarps = 8;
+constexpr int kRouterTcMinTokens = 256;
 
 __global__ void __launch_bounds__(32 * kRouterWarps)
     router_logits_kernel(const uint16_t *__restrict__ x, const float *__restrict__ router,
-                         float *__restrict__ logits, int T, int H, int E) {
-  extern __shared__ float4 rsm[];  // xs [H][8] fp32, then red [warps][8][32]
+                         float *__restrict__ part, int T, int H, int E, int hslice) {
+  extern __shared__ float4 rsm[];  // xs [hslice][8] fp32, then red [warps][8][32]
   float *xs = reinterpret_cast<float *>(rsm);
-  float *red = xs + (size_t)H * kRouterTok;
-  const int e0 = blockIdx.x * 32, t0 = blockIdx.y * kRouterTok;
+  float *red = xs + (size_t)hslice * kRouterTok;
+  const int e0 = blockIdx.x * 32, t0 = blockIdx.y * kRouterTok, h0 = blockIdx.z * hslice;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int i = threadIdx.x; i < H * kRouterTok; i += blockDim.x) {
+  for (int i = threadIdx.x; i < hslice * kRouterTok; i += blockDim.x) {
     const int h = i / kRouterTok, tt = i % kRouterTok;
     const int t = t0 + tt;
-    xs[i] = t < T ? __uint_as_float((uint32_t)x[(int64_t)t * H + h] << 16) : 0.0f;
+    xs[i] = t < T ? __uint_as_float((uint32_t)x[(int64_t)t * H + h0 + h] << 16) : 0.0f;
   }
   __syncthreads();
   const int e = min(e0 + lane, E - 1);
-  const int hs = H / kRouterWarps, hb = warp * hs;
+  const int hs = hslice / kRouterWarps, hb = warp * hs;
   float acc[kRouterTok];
 #pragma unroll
   for (int i = 0; i < kRouterTok; ++i) acc[i] = 0.0f;
-  const float *rp = router + (int64_t)hb * E + e;
+  const float *rp = router + (int64_t)(h0 + hb) * E + e;
 #pragma unroll 8
   for (int h = 0; h < hs; ++h) {
     const float r = __ldg(rp + (int64_t)h * E);
@@ -72,24 +79,177 @@ __global__ void __launch_bounds__(32 * kRouterWarps)
     float v = 0.0f;
     for (int w = 0; w < kRouterWarps; ++w) v += red[(w * kRouterTok + tt) * 32 + l];
     const int t = t0 + tt, ee = e0 + l;
-    if (t < T && ee < E) logits[(int64_t)t * E + ee] = v;
+    if (t < T && ee < E) part[((int64_t)blockIdx.z * T + t) * E + ee] = v;
+  }
+}
+
+__device__ __forceinline__ uint32_t tf32_rna(float f) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(f));
+  return r;
+}
+
+__device__ __forceinline__ void mma_tf32_1688(float c[4], const uint32_t a[4], uint32_t b0,
+                                              uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// CTA: 64 tokens x 64 experts x one H slice (blockIdx.z), 4 warps of 16
+// tokens x 64 experts, the slice in chunks of 32.  Each chunk is fetched with
+// 16-byte loads into registers one chunk ahead (2 x loads + 4 router loads
+// per thread in flight while the previous chunk is multiplied), then stored to
+// shared memory: x as TF32 [token][h] (row stride 36 words), the router as
+// TF32 hi and lo parts [h][expert] (row stride 72 words), strides at which the
+// fragment reads are bank-conflict free.  The tensor cores' fp32 accumulation
+// is not IEEE round-to-nearest, so each chunk's 8 MMAs accumulate into a fresh
+// partial that is then added to the running sum with an ordinary fp32 add
+// (chains of 8 MMAs instead of 2 H / 8), which keeps the logits within ~1e-6
+// of an fp32 dot product.  Requires E % 4 == 0, H % (32 * slices) == 0 and
+// 16-byte aligned x and router.
+constexpr int kRtcTok = 64, kRtcExp = 64, kRtcK = 32, kRtcXLd = 36, kRtcRLd = 72;
+
+__global__ void __launch_bounds__(128) router_logits_tc_kernel(const uint16_t *__restrict__ x,
+                                                               const float *__restrict__ router,
+                                                               float *__restrict__ part, int T,
+                                                               int H, int E, int hslice) {
+  __shared__ __align__(16) uint32_t xs[kRtcTok][kRtcXLd];  // tf32 x
+  __shared__ __align__(16) uint32_t rh[kRtcK][kRtcRLd];    // tf32 hi of router
+  __shared__ __align__(16) uint32_t rl[kRtcK][kRtcRLd];    // tf32 lo of router
+  const int t0 = blockIdx.y * kRtcTok, e0 = blockIdx.x * kRtcExp;
+  const int hbeg = blockIdx.z * hslice, hend = hbeg + hslice;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, c = lane & 3;
+
+  // Fetch assignment: x chunk = 64 tokens x 32 h bf16 = 256 uint4 (2 per
+  // thread); router chunk = 32 h x 64 experts fp32 = 512 float4 (4 per thread).
+  int xt[2], xk[2], rk[4], re[4];
+  bool xv[2], rv[4];
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int i = tid + 128 * u;
+    xt[u] = i >> 2;
+    xk[u] = (i & 3) * 8;
+    xv[u] = t0 + xt[u] < T;
+  }
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int i = tid + 128 * u;
+    rk[u] = i >> 4;
+    re[u] = (i & 15) * 4;
+    rv[u] = e0 + re[u] < E;
+  }
+  uint4 xr[2];
+  float4 rr[4];
+  auto fetch = [&](int h0) {
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+      xr[u] = xv[u] ? __ldg(reinterpret_cast<const uint4 *>(x + (int64_t)(t0 + xt[u]) * H + h0 +
+                                                            xk[u]))
+                    : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      rr[u] = rv[u] ? __ldg(reinterpret_cast<const float4 *>(router + (int64_t)(h0 + rk[u]) * E +
+                                                             e0 + re[u]))
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
+  };
+
+  float acc[8][4];
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[j][i] = 0.0f;
+  fetch(hbeg);
+  for (int h0 = hbeg; h0 < hend; h0 += kRtcK) {
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const uint32_t w[4] = {xr[u].x, xr[u].y, xr[u].z, xr[u].w};
+      uint4 q0, q1;  // h = xk..xk+3 and xk+4..xk+7
+      q0.x = w[0] << 16;
+      q0.y = w[0] & 0xFFFF0000u;
+      q0.z = w[1] << 16;
+      q0.w = w[1] & 0xFFFF0000u;
+      q1.x = w[2] << 16;
+      q1.y = w[2] & 0xFFFF0000u;
+      q1.z = w[3] << 16;
+      q1.w = w[3] & 0xFFFF0000u;
+      *reinterpret_cast<uint4 *>(&xs[xt[u]][xk[u]]) = q0;
+      *reinterpret_cast<uint4 *>(&xs[xt[u]][xk[u] + 4]) = q1;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float v[4] = {rr[u].x, rr[u].y, rr[u].z, rr[u].w};
+      uint32_t hv[4], lv[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        hv[q] = tf32_rna(v[q]);
+        lv[q] = tf32_rna(v[q] - __uint_as_float(hv[q]));
+      }
+      *reinterpret_cast<uint4 *>(&rh[rk[u]][re[u]]) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+      *reinterpret_cast<uint4 *>(&rl[rk[u]][re[u]]) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+    }
+    __syncthreads();
+    if (h0 + kRtcK < hend) fetch(h0 + kRtcK);
+    float pa[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) pa[j][i] = 0.0f;
+#pragma unroll
+    for (int k8 = 0; k8 < kRtcK; k8 += 8) {
+      const int tr = 16 * warp + g;
+      const uint32_t a[4] = {xs[tr][k8 + c], xs[tr + 8][k8 + c], xs[tr][k8 + c + 4],
+                             xs[tr + 8][k8 + c + 4]};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int en = 8 * j + g;
+        mma_tf32_1688(pa[j], a, rl[k8 + c][en], rl[k8 + c + 4][en]);
+        mma_tf32_1688(pa[j], a, rh[k8 + c][en], rh[k8 + c + 4][en]);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[j][i] += pa[j][i];
+    __syncthreads();
+  }
+  float *out = part + (int64_t)blockIdx.z * T * E;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int e = e0 + 8 * j + 2 * c;
+    const int t = t0 + 16 * warp + g;
+    if (e < E) {  // E % 4 == 0: e + 1 < E as well
+      if (t < T)
+        *reinterpret_cast<float2 *>(out + (int64_t)t * E + e) = make_float2(acc[j][0], acc[j][1]);
+      if (t + 8 < T)
+        *reinterpret_cast<float2 *>(out + (int64_t)(t + 8) * E + e) =
+            make_float2(acc[j][2], acc[j][3]);
+    }
   }
 }
 
 // One warp per token: softmax over E (E <= 256: 8 logits per lane), top-k by
 // repeated warp arg-max (ties to the lower index), optional renormalisation.
-__global__ void router_topk_kernel(const float *__restrict__ logits, int T, int E, int k,
+__global__ void router_topk_kernel(const float *__restrict__ part, int nslices,
+                                   float *__restrict__ logits_out, int T, int E, int k,
                                    int renormalize, int32_t *__restrict__ topk_ids,
                                    float *__restrict__ topk_w) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= T) return;
-  const float *lg = logits + (int64_t)warp * E;
   float p[8];
   float mx = -FLT_MAX;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int e = lane + 32 * i;
-    p[i] = e < E ? lg[e] : -FLT_MAX;
+    float v = 0.0f;
+    if (e < E) {
+      for (int z = 0; z < nslices; ++z) v += part[((int64_t)z * T + warp) * E + e];
+      if (logits_out) logits_out[(int64_t)warp * E + e] = v;
+    }
+    p[i] = e < E ? v : -FLT_MAX;
     mx = fmaxf(mx, p[i]);
   }
 #pragma unroll
@@ -152,19 +312,51 @@ __global__ void router_topk_kernel(const float *__restrict__ logits, int T, int 
   }
 }
 
-cudaError_t launch_router(const uint16_t *x, const float *router, float *logits, int T, int H,
-                          int E, int k, int renormalize, int32_t *ids, float *w,
-                          cudaStream_t st) {
-  if (T == 0) return cudaSuccess;
-  const size_t smem = sizeof(float) * ((size_t)H * kRouterTok + kRouterWarps * kRouterTok * 32);
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(router_logits_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
+static bool router_tc_ok(int T, int H, int E) {
+  return T >= kRouterTcMinTokens && E % 4 == 0 && H % kRtcK == 0;
+}
+
+// H slices of the router for T tokens: enough CTAs to cover the GPU.  The
+// logits workspace holds this many [T, E] partial sums.
+int router_slices(int T, int H, int E) {
+  int ctas, unit;
+  if (router_tc_ok(T, H, E)) {
+    ctas = ((E + kRtcExp - 1) / kRtcExp) * ((T + kRtcTok - 1) / kRtcTok);
+    unit = kRtcK;
+  } else {
+    ctas = ((E + 31) / 32) * ((T + kRouterTok - 1) / kRouterTok);
+    unit = kRouterWarps;
   }
-  dim3 grid((E + 31) / 32, (T + kRouterTok - 1) / kRouterTok);
-  router_logits_kernel<<<grid, 32 * kRouterWarps, smem, st>>>(x, router, logits, T, H, E);
-  router_topk_kernel<<<(T * 32 + 255) / 256, 256, 0, st>>>(logits, T, E, k, renormalize, ids, w);
+  int hs = 1;
+  while (hs < 16 && ctas * hs < 148 && H % (2 * hs * unit) == 0 && H / (2 * hs) >= 128) hs *= 2;
+  return hs;
+}
+
+cudaError_t launch_router(const uint16_t *x, const float *router, float *part, int nslices,
+                          float *logits_out, int T, int H, int E, int k, int renormalize,
+                          int32_t *ids, float *w, cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  if (nslices < 1) nslices = 1;
+  const bool aligned16 = (((uintptr_t)x | (uintptr_t)router) & 15) == 0;
+  if (router_tc_ok(T, H, E) && aligned16 && H % (nslices * kRtcK) == 0) {
+    dim3 grid((E + kRtcExp - 1) / kRtcExp, (T + kRtcTok - 1) / kRtcTok, nslices);
+    router_logits_tc_kernel<<<grid, 128, 0, st>>>(x, router, part, T, H, E, H / nslices);
+  } else {
+    while (nslices > 1 && H % (nslices * kRouterWarps) != 0) nslices >>= 1;
+    const int hslice = H / nslices;
+    const size_t smem = sizeof(float) * ((size_t)hslice * kRouterTok + kRouterWarps * kRouterTok * 32);
+    static size_t configured = 48 * 1024;
+    if (smem > configured) {
+      cudaError_t e = cudaFuncSetAttribute(router_logits_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e;
+      configured = smem;
+    }
+    dim3 grid((E + 31) / 32, (T + kRouterTok - 1) / kRouterTok, nslices);
+    router_logits_kernel<<<grid, 32 * kRouterWarps, smem, st>>>(x, router, part, T, H, E, hslice);
+  }
+  router_topk_kernel<<<(T * 32 + 255) / 256, 256, 0, st>>>(part, nslices, logits_out, T, E, k,
+                                                           renormalize, ids, w);
   return cudaGetLastError();
 }
 

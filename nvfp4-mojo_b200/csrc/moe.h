@@ -41,8 +41,13 @@ cudaError_t launch_moe_tc(const MoeTcLaunch &L, bool gate_up, cudaStream_t st);
 bool moe_tc_supported(int H, int I);
 int moe_tc_rows_per_item();
 
-cudaError_t launch_router(const uint16_t *x, const float *router, float *logits, int T, int H,
-                          int E, int k, int renormalize, int32_t *ids, float *w, cudaStream_t st);
+// Router: partial logits in `part` ([nslices][T][E]; nslices from
+// router_slices), summed in slice order by the top-k kernel, which also
+// writes the logits to logits_out (nullable).
+int router_slices(int T, int H, int E);
+cudaError_t launch_router(const uint16_t *x, const float *router, float *part, int nslices,
+                          float *logits_out, int T, int H, int E, int k, int renormalize,
+                          int32_t *ids, float *w, cudaStream_t st);
 cudaError_t launch_moe_permute(const int32_t *row_expert, const int32_t *x_row_index, int R, int E,
                                int tpi, const MoePlan &plan, cudaStream_t st);
 cudaError_t launch_slot_token(int32_t *idx, int R, int k, cudaStream_t st);

@@ -69,8 +69,8 @@ ForwardLayout forward_layout(const nvfp4_moe_desc &d, int64_t T) {
   o = up(o + sizeof(int32_t) * R);
   L.w = o;
   o = up(o + sizeof(float) * R);
-  L.logits = o;
-  o = up(o + sizeof(float) * T * d.num_experts);
+  L.logits = o;  // router partial sums, one [T, E] slice per H slice
+  o = up(o + sizeof(float) * T * d.num_experts * router_slices((int)T, d.hidden, d.num_experts));
   L.slot_tok = o;
   o = up(o + sizeof(int32_t) * R);
   L.y_slot = o;
@@ -239,9 +239,10 @@ extern "C" int nvfp4_moe_route(const nvfp4_moe_desc *d, const float *router, con
   if (T == 0) return NVFP4_OK;
   if (!router || !x || !ids || !w || !logits)
     return fail(NVFP4_ERR_INVALID_ARG, "null router, activation or output pointer");
-  return check_launch(launch_router(static_cast<const uint16_t *>(x), router, logits, (int)T,
-                                    d->hidden, d->num_experts, d->top_k, d->renormalize, ids, w,
-                                    static_cast<cudaStream_t>(stream)),
+  // The caller's logits buffer holds one slice: a single H slice here.
+  return check_launch(launch_router(static_cast<const uint16_t *>(x), router, logits, 1, nullptr,
+                                    (int)T, d->hidden, d->num_experts, d->top_k, d->renormalize,
+                                    ids, w, static_cast<cudaStream_t>(stream)),
                       "router launch");
 }
 
@@ -339,8 +340,10 @@ extern "C" int nvfp4_moe_forward(const nvfp4_moe_desc *d, const nvfp4_moe_weight
   int32_t *slot_tok = reinterpret_cast<int32_t *>(base + L.slot_tok);
   float *y_slot = reinterpret_cast<float *>(base + L.y_slot);
   const int64_t R = T * d->top_k;
-  rc = check_launch(launch_router(static_cast<const uint16_t *>(x), w->router, logits, (int)T,
-                                  d->hidden, d->num_experts, d->top_k, d->renormalize, ids, tw, st),
+  rc = check_launch(launch_router(static_cast<const uint16_t *>(x), w->router, logits,
+                                  router_slices((int)T, d->hidden, d->num_experts), nullptr,
+                                  (int)T, d->hidden, d->num_experts, d->top_k, d->renormalize,
+                                  ids, tw, st),
                     "router launch");
   if (rc) return rc;
   rc = check_launch(launch_slot_token(slot_tok, (int)R, d->top_k, st), "slot index launch");

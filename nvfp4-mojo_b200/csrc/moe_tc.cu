@@ -1,14 +1,14 @@
 // moe_tc.cu -- grouped NVFP4 expert GEMMs on the 5th-generation tensor cores,
 // for MoE batches with many rows per expert (prefill).
 //
-// Rows are sorted by expert (moe_permute_kernel) into items of at most 128
+// Rows are sorted by expert (moe_permute_kernel) into items of at most 256
 // rows; a tile is (item, 128 weight rows).  Persistent CTAs walk the tile list
 // (its length is read from device memory), one CTA per SM.  Roles as in
 // gemm_tc.cu: warp 0 TMA producer, warp 1 TMEM owner + single MMA thread,
 // warps 4-11 E2M1 x E4M3 -> bf16 decoders, warps 12-15 epilogue.
 //
 //   kGateUp: A = gate rows and up rows of the expert (two 128-row tiles, two
-//            accumulators), B = the expert's activation rows (gathered into
+//            128 x 256 accumulators), B = the expert's activation rows (gathered into
 //            sorted order); epilogue h_g, h_u -> silu(h_g) * h_u written as bf16
 //            hi + lo parts (nvfp4/deltanet.mojo:66-80 for SiLU).
 //   kDown:   A = down rows, B = the SiLU*up rows as hi and lo bf16 tiles (two
@@ -27,18 +27,23 @@ namespace nvfp4 {
 
 static __device__ int g_moe_tc_status;
 
-constexpr int kMtBM = 128, kMtBN = 128, kMtBK = 64;
+constexpr int kMtBM = 128, kMtBN = 256, kMtBK = 64;
 constexpr int kMtDecWarps = 8, kMtEpiWarps = 4;
 constexpr int kMtThreads = (4 + kMtDecWarps + kMtEpiWarps) * 32;
 enum MoeTcMode { kGateUp = 0, kDown = 1 };
 
+// 256-token tiles: the weight decode per MMA flop is halved against 128.
+// kGateUp: two 128x256 accumulators fill TMEM (512 columns, one buffer: the
+// epilogue of a tile runs before the next tile's first MMA); kDown: one
+// accumulator, double-buffered.
 template <int MODE>
 struct MtCfg {
   static constexpr int NA = MODE == kGateUp ? 2 : 1;   // A tiles (weight row sets)
   static constexpr int NB = MODE == kGateUp ? 1 : 2;   // B tiles (activation parts)
-  static constexpr int S = MODE == kGateUp ? 3 : 4;    // pipeline stages
+  static constexpr int S = MODE == kGateUp ? 3 : 2;    // pipeline stages
+  static constexpr int NBUF = MODE == kGateUp ? 1 : 2; // TMEM accumulator buffers
   static constexpr int kA = kMtBM * kMtBK * 2;         // 16 KB
-  static constexpr int kB = kMtBN * kMtBK * 2;         // 16 KB
+  static constexpr int kB = kMtBN * kMtBK * 2;         // 32 KB
   static constexpr int kR = kMtBM * kMtBK / 2;         // 4 KB
   static constexpr int kS = kMtBM * 16;                // 2 KB per 4 stages
   static constexpr int offA = 0;
@@ -50,7 +55,9 @@ struct MtCfg {
   static constexpr int nBars = 3 * S + 4;
   static constexpr int offTmem = offBar + nBars * 8;
   static constexpr int alloc = offTmem + 16 + 1024;
-  static constexpr int tmem_cols = 2 * NA * kMtBN;     // double-buffered accumulators
+  static constexpr int tmem_cols = NBUF * NA * kMtBN;
+  static_assert(tmem_cols <= 512, "TMEM has 512 columns");
+  static_assert(alloc <= 232448, "dynamic shared memory per CTA");
 };
 
 struct MoeTcArgs {
@@ -100,7 +107,7 @@ __global__ void __launch_bounds__(kMtThreads, 1)
       mbar_init(bar_dec + 8 * s, kMtDecWarps);
       mbar_init(bar_empty + 8 * s, 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < C::NBUF; ++b) {
       mbar_init(bar_tfull + 8 * b, 1);
       mbar_init(bar_tempty + 8 * b, kMtEpiWarps);
     }
@@ -173,7 +180,7 @@ __global__ void __launch_bounds__(kMtThreads, 1)
       int g = 0, i = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x, ++i) {
-        const int b = i & 1, ub = i >> 1;
+        const int b = i % C::NBUF, ub = i / C::NBUF;
         if (ub > 0 && !mbar_wait(bar_tempty + 8 * b, (ub - 1) & 1, &g_moe_tc_status,
                                  kDevTimeoutAcc, abort))
           break;
@@ -251,7 +258,7 @@ __global__ void __launch_bounds__(kMtThreads, 1)
     const int q = warp & 3;
     int i = 0;
     for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++i) {
-      const int b = i & 1, ub = i >> 1;
+      const int b = i % C::NBUF, ub = i / C::NBUF;
       const bool w_ok = mbar_wait(bar_tfull + 8 * b, ub & 1, &g_moe_tc_status, kDevTimeoutAcc, abort);
       if (!__all_sync(0xffffffffu, w_ok && !*abort)) break;
       tc_fence_after();
