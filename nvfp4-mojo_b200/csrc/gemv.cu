@@ -1,0 +1,598 @@
+// gemv.cu -- decode GEMV for M <= 8 tokens: y[M, N] = alpha[n] * x[M, K] . W[N, K]^T
+// with W in NVFP4 (the reference's nvfp4_matvec / nvfp4_linear_forward at
+// batch_seq_len <= 8: nvfp4/deltanet.mojo:549-584, nvfp4/nvfp4_gemm_gpu.mojo:185-224).
+//
+// HBM-bound: every weight byte is read once, so the kernel is organised around
+// keeping enough bytes in flight with few instructions per byte.
+//
+//   * Two CTAs per SM.  A cluster of C CTAs (grid.x = C) splits K into C
+//     slices and reduces the fp32 partial sums through distributed shared
+//     memory; the clusters split the 16-row tiles as evenly as tile counts
+//     allow.  CTA = one consumer warp per tile + 1 producer warp.
+//   * The producer streams 256-k chunks of the CTA's tiles with TMA (codes in
+//     a 128-byte-swizzled box, blockscales in a plain one) through an
+//     S-stage mbarrier ring: per-thread loads through L1 cannot keep enough
+//     bytes in flight to saturate HBM, the TMA engine can.  Lane quad c of
+//     row g takes bytes [32c, 32c + 32) of each 128-byte row chunk.
+//   * Launched with programmatic stream serialization: the set-up overlaps
+//     the previous kernel's tail (griddepcontrol).
+//   * Decode: the hardware E2M1x2 -> f16x2 conversion (exact), times the E4M3
+//     blockscale converted E4M3x2 -> f16x2 (exact); the product LUT*scale has
+//     at most 6 significant bits and lies in [2^-10, 2688], so it is exact in
+//     f16.  mma.sync m16n8k16 f16 x f16 -> f32 does the multiply-adds.
+//   * K permutation: the MMA's 16 k positions are taken as the lane quad's
+//     4 codes at k = 64c + 4j .. 4j+3 of the chunk (MMA j = 0..15), so each
+//     lane's A fragment comes from 2 bytes of its own loaded words, its
+//     blockscale is byte j/4 of one 4-byte scale word per row and chunk, and
+//     its B fragment is x[token g][64c + 4j .. +3]: 8 bytes of the token's row.
+//   * Activations: each CTA converts its K slice of x (bf16) to f16 in shared
+//     memory, scaled per token by a power of two 2^s chosen so that
+//     max|x| * 2^s lies in [2^14, 2^15): bf16 values are then exact in f16
+//     (apart from elements below max|x| * 2^-28, which become f16 subnormals),
+//     and the partial sums are multiplied by 2^-s (exact) before the reduction.
+//     Rows of x are stored with a 16-byte-unit XOR swizzle and a 64-byte pad,
+//     which makes the B-fragment loads (LDS.128) bank-conflict free.
+#include <cooperative_groups.h>
+#include <map>
+#include <mutex>
+#include <tuple>
+#include <cuda_fp16.h>
+
+#include "../../include/nvfp4.h"
+#include "kernels.h"
+#include "nvfp4_common.cuh"
+#include "tc_common.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace nvfp4 {
+
+bool make_tmap_2d(CUtensorMap *m, CUtensorMapDataType dt, int esize, const void *base,
+                  int64_t rows, int64_t cols, int64_t ld_elems, int box_cols, int box_rows,
+                  CUtensorMapSwizzle sw);
+int tc_sm_count();
+
+namespace {
+
+static __device__ int g_gemv_status;  // DeviceStatus of the last failing CTA
+
+constexpr int kGvChunk = 256;  // k per row chunk (128 bytes of codes)
+constexpr int kGvTok = 8;      // tokens per MMA (n = 8)
+
+__device__ __forceinline__ void ldg_v8(const uint8_t *p, uint32_t (&r)[8]) {
+  asm("ld.global.nc.L1::no_allocate.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7])
+      : "l"(p));
+}
+
+__device__ __forceinline__ uint32_t ldg_u32(const uint8_t *p) {
+  uint32_t v;
+  asm("ld.global.nc.L1::no_allocate.b32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+
+// Four f16x2 from the four bytes of w: d_i = (lo: low nibble, hi: high nibble of byte i).
+__device__ __forceinline__ void e2m1x8_to_f16x2(uint32_t w, uint32_t (&d)[4]) {
+  asm("{\n"
+      ".reg .b8 b0, b1, b2, b3;\n"
+      "mov.b32 {b0, b1, b2, b3}, %4;\n"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n"
+      "cvt.rn.f16x2.e2m1x2 %1, b1;\n"
+      "cvt.rn.f16x2.e2m1x2 %2, b2;\n"
+      "cvt.rn.f16x2.e2m1x2 %3, b3;\n"
+      "}"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(w));
+}
+
+// f16x2 of the blockscale pair in half `h` (0: bytes 0-1, 1: bytes 2-3) of sw.
+__device__ __forceinline__ uint32_t scale_pair_f16x2(uint32_t sw, int h) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"((unsigned short)(h ? sw >> 16 : sw)));
+  return r;
+}
+
+// a * (s.lo, s.lo) or a * (s.hi, s.hi): the broadcast folds into the multiply.
+__device__ __forceinline__ uint32_t hmul2_bcast(uint32_t a, uint32_t s, int hi) {
+  const __half2 av = *reinterpret_cast<const __half2 *>(&a);
+  const __half2 sv = *reinterpret_cast<const __half2 *>(&s);
+  const __half2 r = __hmul2(av, hi ? __high2half2(sv) : __low2half2(sv));
+  return *reinterpret_cast<const uint32_t *>(&r);
+}
+
+__device__ __forceinline__ void mma_f16_16816(float (&c)[4], uint32_t a0, uint32_t a1,
+                                              uint32_t a2, uint32_t a3, uint32_t b0,
+                                              uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Address of the same shared-memory variable in CTA `rank` of the cluster.
+__device__ __forceinline__ float *cluster_map(float *p, int rank) {
+  return cg::this_cluster().map_shared_rank(p, rank);
+}
+
+// Physical 16-byte unit of logical unit u in a token row of x (XOR swizzle).
+__device__ __forceinline__ int xs_unit(int u) { return u ^ ((u >> 3) & 3); }
+
+struct GemvArgs {
+  const uint8_t *w;
+  const uint8_t *sf;
+  AlphaSpec al;
+  const uint16_t *x;
+  int64_t x_ld;
+  void *y;
+  int y_dtype;
+  int64_t y_ld;
+  int M, N, K;
+  int ks;       // K per CTA (multiple of kGvChunk)
+  int xstride;  // bytes per token row of the f16 x slice in shared memory
+  int stages;   // TMA ring stages
+};
+
+// Consumer view of one staged chunk: codes of rows g and g+8 of the warp's
+// tile (bytes [32c, 32c + 32) of each 128-byte row) and their scale words.
+struct GemvChunk {
+  uint32_t wg[8], wh[8];
+  uint32_t sg, sh;
+};
+
+__device__ __forceinline__ void gemv_fetch(GemvChunk &b, uint32_t codes, uint32_t scales, int rl,
+                                           int c) {
+  // 128-byte swizzle of the TMA box: 16-byte unit u of row r sits at u ^ (r & 7).
+  const int sw = rl & 7;
+  const uint32_t rg = codes + 128u * rl, rh = rg + 128u * 8;
+  const uint4 a0 = lds_v4(rg + 16u * ((2 * c) ^ sw)), a1 = lds_v4(rg + 16u * ((2 * c + 1) ^ sw));
+  const uint4 b0 = lds_v4(rh + 16u * ((2 * c) ^ sw)), b1 = lds_v4(rh + 16u * ((2 * c + 1) ^ sw));
+  b.wg[0] = a0.x; b.wg[1] = a0.y; b.wg[2] = a0.z; b.wg[3] = a0.w;
+  b.wg[4] = a1.x; b.wg[5] = a1.y; b.wg[6] = a1.z; b.wg[7] = a1.w;
+  b.wh[0] = b0.x; b.wh[1] = b0.y; b.wh[2] = b0.z; b.wh[3] = b0.w;
+  b.wh[4] = b1.x; b.wh[5] = b1.y; b.wh[6] = b1.z; b.wh[7] = b1.w;
+  b.sg = lds_u32(scales + 16u * rl + 4u * c);
+  b.sh = lds_u32(scales + 16u * (rl + 8) + 4u * c);
+}
+
+__device__ __forceinline__ void gemv_compute(const GemvChunk &b, float (&acc)[4], uint32_t xrow,
+                                             bool has_x, int ch, int c) {
+  // This lane's x units for the chunk: logical 32*ch + 8c + p, p = 0..7.
+  const int ub = 32 * ch + 8 * c;
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {  // blockscales 2hh, 2hh+1 of the lane's 64 k
+    const uint32_t s_g = scale_pair_f16x2(b.sg, hh), s_h = scale_pair_f16x2(b.sh, hh);
+#pragma unroll
+    for (int p4 = 0; p4 < 4; ++p4) {  // code word p = 4hh + p4: MMAs j = 2p, 2p+1
+      const int p = 4 * hh + p4, hi = p4 >> 1;  // blockscale q = p / 2 = 2hh + hi
+      const uint4 xv = has_x ? lds_v4(xrow + 16u * (uint32_t)xs_unit(ub + p))
+                             : make_uint4(0u, 0u, 0u, 0u);
+      uint32_t dg[4], dh[4];
+      e2m1x8_to_f16x2(b.wg[p], dg);
+      e2m1x8_to_f16x2(b.wh[p], dh);
+      mma_f16_16816(acc, hmul2_bcast(dg[0], s_g, hi), hmul2_bcast(dh[0], s_h, hi),
+                    hmul2_bcast(dg[1], s_g, hi), hmul2_bcast(dh[1], s_h, hi), xv.x, xv.y);
+      mma_f16_16816(acc, hmul2_bcast(dg[2], s_g, hi), hmul2_bcast(dh[2], s_h, hi),
+                    hmul2_bcast(dg[3], s_g, hi), hmul2_bcast(dh[3], s_h, hi), xv.z, xv.w);
+    }
+  }
+}
+
+constexpr int kGvMaxWarps = 13;    // consumer warps: 2 CTAs of 14 warps per SM
+constexpr int kGvTileCodes = 16 * (kGvChunk / 2);       // 2 KB: one 16-row tile
+constexpr int kGvTileScales = 16 * (kGvChunk / kGroup);  // 256 B
+constexpr int kGvMaxKs = 2048;     // K per CTA (f16 x slice in shared memory)
+constexpr int kGvSmemCap = 110 * 1024;  // dynamic shared memory per CTA (two per SM)
+
+// Shared memory of a CTA with `w` consumer warps, `stages` ring stages, `m`
+// token rows of x and a K split of `cs`: the ring, the f16 x slice, the
+// receive buffer of the cluster reduction ([cs][per rows][8 tokens] fp32,
+// per = ceil(16 w / cs)), per-token scales and exponents, alpha of the rows
+// this CTA finalises, the mbarriers.
+struct GemvSmem {
+  int stage, codes, ring, xs, recv, inv, emax, alpha, bars, total;
+  __host__ __device__ GemvSmem(int w, int stages, int xstride, int m, int cs) {
+    codes = w * kGvTileCodes;
+    stage = (codes + w * kGvTileScales + 1023) & ~1023;
+    ring = 0;
+    xs = stages * stage;
+    recv = xs + m * xstride;
+    inv = recv + (int)sizeof(float) * cs * ((16 * w + cs - 1) / cs) * kGvTok;
+    emax = inv + (int)sizeof(float) * kGvTok;
+    alpha = emax + (int)sizeof(int) * kGvTok;
+    bars = (alpha + (int)sizeof(float) * ((16 * w + cs - 1) / cs) + 7) & ~7;
+    total = bars + 16 * stages;
+  }
+};
+
+// Cluster q of a K split into gridDim.x slices owns row tiles
+// [q * nt / nq, (q + 1) * nt / nq) (nq = gridDim.y clusters, nt = 16-row
+// tiles): tile counts differ by at most one, so every SM gets the same
+// weight bytes to within one tile.  CTA = one consumer warp per tile of the
+// cluster + a producer warp that streams the CTA's 256-k chunks of those
+// tiles with TMA (per stage: a 128-byte-swizzled box of the tiles' rows x
+// 128 B of codes and one of their rows x 16 B of blockscales) through an
+// S-stage ring.
+__global__ void __launch_bounds__(32 * (kGvMaxWarps + 1), 2)
+    gemv_kernel(const __grid_constant__ CUtensorMap tmW_hi, const __grid_constant__ CUtensorMap tmS_hi,
+                const __grid_constant__ CUtensorMap tmW_lo, const __grid_constant__ CUtensorMap tmS_lo,
+                GemvArgs a) {
+  constexpr int kRedLd = kGvTok + 1;
+  extern __shared__ __align__(1024) uint8_t gsm_raw[];
+  uint8_t *gsm = reinterpret_cast<uint8_t *>(((uintptr_t)gsm_raw + 1023) & ~(uintptr_t)1023);
+  __shared__ int abort_flag;
+
+  const int W = (int)(blockDim.x >> 5) - 1;  // consumer warps
+  const int S = a.stages;
+  const GemvSmem L(W, S, a.xstride, a.M, gridDim.x);
+  uint8_t *ring = gsm + L.ring;
+  uint8_t *xs = gsm + L.xs;
+  float *recv = reinterpret_cast<float *>(gsm + L.recv);
+  float *inv_scale = reinterpret_cast<float *>(gsm + L.inv);
+  int *emax = reinterpret_cast<int *>(gsm + L.emax);
+  float *alpha_s = reinterpret_cast<float *>(gsm + L.alpha);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(gsm + L.bars);  // full[S], empty[S]
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, c = lane & 3;
+  const int Cn = gridDim.x, slice = blockIdx.x;
+  const int nt = (a.N + 15) / 16, nq = gridDim.y, q = blockIdx.y;
+  const int tile0 = (int)((int64_t)q * nt / nq), ntiles = (int)((int64_t)(q + 1) * nt / nq) - tile0;
+  const int k0 = slice * a.ks;
+  const int nch = a.ks / kGvChunk;
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + S);
+  volatile int *abort = &abort_flag;
+
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, ntiles);
+    }
+    abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (tid < kGvTok) emax[tid] = 0;
+  __syncthreads();
+  // Programmatic dependent launch: everything above overlapped the previous
+  // kernel; inputs are read only after it has completed.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // Rows this CTA finalises: [lo, lo + nr) of the cluster's 16 * ntiles.
+  const int rows = 16 * ntiles;
+  const int per = (rows + Cn - 1) / Cn;
+  const int lo = min(slice * per, rows), nr = min(lo + per, rows) - lo;
+  for (int i = tid; i < nr; i += blockDim.x)
+    alpha_s[i] = 16 * tile0 + lo + i < a.N ? alpha_of(a.al, 0, 16 * tile0 + lo + i) : 0.0f;
+
+  if (warp == W) {
+    // Producer: one thread issues the TMA loads, S stages ahead of use; one
+    // box per stage for all of the CTA's tiles (maps with W and W-1 tiles).
+    if (lane == 0) {
+      const uint64_t pol = l2_evict_first_policy();
+      const CUtensorMap *tmW = ntiles == W ? &tmW_hi : &tmW_lo;
+      const CUtensorMap *tmS = ntiles == W ? &tmS_hi : &tmS_lo;
+      prefetch_tmap(tmW);
+      prefetch_tmap(tmS);
+      int issued = 0;
+      for (int ch = 0; ch < nch; ++ch) {
+        const int s = ch % S, u = ch / S;
+        if (u > 0 && !mbar_wait(empty0 + 8 * s, (u - 1) & 1, &g_gemv_status, kDevTimeoutEmpty,
+                                abort))
+          break;
+        const uint32_t st = smem_u32(ring + s * L.stage);
+        mbar_arrive_expect_tx(full0 + 8 * s, ntiles * (kGvTileCodes + kGvTileScales));
+        const int xc = (k0 + ch * kGvChunk) / 2, xsf = (k0 + ch * kGvChunk) / kGroup;
+        tma_load_2d_hint(st, tmW, xc, 16 * tile0, full0 + 8 * s, pol);
+        tma_load_2d_hint(st + L.codes, tmS, xsf, 16 * tile0, full0 + 8 * s, pol);
+        issued = ch + 1;
+      }
+      // After an abort, wait (bounded) for the copies still in flight before exit.
+      volatile int no_abort = 0;
+      for (int ch = max(issued - S, 0); ch < issued; ++ch)
+        mbar_wait(full0 + 8 * (ch % S), (ch / S) & 1, &g_gemv_status, kDevTimeoutFull,
+                  &no_abort);
+    }
+    __syncwarp();
+  } else {
+    // x slice -> f16 with a per-token power-of-two scale.  The M * ks / 8
+    // 16-byte units of the slice are spread over all consumer threads: the
+    // largest bf16 exponent per token is taken with shared atomicMax, then
+    // the units are converted.  Up to 4 units per thread stay in registers
+    // (one read of x); beyond that x is read twice (through L1).
+    const int nunits = a.ks / 8, total_units = a.M * nunits, nthr = 32 * W;
+    auto load_units = [&](int base, uint4 (&v)[4]) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int i = base + j * nthr;
+        v[j] = make_uint4(0u, 0u, 0u, 0u);
+        if (i < total_units) {
+          const int tt = i / nunits, u = i - tt * nunits;
+          v[j] = __ldg(reinterpret_cast<const uint4 *>(a.x + (int64_t)tt * a.x_ld + k0 + 8 * u));
+        }
+      }
+    };
+    auto max_units = [&](int base, const uint4 (&v)[4]) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int i = base + j * nthr;
+        if (i < total_units) {
+          uint32_t m = __vmaxu2(__vmaxu2(v[j].x & 0x7F807F80u, v[j].y & 0x7F807F80u),
+                                __vmaxu2(v[j].z & 0x7F807F80u, v[j].w & 0x7F807F80u));
+          m = max(m & 0xFFFFu, m >> 16);
+          atomicMax(&emax[i / nunits], (int)(m >> 7));
+        }
+      }
+    };
+    auto convert_units = [&](int base, const uint4 (&v)[4]) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int i = base + j * nthr;
+        if (i < total_units) {
+          const int tt = i / nunits, u = i - tt * nunits;
+          const int e = max(emax[tt], 1);  // biased bf16 exponent of max|x|
+          const int sc = min(max(141 - e, -126), 127);
+          const float f = __int_as_float((sc + 127) << 23);
+          const uint32_t in[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+          uint32_t o[4];
+#pragma unroll
+          for (int q2 = 0; q2 < 4; ++q2) {
+            const __half2 h2 = __floats2half2_rn(bf16lo(in[q2]) * f, bf16hi(in[q2]) * f);
+            o[q2] = *reinterpret_cast<const uint32_t *>(&h2);
+          }
+          *reinterpret_cast<uint4 *>(xs + tt * a.xstride + 16 * xs_unit(u)) =
+              make_uint4(o[0], o[1], o[2], o[3]);
+        }
+      }
+    };
+    if (total_units <= 4 * nthr) {
+      uint4 v[4];
+      load_units(tid, v);
+      max_units(tid, v);
+      asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
+      convert_units(tid, v);
+    } else {
+      for (int base = tid; base < total_units; base += 4 * nthr) {
+        uint4 v[4];
+        load_units(base, v);
+        max_units(base, v);
+      }
+      asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
+      for (int base = tid; base < total_units; base += 4 * nthr) {
+        uint4 v[4];
+        load_units(base, v);
+        convert_units(base, v);
+      }
+    }
+    if (tid < kGvTok) {
+      const int e = max(emax[tid], 1);
+      const int sc = min(max(141 - e, -126), 127);
+      inv_scale[tid] = tid < a.M ? __frcp_rn(__int_as_float((sc + 127) << 23)) : 0.0f;
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(32 * W) : "memory");  // consumer warps only
+    // The next kernel in the stream may start its prologue now.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+    if (warp < ntiles) {
+      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      const bool has_x = g < a.M;  // tokens >= M: zero B fragments
+      const uint32_t xrow = smem_u32(xs + (has_x ? g : 0) * a.xstride);
+      for (int ch = 0; ch < nch; ++ch) {
+        const int s = ch % S, u = ch / S;
+        const bool ok = mbar_wait(full0 + 8 * s, u & 1, &g_gemv_status, kDevTimeoutFull, abort);
+        if (!__all_sync(0xffffffffu, ok)) break;
+        const uint32_t st = smem_u32(ring + s * L.stage);
+        GemvChunk b;
+        gemv_fetch(b, st + warp * kGvTileCodes, st + L.codes + warp * kGvTileScales, g, c);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty0 + 8 * s);  // operands are in registers
+        // The MMA's fp32 accumulation is not IEEE round-to-nearest: chains are
+        // kept to one chunk (16 MMAs) and chunk sums added with fp32 adds.
+        float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        gemv_compute(b, part, xrow, has_x, ch, c);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[i] += part[i];
+      }
+      // Partial sums (times 2^-s per token) go straight to the CTA of the
+      // cluster that owns the row: slot [slice][row - owner's first row].
+      const float is0 = inv_scale[2 * c], is1 = inv_scale[2 * c + 1];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int r = warp * 16 + g + 8 * h;
+        const int owner = r / per, local = r - owner * per;
+        float *dst = recv + ((size_t)slice * per + local) * kGvTok + 2 * c;
+        if (Cn > 1) dst = cluster_map(dst, owner);
+        if (2 * c < a.M) dst[0] = acc[2 * h] * is0;
+        if (2 * c + 1 < a.M) dst[1] = acc[2 * h + 1] * is1;
+      }
+    }
+  }
+
+  // One cluster barrier (release / acquire) publishes the pushed partial
+  // sums; each CTA then adds its rows' Cn slices in slice order and stores.
+  if (Cn > 1) {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                     : "memory");
+  } else {
+    __syncthreads();
+  }
+  for (int i = tid; i < nr * a.M; i += blockDim.x) {
+    const int r = i % nr, tok = i / nr;
+    float v = 0.0f;
+    for (int qq = 0; qq < Cn; ++qq) v += recv[((size_t)qq * per + r) * kGvTok + tok];
+    const int n = 16 * tile0 + lo + r;
+    if (n < a.N) {
+      v *= alpha_s[r];
+      if (a.y_dtype == kBF16)
+        reinterpret_cast<uint16_t *>(a.y)[(int64_t)tok * a.y_ld + n] = f32_to_bf16_bits(v);
+      else
+        reinterpret_cast<float *>(a.y)[(int64_t)tok * a.y_ld + n] = v;
+    }
+  }
+}
+
+}  // namespace
+
+bool gemv_supported(int M, int K, const void *w, const void *sf, const void *x, int64_t x_ld) {
+  return M >= 1 && M <= kGvTok && K % kGvChunk == 0 && K <= 8 * kGvMaxKs &&
+         ((uintptr_t)w & 15) == 0 && ((uintptr_t)sf & 15) == 0 && ((uintptr_t)x & 15) == 0 &&
+         x_ld % 8 == 0 && tc_gemm_supported(K, w, x, x_ld);
+}
+
+int read_gemv_device_status() {
+  int v = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&v, g_gemv_status, sizeof(int)) != cudaSuccess) return -1;
+  if (v) cudaMemcpyToSymbol(g_gemv_status, &zero, sizeof(int));
+  return v;
+}
+
+namespace {
+
+// Ring stages that fit in the per-CTA budget (two CTAs per SM).
+int gemv_stages(int w, int xstride, int m, int cs) {
+  int s = 4;
+  while (s > 2 && GemvSmem(w, s, xstride, m, cs).total + 1024 > kGvSmemCap) --s;
+  return GemvSmem(w, s, xstride, m, cs).total + 1024 <= kGvSmemCap ? s : 0;
+}
+
+// Clusters of C CTAs (w consumer warps, smem bytes) the GPU holds at once.
+int gemv_cluster_capacity(int C, int w, size_t smem) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int, size_t>, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const auto key = std::make_tuple(dev, C, w, smem);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(C, 1, 1);
+  cfg.blockDim = dim3(32 * (w + 1), 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, gemv_kernel, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  cache[key] = n;
+  return n;
+}
+
+}  // namespace
+
+cudaError_t launch_gemv(const WeightSpec &ws, const AlphaSpec &al, const uint16_t *x,
+                        int64_t x_ld, void *y, int y_dtype, int64_t y_ld, int M,
+                        cudaStream_t st) {
+  if (M == 0 || ws.N == 0) return cudaSuccess;
+  GemvArgs a;
+  a.w = ws.w;
+  a.sf = ws.sf;
+  a.al = al;
+  a.x = x;
+  a.x_ld = x_ld;
+  a.y = y;
+  a.y_dtype = y_dtype;
+  a.y_ld = y_ld;
+  a.M = M;
+  a.N = ws.N;
+  a.K = ws.K;
+  // Two CTAs per SM.  K split C (cluster size): a divisor of the chunk count,
+  // at most 8, with K / C <= kGvMaxKs.  Clusters: two CTAs per SM / C, or
+  // fewer when the GPU cannot hold that many clusters of C at once (a cluster
+  // must fit in one GPC); consumer warps W = the largest tile count of a
+  // cluster (at most kGvMaxWarps).  The C taken minimises the work of the
+  // busiest CTA times the waves of clusters, ks * (W + 0.16 M) * waves: W
+  // tiles of decode + MMA plus the conversion of M activation rows (about
+  // 0.16 of a tile's instructions per row of x).
+  {
+    static std::mutex mu;
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!attr_set[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(
+          gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGvSmemCap + 1024);
+      if (e != cudaSuccess) return e;
+      attr_set[dev] = true;
+    }
+  }
+  const int nck = ws.K / kGvChunk;
+  const int nt = (ws.N + 15) / 16;
+  const int ctas_target = 2 * tc_sm_count();
+  int bestC = 0, bestW = 0, bestNq = 0, bestS = 0;
+  double best_cost = 0.0;
+  for (int C = 1; C <= 8; ++C) {
+    if (nck % C || ws.K / C > kGvMaxKs) continue;
+    const int xstride = 2 * (ws.K / C) + 64;
+    int nq = ctas_target / C;
+    if (nq > nt) nq = nt;
+    if (nq < 1) nq = 1;
+    int w = 0, stages = 0, waves = 1;
+    for (int it = 0; it < 2; ++it) {
+      w = (nt + nq - 1) / nq;
+      if (w > kGvMaxWarps) {
+        w = kGvMaxWarps;
+        nq = (nt + w - 1) / w;
+        w = (nt + nq - 1) / nq;
+      }
+      stages = gemv_stages(w, xstride, M, C);
+      const int cap =
+          gemv_cluster_capacity(C, w, 1024 + GemvSmem(w, stages, xstride, M, C).total);
+      if (cap <= 0) break;
+      waves = (nq + cap - 1) / cap;
+      if (waves == 1 || it == 1) break;
+      nq = cap;  // one wave of the clusters that fit, with more tiles each
+    }
+    if (w <= 0 || stages <= 0) continue;
+    const double cost = (double)(ws.K / C) * (w + 0.16 * M) * waves * (1.0 + 0.01 * (waves - 1));
+    if (bestC == 0 || cost < best_cost) {
+      bestC = C;
+      bestW = w;
+      bestNq = nq;
+      bestS = stages;
+      best_cost = cost;
+    }
+  }
+  if (bestC == 0) return cudaErrorInvalidValue;
+  a.ks = ws.K / bestC;
+  a.xstride = 2 * a.ks + 64;
+  a.stages = bestS;
+  CUtensorMap tm[4];
+  for (int i = 0; i < 2; ++i) {
+    const int rows = 16 * (bestW - i > 0 ? bestW - i : 1);
+    if (!make_tmap_2d(&tm[2 * i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.w, a.N, a.K / 2, a.K / 2,
+                      kGvChunk / 2, rows, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_tmap_2d(&tm[2 * i + 1], CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.sf, a.N, a.K / kGroup,
+                      a.K / kGroup, kGvChunk / kGroup, rows, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return cudaErrorInvalidValue;
+  }
+  const size_t smem = 1024 + (size_t)GemvSmem(bestW, a.stages, a.xstride, M, bestC).total;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(bestC, bestNq, 1);
+  cfg.blockDim = dim3(32 * (bestW + 1), 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = bestC;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, gemv_kernel, tm[0], tm[1], tm[2], tm[3], a);
+}
+
+}  // namespace nvfp4

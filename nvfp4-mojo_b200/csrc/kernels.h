@@ -85,12 +85,22 @@ struct SkinnyArgs {
 };
 cudaError_t launch_skinny(const SkinnyArgs &a, cudaStream_t s);
 
+// Decode GEMV for M <= 8 tokens (token-major bf16 x, K % 256 == 0, 32-byte
+// aligned weights, 4-byte aligned blockscales, 16-byte aligned x rows).
+bool gemv_supported(int M, int K, const void *w, const void *sf, const void *x, int64_t x_ld);
+cudaError_t launch_gemv(const WeightSpec &ws, const AlphaSpec &al, const uint16_t *x,
+                        int64_t x_ld, void *y, int y_dtype, int64_t y_ld, int M,
+                        cudaStream_t st);
+
 // tcgen05 W4A16 GEMM (token-major x [M, K] bf16 with row stride x_ld).
 bool tc_gemm_supported(int K, const void *w, const void *x, int64_t x_ld);
 cudaError_t launch_w4a16_tc(const WeightSpec &ws, const AlphaSpec &al, const uint16_t *x,
                             int64_t x_ld, void *y, int y_dtype, int64_t y_ld, int M,
                             cudaStream_t st);
-// Returns and clears the device status word of the tensor-core kernels.
+// Return and clear the device status word of the tensor-core GEMM, the
+// decode GEMV and the grouped MoE tensor-core kernels (-1: not readable).
 int read_gemm_device_status();
+int read_gemv_device_status();
+int read_moe_tc_device_status();
 
 }  // namespace nvfp4

@@ -380,4 +380,11 @@ bool moe_tc_supported(int H, int I) {
 
 int moe_tc_rows_per_item() { return kMtBN; }
 
+int read_moe_tc_device_status() {
+  int v = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&v, g_moe_tc_status, sizeof(int)) != cudaSuccess) return -1;
+  if (v) cudaMemcpyToSymbol(g_moe_tc_status, &zero, sizeof(int));
+  return v;
+}
+
 }  // namespace nvfp4

@@ -65,6 +65,13 @@ static int run_linear(const WeightSpec &ws, const AlphaSpec &al, const void *x, 
     return check_launch(launch_w4a16_tc(ws, al, reinterpret_cast<const uint16_t *>(x), xs_m, y,
                                         y_dt, ys_m, (int)M, st),
                         "tcgen05 GEMM launch");
+  // M <= 8: the decode GEMV (f16 tensor-core MMAs fed by hardware FP4 / FP8
+  // conversions, K split across a thread-block cluster).
+  if (!force_f32 && token_major && x_dt == kBF16 &&
+      gemv_supported((int)M, ws.K, ws.w, ws.sf, x, xs_m))
+    return check_launch(launch_gemv(ws, al, reinterpret_cast<const uint16_t *>(x), xs_m, y, y_dt,
+                                    ys_m, (int)M, st),
+                        "decode GEMV launch");
   if (!force_f32 && skinny_ok && (M <= 64 || !tc_ok || (flags & NVFP4_FLAG_FORCE_SKINNY))) {
     SkinnyArgs a;
     a.ws = ws;
@@ -178,8 +185,13 @@ extern "C" int nvfp4_dequant_tile(const uint8_t *w, const uint8_t *sf, float *ou
 }
 
 extern "C" int nvfp4_device_status(void) {
-  const int v = read_gemm_device_status();
-  if (v < 0) return fail(NVFP4_ERR_CUDA, "could not read the device status word");
+  const int words[3] = {read_gemm_device_status(), read_gemv_device_status(),
+                        read_moe_tc_device_status()};
+  int v = 0;
+  for (int w : words) {
+    if (w < 0) return fail(NVFP4_ERR_CUDA, "could not read the device status word");
+    if (!v) v = w;
+  }
   return v;
 }
 

@@ -109,7 +109,7 @@ def test_config0_fp32_linear_and_matvec(O, cuda):
 @pytest.mark.parametrize("K,N", [(2048, 1536), (768, 2048), (4096, 14336)])
 @pytest.mark.parametrize("M", [1, 2, 4, 8])
 def test_decode_gemv_sweep(O, cuda, K, N, M):
-    """Decode GEMV sweep: bf16 x, tensor-core skinny path, fp32 and bf16 out."""
+    """Decode GEMV sweep: bf16 x, the M <= 8 decode path, fp32 and bf16 out."""
     import nvfp4
     from nvfp4 import synthetic
 
@@ -124,6 +124,52 @@ def test_decode_gemv_sweep(O, cuda, K, N, M):
     # Exact decode + fp32 accumulation: only summation order differs.
     assert rel_err(y32.cpu().numpy(), ref) <= 1e-5
     assert rel_err(ybf.float().cpu().numpy(), ref) <= TOL_BF16
+
+
+@pytest.mark.parametrize("N,K,M", [(100, 512, 1), (100, 512, 3), (136, 768, 8), (64, 256, 5),
+                                   (1000, 4096, 7), (24, 2048, 2)])
+def test_decode_gemv_shapes(O, cuda, N, K, M):
+    """Decode GEMV (M <= 8, K % 256 == 0): ragged N, K slices of 1 to 8 chunks
+    per cluster rank; fp32 and bf16 outputs, scalar alpha."""
+    import nvfp4
+    from nvfp4 import synthetic
+
+    wd = synthetic.linear_weights(N, K, seed=N + K + M)
+    x = synthetic.bf16_round(synthetic.activations(M, K, seed=M + 3))
+    lin = nvfp4.NvFp4Linear(K, N, input_scale=0.75, weight_scale_2=0.004)
+    W, SF, X = dev(wd["w"]), dev(wd["sf"]), dev(x, torch.bfloat16)
+    y32 = torch.full((M, N), float("nan"), dtype=torch.float32, device=cuda)
+    nvfp4.nvfp4_linear_forward(lin, W, SF, X, y32, M)
+    ybf = nvfp4.nvfp4_linear(lin, W, SF, X)
+    ref = O.linear(wd["w"], wd["sf"], x, input_scale=0.75, ws2=0.004)
+    assert not torch.isnan(y32).any()
+    assert rel_err(y32.cpu().numpy(), ref) <= 1e-5
+    assert rel_err(ybf.float().cpu().numpy(), ref) <= TOL_BF16
+
+
+def test_decode_gemv_activation_range(O, cuda):
+    """Per-token power-of-two scaling of the f16 activations: tokens far
+    outside the f16 range (|x| ~ 1e30, 1e-30), an all-zero token, and
+    ordinary ones in one call, each exact to fp32 summation order."""
+    import nvfp4
+    from nvfp4 import synthetic
+
+    N, K = 96, 1024
+    scales = [1.0, 1e30, 1e-30, 0.0, 3e4, 1e-6]
+    M = len(scales)
+    wd = synthetic.linear_weights(N, K, seed=77)
+    x = synthetic.activations(M, K, seed=78) * np.asarray(scales, np.float32)[:, None]
+    x = synthetic.bf16_round(x)
+    lin = nvfp4.NvFp4Linear(K, N)
+    y = torch.empty((M, N), dtype=torch.float32, device=cuda)
+    nvfp4.nvfp4_linear_forward(lin, dev(wd["w"]), dev(wd["sf"]), dev(x, torch.bfloat16), y, M)
+    y = y.cpu().numpy()
+    ref = O.linear(wd["w"], wd["sf"], x)
+    for t, sc in enumerate(scales):
+        if sc == 0.0:
+            assert (y[t] == 0).all()
+        else:
+            assert rel_err(y[t], ref[t]) <= 1e-5, (t, sc)
 
 
 @pytest.mark.parametrize("M", [3, 13, 17, 33, 64])
