@@ -86,7 +86,8 @@ const char *nvfp4_last_error_string(void);
 /*
  * Status word of the tensor-core kernels, read (synchronously) and cleared:
  * 0 = no failure; > 0 = a kernel abandoned a bounded wait (1 TMA stage,
- * 2 decoded operands, 3 stage release, 4 accumulator) and returned early,
+ * 2 decoded operands or blockscales, 3 stage release, 4 accumulator) and
+ * returned early,
  * its output then being undefined; < 0 = the status could not be read.
  * No reference counterpart (the reference has no GPU kernel that runs).
  */
@@ -98,14 +99,41 @@ int nvfp4_device_status(void);
  * activations [batch_seq_len, in_features] (act_dtype bf16 or f32), output
  * [batch_seq_len, out_features] (out_dtype bf16 or f32): token-major, as the
  * reference's docstring states (:203-206).
- * Dispatch: M <= 64 tokens -> tensor-core decode GEMV (HBM-bound), larger M ->
- * tcgen05 W4A16 GEMM; fp32 activations with M <= 8 -> the CUDA-core fp32 path
- * (nvfp4_matvec arithmetic).  NVFP4_FLAG_W4A4 -> block-scaled FP4 MMA.
+ * Dispatch: M <= 8 tokens -> decode GEMV, M <= 64 -> tensor-core skinny GEMM
+ * (both HBM-bound), larger M -> tcgen05 W4A16 GEMM; fp32 activations -> the
+ * CUDA-core fp32 path (nvfp4_matvec arithmetic).  NVFP4_FLAG_W4A4 -> the
+ * activations are quantized to NVFP4 with input_scale (nvfp4_quantize_act,
+ * into stream-ordered scratch from cudaMallocAsync) and multiplied on the
+ * block-scaled FP4 tensor cores (nvfp4_linear_w4a4); in_features % 256 == 0.
  */
 int nvfp4_linear_forward(const nvfp4_linear_desc *linear, const uint8_t *packed_weights,
                          const uint8_t *blockscales, const void *activations,
                          int act_dtype, void *output, int out_dtype,
                          int64_t batch_seq_len, uint32_t flags, void *stream);
+
+/*
+ * W4A4 activation quantizer (no reference counterpart: the reference stores
+ * input_scale, nvfp4/weight_loader.mojo:713-758, but never quantizes
+ * activations).  x [M, K] (x_dtype bf16 or f32, row stride x_ld elements,
+ * 16-byte aligned rows) -> codes [M, K/2] (E2M1, low nibble = even k) and
+ * blockscales [M, K/16] (E4M3): per 16-group, sf = e4m3(amax / (6 *
+ * input_scale)), code = e2m1(x / (float(sf) * input_scale)), both
+ * round-to-nearest-even with saturation; a zero scale gives zero codes.
+ */
+int nvfp4_quantize_act(const void *x, int x_dtype, int64_t M, int64_t K, int64_t x_ld,
+                       float input_scale, uint8_t *codes, uint8_t *scales, void *stream);
+
+/*
+ * W4A4 GEMM on the block-scaled FP4 tensor cores (tcgen05 kind::mxf4nvf4):
+ * y[M, N] = input_scale * weight_scale_2[n] * sum_k W~[n, k] * X~[m, k],
+ * W~ / X~ = e2m1 code * e4m3 blockscale of the weights / of the activations
+ * from nvfp4_quantize_act; fp32 accumulation; y token-major (bf16 or f32).
+ * in_features % 256 == 0; all buffers 16-byte aligned.
+ */
+int nvfp4_linear_w4a4(const nvfp4_linear_desc *linear, const uint8_t *packed_weights,
+                      const uint8_t *blockscales, const uint8_t *act_codes,
+                      const uint8_t *act_scales, void *output, int out_dtype, int64_t M,
+                      void *stream);
 
 /*
  * Replaces nvfp4_gemm_kernel (nvfp4/nvfp4_gemm_gpu.mojo:99-182) in the

@@ -98,9 +98,19 @@ cudaError_t launch_w4a16_tc(const WeightSpec &ws, const AlphaSpec &al, const uin
                             int64_t x_ld, void *y, int y_dtype, int64_t y_ld, int M,
                             cudaStream_t st);
 // Return and clear the device status word of the tensor-core GEMM, the
-// decode GEMV and the grouped MoE tensor-core kernels (-1: not readable).
+// decode GEMV, the grouped MoE tensor-core kernels and the W4A4 GEMM
+// (-1: not readable).
 int read_gemm_device_status();
 int read_gemv_device_status();
 int read_moe_tc_device_status();
+int read_w4a4_device_status();
+
+// W4A4: activation quantizer and block-scaled FP4 GEMM (tcgen05 mxf4nvf4).
+cudaError_t launch_quantize_act(const void *x, int x_dtype, int64_t x_ld, int64_t M, int64_t K,
+                                float input_scale, uint8_t *q, uint8_t *qsf, cudaStream_t st);
+bool w4a4_supported(int K, const void *w, const void *sf, const void *xq, const void *xsf);
+cudaError_t launch_w4a4_gemm(const WeightSpec &ws, const AlphaSpec &al, const uint8_t *xq,
+                             const uint8_t *xsf, int M, void *y, int y_dtype, int64_t y_ld,
+                             cudaStream_t st);
 
 }  // namespace nvfp4

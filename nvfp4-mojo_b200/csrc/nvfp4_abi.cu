@@ -2,6 +2,7 @@
 //
 // Validation, dispatch and error reporting.  Every compute entry point ends
 // in a CUDA launch on the caller's stream; there is no host compute path.
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <string>
@@ -104,6 +105,75 @@ static int check_weights(const uint8_t *w, const uint8_t *sf, int64_t N, int64_t
   return NVFP4_OK;
 }
 
+extern "C" int nvfp4_quantize_act(const void *x, int x_dt, int64_t M, int64_t K, int64_t x_ld,
+                                  float input_scale, uint8_t *codes, uint8_t *scales,
+                                  void *stream) {
+  if (!valid_dtype(x_dt)) return fail(NVFP4_ERR_INVALID_ARG, "bad dtype");
+  if (M < 0 || K <= 0 || K % NVFP4_GROUP_SIZE || x_ld < K)
+    return fail(NVFP4_ERR_INVALID_ARG, "bad shape M=%lld K=%lld ld=%lld", (long long)M,
+                (long long)K, (long long)x_ld);
+  if (M == 0) return NVFP4_OK;
+  if (!x || !codes || !scales) return fail(NVFP4_ERR_INVALID_ARG, "null pointer");
+  const int esize = x_dt == kBF16 ? 2 : 4;
+  if (!aligned(x, 16) || (x_ld * esize) % 16 || !aligned(codes, 8))
+    return fail(NVFP4_ERR_INVALID_ARG,
+                "activation rows must be 16-byte aligned and codes 8-byte aligned");
+  if (!(input_scale > 0.0f) || !isfinite(input_scale))
+    return fail(NVFP4_ERR_INVALID_ARG, "input_scale must be positive and finite");
+  return check_launch(launch_quantize_act(x, x_dt, x_ld, M, K, input_scale, codes, scales,
+                                          static_cast<cudaStream_t>(stream)),
+                      "activation quantizer launch");
+}
+
+extern "C" int nvfp4_linear_w4a4(const nvfp4_linear_desc *lin, const uint8_t *w,
+                                 const uint8_t *sf, const uint8_t *xq, const uint8_t *xsf,
+                                 void *y, int y_dt, int64_t M, void *stream) {
+  if (!lin) return fail(NVFP4_ERR_INVALID_ARG, "null linear descriptor");
+  int rc = check_weights(w, sf, lin->out_features, lin->in_features);
+  if (rc) return rc;
+  if (!valid_dtype(y_dt)) return fail(NVFP4_ERR_INVALID_ARG, "bad dtype");
+  if (M < 0 || M > INT32_MAX) return fail(NVFP4_ERR_INVALID_ARG, "bad token count");
+  if (M == 0) return NVFP4_OK;
+  if (!xq || !xsf || !y) return fail(NVFP4_ERR_INVALID_ARG, "null activation or output pointer");
+  if (!w4a4_supported((int)lin->in_features, w, sf, xq, xsf))
+    return fail(NVFP4_ERR_UNSUPPORTED,
+                "W4A4 GEMM needs in_features %% 256 == 0 and 16-byte aligned operands");
+  WeightSpec ws;
+  ws.w = w;
+  ws.sf = sf;
+  ws.N = (int)lin->out_features;
+  ws.K = (int)lin->in_features;
+  AlphaSpec al;
+  al.input_scale = lin->input_scale;
+  al.ws2 = lin->weight_scale_2;
+  al.ws2_rows = lin->weight_scale_2_rows;
+  return check_launch(launch_w4a4_gemm(ws, al, xq, xsf, (int)M, y, y_dt, ws.N,
+                                       static_cast<cudaStream_t>(stream)),
+                      "W4A4 GEMM launch");
+}
+
+// nvfp4_linear_forward with NVFP4_FLAG_W4A4: quantized activations live in
+// stream-ordered scratch (cudaMallocAsync / cudaFreeAsync on the caller's
+// stream, so the call stays asynchronous and capturable).
+static int run_w4a4_with_scratch(const nvfp4_linear_desc *lin, const uint8_t *w,
+                                 const uint8_t *sf, const void *x, int x_dt, void *y, int y_dt,
+                                 int64_t M, void *stream) {
+  if (M == 0) return NVFP4_OK;
+  const int64_t K = lin->in_features;
+  const size_t codes = (size_t)M * (size_t)(K / 2), scales = (size_t)M * (size_t)(K / 16);
+  const size_t off = (codes + 255) & ~(size_t)255;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  void *buf = nullptr;
+  cudaError_t e = cudaMallocAsync(&buf, off + scales, st);
+  if (e != cudaSuccess) return check_launch(e, "W4A4 activation scratch (cudaMallocAsync)");
+  uint8_t *q = static_cast<uint8_t *>(buf), *qsf = q + off;
+  int rc = nvfp4_quantize_act(x, x_dt, M, K, K, lin->input_scale, q, qsf, stream);
+  if (rc == NVFP4_OK) rc = nvfp4_linear_w4a4(lin, w, sf, q, qsf, y, y_dt, M, stream);
+  e = cudaFreeAsync(buf, st);
+  if (rc == NVFP4_OK && e != cudaSuccess) return check_launch(e, "W4A4 scratch release");
+  return rc;
+}
+
 extern "C" int nvfp4_linear_forward(const nvfp4_linear_desc *lin, const uint8_t *w,
                                     const uint8_t *sf, const void *x, int x_dt, void *y,
                                     int y_dt, int64_t M, uint32_t flags, void *stream) {
@@ -113,8 +183,7 @@ extern "C" int nvfp4_linear_forward(const nvfp4_linear_desc *lin, const uint8_t 
   if (!valid_dtype(x_dt) || !valid_dtype(y_dt)) return fail(NVFP4_ERR_INVALID_ARG, "bad dtype");
   if (M < 0) return fail(NVFP4_ERR_INVALID_ARG, "negative batch_seq_len");
   if (M > 0 && (!x || !y)) return fail(NVFP4_ERR_INVALID_ARG, "null activation or output pointer");
-  if (flags & NVFP4_FLAG_W4A4)
-    return fail(NVFP4_ERR_UNSUPPORTED, "W4A4 mode not available in this build");
+  if (flags & NVFP4_FLAG_W4A4) return run_w4a4_with_scratch(lin, w, sf, x, x_dt, y, y_dt, M, stream);
   WeightSpec ws;
   ws.w = w;
   ws.sf = sf;
@@ -185,8 +254,8 @@ extern "C" int nvfp4_dequant_tile(const uint8_t *w, const uint8_t *sf, float *ou
 }
 
 extern "C" int nvfp4_device_status(void) {
-  const int words[3] = {read_gemm_device_status(), read_gemv_device_status(),
-                        read_moe_tc_device_status()};
+  const int words[4] = {read_gemm_device_status(), read_gemv_device_status(),
+                        read_moe_tc_device_status(), read_w4a4_device_status()};
   int v = 0;
   for (int w : words) {
     if (w < 0) return fail(NVFP4_ERR_CUDA, "could not read the device status word");

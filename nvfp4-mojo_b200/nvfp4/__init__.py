@@ -29,6 +29,8 @@ from .nvfp4_gemm_gpu import (
     nvfp4_gemm_kernel,
     nvfp4_linear,
     nvfp4_linear_forward,
+    nvfp4_linear_w4a4,
+    quantize_act,
 )
 from ._lib import LIB_PATH, Nvfp4Error
 
@@ -37,5 +39,6 @@ __all__ = [
     "compute_effective_scale", "dequant_fp4", "dequant_fp4_simd", "pack_fp4_pair",
     "unpack_fp4_pair", "nvfp4_matvec", "sigmoid", "silu", "BK", "BM", "BN", "WM", "WN",
     "FP8_SCALE_DTYPE", "dequant", "load_and_dequant_fp4_tile", "nvfp4_gemm_kernel",
-    "nvfp4_linear", "nvfp4_linear_forward", "LIB_PATH", "Nvfp4Error",
+    "nvfp4_linear", "nvfp4_linear_forward", "nvfp4_linear_w4a4", "quantize_act", "LIB_PATH",
+    "Nvfp4Error",
 ]

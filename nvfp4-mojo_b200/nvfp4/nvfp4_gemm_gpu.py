@@ -143,8 +143,42 @@ def dequant(packed_weights: torch.Tensor, blockscales: torch.Tensor,
     return out
 
 
+def quantize_act(activations: torch.Tensor, input_scale: float, stream=None):
+    """W4A4 activation quantizer (nvfp4_quantize_act): x [M, K] bf16/fp32 ->
+    (codes uint8 [M, K/2], blockscales uint8 (e4m3 bytes) [M, K/16])."""
+    L = _lib.load()
+    if activations.dtype not in _DT or activations.dim() != 2:
+        raise TypeError("activations must be a 2-D bf16 or fp32 tensor")
+    M, K = activations.shape
+    codes = torch.empty((M, K // 2), dtype=torch.uint8, device=activations.device)
+    scales = torch.empty((M, K // NVFP4_GROUP_SIZE), dtype=torch.uint8,
+                         device=activations.device)
+    rc = L.nvfp4_quantize_act(_dev(activations, "activations"), _DT[activations.dtype], M, K, K,
+                              float(input_scale), _dev(codes, "codes"), _dev(scales, "scales"),
+                              _stream(stream))
+    _lib.check(rc)
+    return codes, scales
+
+
+def nvfp4_linear_w4a4(linear: NvFp4Linear, packed_weights: torch.Tensor,
+                      blockscales: torch.Tensor, act_codes: torch.Tensor,
+                      act_scales: torch.Tensor, output: torch.Tensor, stream=None) -> None:
+    """W4A4 GEMM on the block-scaled FP4 tensor cores (nvfp4_linear_w4a4):
+    output [M, out] = input_scale * ws2 * dequant(W) @ dequant(X)^T."""
+    L = _lib.load()
+    desc = make_desc(linear)
+    M = act_codes.shape[0]
+    if output.dtype not in _DT or output.numel() < M * linear.out_features:
+        raise ValueError("output must be bf16/fp32 with M * out_features elements")
+    rc = L.nvfp4_linear_w4a4(ctypes.byref(desc), _dev(_u8(packed_weights), "packed_weights"),
+                             _dev(_u8(blockscales), "blockscales"), _dev(act_codes, "act_codes"),
+                             _dev(act_scales, "act_scales"), _dev(output, "output"),
+                             _DT[output.dtype], M, _stream(stream))
+    _lib.check(rc)
+
+
 __all__ = [
     "BM", "BN", "BK", "WM", "WN", "FP8_SCALE_DTYPE", "NVFP4_GROUP_SIZE",
     "nvfp4_linear_forward", "nvfp4_linear", "nvfp4_gemm_kernel",
-    "load_and_dequant_fp4_tile", "dequant", "make_desc",
+    "load_and_dequant_fp4_tile", "dequant", "make_desc", "quantize_act", "nvfp4_linear_w4a4",
 ]

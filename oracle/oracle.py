@@ -212,6 +212,16 @@ def quantize_act(x, input_scale):
     return q, s
 
 
+def linear_w4a4(packed, scales, x, input_scale, ws2=1.0, ws2_rows=None, rows=None, cols=None,
+                n_threads=1):
+    """W4A4 linear: x quantized to NVFP4 with input_scale (quantize_act), then
+    y = input_scale * ws2 * dequant(W) @ dequant(Xq)^T in fp32 (linear on
+    the dequantized activations)."""
+    q, s = quantize_act(_f32(x), input_scale)
+    return linear(packed, scales, dequant(q, s), input_scale=input_scale, ws2=ws2,
+                  ws2_rows=ws2_rows, rows=rows, cols=cols, n_threads=n_threads)
+
+
 def router(x, router_w):
     x, r = _f32(x), _f32(router_w)
     T, H = x.shape
