@@ -222,6 +222,7 @@ PREFILL_K, PREFILL_N = 4096, 14336
 class PrefillSweep:
     name = "prefill"
     unit = "TFLOP/s"
+    flags = 0
     workload = ("prefill W4A16 GEMM sweep: bf16 x [M, 4096] ~N(0,1), M in {512, 2048, 8192} x "
                 "NVFP4 W [14336, 4096] (u8 [14336, 2048], e4m3 [14336, 256], fp32 scale_2 "
                 "[14336]); fp32 accumulate, bf16 out; 2*M*N*K flop per GEMM")
@@ -255,13 +256,13 @@ class PrefillSweep:
 
     def run_step(self, i):
         for (lin, W, SF, X, Y, _f, _d) in self.calls[i % self.sets]:
-            self.nvfp4.nvfp4_linear_forward(lin, W, SF, X, Y, X.shape[0])
+            self.nvfp4.nvfp4_linear_forward(lin, W, SF, X, Y, X.shape[0], flags=self.flags)
 
     def run_dominant(self, i):
         n = 0
         for (lin, W, SF, X, Y, _f, dom) in self.calls[i % self.sets]:
             if dom:
-                self.nvfp4.nvfp4_linear_forward(lin, W, SF, X, Y, X.shape[0])
+                self.nvfp4.nvfp4_linear_forward(lin, W, SF, X, Y, X.shape[0], flags=self.flags)
                 n += 1
         return n
 
@@ -278,7 +279,7 @@ class PrefillSweep:
     def e2e_step(self, i):
         for j, (lin, W, SF, X, Y, _f, _d) in enumerate(self.calls[i % self.sets]):
             X.copy_(self.h_x[j], non_blocking=True)
-            self.nvfp4.nvfp4_linear_forward(lin, W, SF, X, Y, X.shape[0])
+            self.nvfp4.nvfp4_linear_forward(lin, W, SF, X, Y, X.shape[0], flags=self.flags)
             self.h_y[j].copy_(Y, non_blocking=True)
 
     def cpu_sample(self, threads, rows=8, cols=256):
@@ -296,6 +297,63 @@ class PrefillSweep:
         desc = (f"{rows} tokens x {cols} output features of the K=4096 GEMM per pass "
                 f"({flop / 1e6:.1f} MFLOP; the oracle's cost is linear in tokens x features)")
         return run, flop / 1e12, desc
+
+
+class PrefillW4A4Sweep(PrefillSweep):
+    """The prefill sweep in W4A4 mode: each call quantizes x to NVFP4 with
+    input_scale = max|x| / (6 * 448) (nvfp4_quantize_act) and multiplies on the
+    block-scaled FP4 tensor cores; the dominant launch is the GEMM alone, on
+    activations quantized beforehand."""
+
+    name = "prefill_w4a4"
+    dtype = "fp4 e2m1 x e2m1, e4m3 block scales, fp32 accumulate"
+    workload = ("prefill W4A4 GEMM sweep: bf16 x [M, 4096] ~N(0,1), M in {512, 2048, 8192}, "
+                "quantized to NVFP4 each call with input_scale = max|x|/(6*448) x NVFP4 W "
+                "[14336, 4096] (u8 [14336, 2048], e4m3 [14336, 256], fp32 scale_2 [14336]); "
+                "block-scaled FP4 MMA, fp32 accumulate, bf16 out; 2*M*N*K flop per GEMM")
+
+    def __init__(self, device, seed=0):
+        import nvfp4
+
+        super().__init__(device, seed)
+        self.flags = nvfp4._lib.FLAG_W4A4
+        self.config["workload"] = self.workload
+        self.quant = []
+        for calls in self.calls:
+            q = []
+            for (lin, W, SF, X, Y, _f, dom) in calls:
+                lin.input_scale = float(X.float().abs().max().item() / (6 * 448))
+                if dom:
+                    q.append(nvfp4.quantize_act(X, lin.input_scale))
+            self.quant.append(q)
+        self.dominant_name = "w4a4_gemm_kernel (tcgen05 mxf4nvf4, M=8192 K=4096 N=14336)"
+        self.peak_scale = 4.0  # dense FP4 = 4 x dense BF16
+
+    def cpu_sample(self, threads, rows=8, cols=256):
+        from nvfp4 import synthetic
+        from oracle import oracle as O
+
+        K = PREFILL_K
+        wd = synthetic.linear_weights(cols, K, seed=5)
+        x = synthetic.activations(rows, K, seed=6)
+        ins = float(abs(x).max() / (6 * 448))
+
+        def run():
+            O.linear_w4a4(wd["w"], wd["sf"], x, ins, ws2_rows=wd["ws2"], n_threads=threads)
+
+        flop = 2.0 * rows * cols * K
+        desc = (f"{rows} tokens x {cols} output features of the K=4096 W4A4 GEMM per pass "
+                f"(activation quantization included; {flop / 1e6:.1f} MFLOP)")
+        return run, flop / 1e12, desc
+
+    def run_dominant(self, i):
+        n = 0
+        for (lin, W, SF, X, Y, _f, dom) in self.calls[i % self.sets]:
+            if dom:
+                q, s = self.quant[i % self.sets][0]
+                self.nvfp4.nvfp4_linear_w4a4(lin, W, SF, q, s, Y)
+                n += 1
+        return n
 
 
 # ---------------------------------------------------------------------------
@@ -474,8 +532,8 @@ def synthetic_local_experts(epr, seed, device):
     return d
 
 
-WORKLOADS = {"gemv": GemvSweep, "prefill": PrefillSweep, "moe": MoELayerBench,
-             "ep": EPStackBench}
+WORKLOADS = {"gemv": GemvSweep, "prefill": PrefillSweep, "prefill_w4a4": PrefillW4A4Sweep,
+             "moe": MoELayerBench, "ep": EPStackBench}
 
 
 # ---------------------------------------------------------------------------
@@ -682,13 +740,17 @@ def main():
         traffic = load_traffic(wl.name)
         if getattr(wl, "bound", "hbm") == "tensor":
             achieved = wl.dominant_bytes / (dom_ms / 1e3) / 1e12
-            roof = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
-                    "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
+            scale = getattr(wl, "peak_scale", 1.0)
+            peak = peaks["bf16_tflops"] * scale
+            src = (f"{peaks['source']} (MEASURED_PEAKS.json bf16_tflops, cuBLAS bf16 burst)"
+                   if scale == 1.0 else
+                   f"{scale:g} x {peaks['source']} bf16_tflops (MEASURED_PEAKS.json, cuBLAS bf16 "
+                   f"burst): dense FP4 is {scale:g} x dense BF16 on B200; no FP4 peak is measured")
+            roof = {"bound": "tensor", "achieved": achieved, "peak": peak,
+                    "unit": "TFLOP/s", "frac": achieved / peak,
                     "traffic": traffic, "kernel": wl.dominant_name,
                     "algorithmic_flop_per_launch": wl.dominant_bytes,
-                    "avg_launch_us": dom_ms * 1e3,
-                    "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json bf16_tflops, "
-                                   "cuBLAS bf16 burst)"}
+                    "avg_launch_us": dom_ms * 1e3, "peak_source": src}
         else:
             achieved = wl.dominant_bytes / (dom_ms / 1e3) / 1e9
             roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -712,7 +774,7 @@ def main():
             "metric": METRIC, "value": value, "unit": wl.unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
             "higher_is_better": True, "scaling": getattr(wl, "scaling", "weak"),
-            "vs_baseline": None, "dtype": "bf16",
+            "vs_baseline": None, "dtype": getattr(wl, "dtype", "bf16"),
             "data": "synthetic", "config": dict({"parallelism": (
                 "replicas" if world > 1 else "single GPU")}, **wl.config, graph=bool(graphs)),
             "roofline": roof, "cpu_baseline": cpu,
