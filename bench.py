@@ -17,6 +17,7 @@ the GEMV does not shard, so each rank runs an independent replica.
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import math
 import os
@@ -357,6 +358,91 @@ class PrefillW4A4Sweep(PrefillSweep):
 
 
 # ---------------------------------------------------------------------------
+# Workload: dequant microbenchmark in the shape of the reference's
+# bench_nvfp4.mojo (element counts 1024 .. 1048576, fp32 output), plus the
+# [14336, 4096] prefill weight as the large, HBM-bound case.
+# ---------------------------------------------------------------------------
+DEQ_SIZES = [1024, 4096, 16384, 65536, 262144, 1048576]
+DEQ_ROW = 1024  # elements per row for the small sizes
+
+
+class DequantBench:
+    name = "dequant"
+    unit = "Gelem/s"
+    workload = ("NVFP4 dequant to fp32 (LUT * e4m3 blockscale): element counts 1024, 4096, "
+                "16384, 65536, 262144, 1048576 as in bench_nvfp4.mojo, plus the [14336, 4096] "
+                "prefill weight; nibbles uniform, e4m3 scales U(0.25, 4)")
+
+    def __init__(self, device, seed=0):
+        import torch
+        import nvfp4
+        from nvfp4 import synthetic
+
+        self.torch, self.nvfp4 = torch, nvfp4
+        self.sets = 2
+        self.calls = []
+        shapes = [(n // DEQ_ROW, DEQ_ROW) for n in DEQ_SIZES] + [(PREFILL_N, PREFILL_K)]
+        for s in range(self.sets):
+            calls = []
+            for (rows, K) in shapes:
+                wd = synthetic.linear_weights_cuda(rows, K, seed=seed + 13 * s + rows, device=device)
+                out = torch.empty((rows, K), dtype=torch.float32, device=device)
+                calls.append((wd["w"], wd["sf"], out, rows * K, rows == PREFILL_N))
+            self.calls.append(calls)
+        self.elems_per_step = sum(c[3] for c in self.calls[0])
+        self.launches_per_step = len(shapes)
+        # HBM bytes per element: 0.5 packed + 1/16 e4m3 scale + 4 fp32 out.
+        self.dominant_bytes = PREFILL_N * PREFILL_K * (0.5 + 1.0 / 16 + 4.0)
+        self.dominant_name = "dequant_kernel (fp32 out, [14336, 4096])"
+        self.config = {"workload": self.workload, "sizes": DEQ_SIZES,
+                       "large": [PREFILL_N, PREFILL_K],
+                       "l2": "inputs larger than L2: two sets alternate (2 x 268 MB in + out)"}
+
+    def run_step(self, i):
+        for (w, sf, out, _n, _d) in self.calls[i % self.sets]:
+            self.nvfp4.dequant(w, sf, out=out)
+
+    def run_dominant(self, i):
+        n = 0
+        for (w, sf, out, _n, dom) in self.calls[i % self.sets]:
+            if dom:
+                self.nvfp4.dequant(w, sf, out=out)
+                n += 1
+        return n
+
+    def units(self, steps):
+        return self.elems_per_step * steps / 1e9
+
+    def e2e_setup(self):
+        torch = self.torch
+        self.h_w = [c[0].cpu().pin_memory() for c in self.calls[0]]
+        self.h_out = [torch.empty(c[2].shape, dtype=torch.float32).pin_memory()
+                      for c in self.calls[0]]
+        self.h2d = sum(t.numel() for t in self.h_w)
+        self.d2h = sum(t.numel() * 4 for t in self.h_out)
+
+    def e2e_step(self, i):
+        for j, (w, sf, out, _n, _d) in enumerate(self.calls[i % self.sets]):
+            w.copy_(self.h_w[j], non_blocking=True)
+            self.nvfp4.dequant(w, sf, out=out)
+            self.h_out[j].copy_(out, non_blocking=True)
+
+    def cpu_sample(self, threads):
+        from nvfp4 import synthetic
+        from oracle import oracle as O
+
+        wd = synthetic.linear_weights(256, PREFILL_K, seed=5)
+
+        def run():
+            O.dequant(wd["w"], wd["sf"])
+
+        n = 256 * PREFILL_K
+        desc = (f"dequant of a [256, 4096] slice per pass ({n / 1e6:.2f} M elements; the "
+                "oracle's cost is linear in elements; single thread)")
+        return run, n / 1e9, desc, 1
+
+
+# ---------------------------------------------------------------------------
 # Workload: one MoE FFN layer (128 experts, top-8, H=2048, I=768).
 # ---------------------------------------------------------------------------
 MOE_E, MOE_K, MOE_H, MOE_I = 128, 8, 2048, 768
@@ -371,6 +457,12 @@ class MoELayerBench:
     name = "moe"
     unit = "tokens/s"
 
+    @staticmethod
+    def describe(tokens, layers=None, world=1):
+        return (f"one MoE FFN layer, 128 experts, top-8 (softmax, renormalised), hidden "
+                f"2048, expert intermediate 768, NVFP4 gate_up [1536, 2048] and down "
+                f"[2048, 768] per expert; T = {tokens} bf16 tokens ~N(0,1)")
+
     def __init__(self, device, seed=0, tokens=4096, layers=4):
         import torch
         from nvfp4 import synthetic
@@ -378,9 +470,7 @@ class MoELayerBench:
 
         self.torch = torch
         self.T = tokens
-        self.workload = (f"one MoE FFN layer, 128 experts, top-8 (softmax, renormalised), hidden "
-                         f"2048, expert intermediate 768, NVFP4 gate_up [1536, 2048] and down "
-                         f"[2048, 768] per expert; T = {tokens} bf16 tokens ~N(0,1)")
+        self.workload = self.describe(tokens)
         # Distinct layers (weights 342 MB each) cycle so that inputs exceed L2.
         self.layers = []
         for l in range(layers):
@@ -443,8 +533,16 @@ class MoELayerBench:
 class EPStackBench:
     name = "ep"
     unit = "tokens/s"
-    graphable = False  # the per-layer slot counts are read on the host (exchange sizes)
+    graphable = False  # set per batch: True with the fixed-capacity exchange
     scaling = "strong"  # the global token batch is fixed; experts and tokens split over GPUs
+
+    @staticmethod
+    def describe(tokens, layers=48, world=1):
+        return (f"{layers}-layer stack of pre-norm MoE blocks h += MoE(RMSNorm(h)) (128 "
+                f"experts, top-8, hidden 2048, intermediate 768, NVFP4 experts; the "
+                f"residual add is fused in the combine); expert-parallel over {world} GPU(s) "
+                f"({MOE_E // world} experts each) with NCCL all-to-all dispatch/combine; "
+                f"{tokens} bf16 tokens ~N(0,1) per step ({tokens // world} per GPU)")
 
     def __init__(self, device, seed=0, tokens=64, layers=48):
         import torch
@@ -460,12 +558,7 @@ class EPStackBench:
         self.T = tokens
         self.T_local = tokens // world
         epr = MOE_E // world
-        self.workload = (f"{layers}-layer stack of pre-norm MoE blocks h += MoE(RMSNorm(h)) (128 "
-                         f"experts, top-8, hidden 2048, intermediate 768, NVFP4 experts; the "
-                         f"residual add is fused in the combine); "
-                         f"expert-parallel over {world} GPU(s) ({epr} experts each) with NCCL "
-                         f"all-to-all dispatch/combine; {tokens} bf16 tokens ~N(0,1) per step "
-                         f"({self.T_local} per GPU)")
+        self.workload = self.describe(tokens, layers, world)
         self.layers = []
         for l in range(layers):
             g = torch.Generator(device=device)
@@ -476,11 +569,16 @@ class EPStackBench:
             local = MoEWeights.from_dict(wd, device)
             self.layers.append(EPMoELayer(local, router, top_k=MOE_K, num_experts=MOE_E))
         self.x = torch.randn((self.T_local, MOE_H), device=device).to(torch.bfloat16)
+        # Fixed-capacity exchange (no host-side counts) for small batches: the
+        # whole step, NCCL calls included, is then replayed from a CUDA graph.
+        self.graphable = self.layers[0].uses_static(self.T_local)
+        self.exchange = "fixed capacity, CUDA graph" if self.graphable else "variable counts"
         self.sets = 1
         self.launches_per_step = layers * 10
         self.dominant_bytes = None
         self.config = {"workload": self.workload, "layers": layers, "global_tokens": tokens,
                        "experts_per_gpu": epr, "parallelism": f"ep{world}",
+                       "exchange": self.exchange,
                        "l2": f"inputs larger than L2: {layers} layers x {342 // world} MB of "
                              f"expert weights per GPU per step"}
 
@@ -518,9 +616,10 @@ class EPStackBench:
         def run():
             O.moe(x, wd, top_k=MOE_K, n_threads=threads)
 
+        n_layers = len(self.layers) if hasattr(self, "layers") else 48
         desc = (f"{n_tok} tokens through one layer, reported per layer-token and divided by "
-                f"the layer count (oracle cost is linear in tokens and layers)")
-        return run, float(n_tok) / len(self.layers), desc
+                f"the layer count {n_layers} (oracle cost is linear in tokens and layers)")
+        return run, float(n_tok) / n_layers, desc
 
 
 def synthetic_local_experts(epr, seed, device):
@@ -533,7 +632,7 @@ def synthetic_local_experts(epr, seed, device):
 
 
 WORKLOADS = {"gemv": GemvSweep, "prefill": PrefillSweep, "prefill_w4a4": PrefillW4A4Sweep,
-             "moe": MoELayerBench, "ep": EPStackBench}
+             "dequant": DequantBench, "moe": MoELayerBench, "ep": EPStackBench}
 
 
 # ---------------------------------------------------------------------------
@@ -595,7 +694,9 @@ def run_reference(args, world, rank):
     cores = O.host_cores()
     # Build only what the CPU sample needs (no GPU use).
     wl = wl_cls.__new__(wl_cls)
-    run, units, desc = wl_cls.cpu_sample(wl, cores)
+    res = wl_cls.cpu_sample(wl, cores)
+    run, units, desc = res[:3]
+    cores = res[3] if len(res) > 3 else cores
     for _ in range(args.warmup):
         run()
     t0 = time.perf_counter()
@@ -603,12 +704,16 @@ def run_reference(args, world, rank):
         run()
     el = time.perf_counter() - t0
     value = units * args.steps / el
+    if hasattr(wl_cls, "describe"):
+        wdesc = wl_cls.describe(args.tokens, args.layers, world)
+    else:
+        wdesc = wl_cls.workload
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": wl_cls.unit,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * el / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": wl_cls.workload, "sample": desc},
+        "config": {"workload": wdesc, "sample": desc},
         "cpu_baseline": {"value": value, "unit": wl_cls.unit, "cores": cores, "kind": "port",
                          "sample": desc},
         "e2e": {"value": value, "unit": wl_cls.unit, "h2d_bytes_per_step": 0,
@@ -662,10 +767,14 @@ def main():
     if not args.no_graph and getattr(wl, "graphable", True):
         graphs = []
         for s in range(getattr(wl, "sets", 1)):
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=stream):
+            graphs.append(torch.cuda.CUDAGraph())
+            with torch.cuda.graph(graphs[-1], stream=stream):
                 wl.run_step(s)
-            graphs.append(g)
+        torch.cuda.synchronize()
+        # A first replay outside the timed region.
+        with torch.cuda.stream(stream):
+            for gi in range(len(graphs)):
+                graphs[gi].replay()
         torch.cuda.synchronize()
 
     # Dominant-kernel launch duration: a CUDA graph holding only the dominant
@@ -691,7 +800,7 @@ def main():
             d1.record(stream)
         torch.cuda.synchronize()
         dom_ms = d0.elapsed_time(d1) / (args.steps * n_dom)
-        del dg
+        del dg, g
 
     barrier(world)
     torch.cuda.synchronize()
@@ -764,10 +873,13 @@ def main():
         from oracle import oracle as O
 
         cores = O.host_cores()
-        run, units, desc = wl.cpu_sample(cores)
+        res = wl.cpu_sample(cores)
+        run, units, desc = res[:3]
+        cores = res[3] if len(res) > 3 else cores
         v, n, el = time_cpu(run, units)
+        extra = ", OpenMP over output rows" if cores > 1 else ""
         cpu = {"value": v, "unit": wl.unit, "cores": cores, "kind": "port",
-               "sample": f"{desc}; {n} passes in {el:.1f} s, OpenMP over output rows"}
+               "sample": f"{desc}; {n} passes in {el:.1f} s{extra}"}
 
     if rank == 0:
         line = {
@@ -786,7 +898,13 @@ def main():
     if world > 1:
         import torch.distributed as dist
 
+        # CUDA graphs that hold NCCL calls must be gone before the process
+        # group is destroyed, or the exit waits for them forever.
+        torch.cuda.synchronize()
         graphs = None
+        wl = None
+        gc.collect()
+        torch.cuda.synchronize()
         dist.destroy_process_group()
     return 0
 

@@ -239,7 +239,10 @@ int nvfp4_moe_forward_noalloc(const nvfp4_moe_desc *desc, const nvfp4_moe_weight
                               int64_t T, int32_t *topk_ids, float *topk_w, void *stream);
 
 /* Router alone: topk_ids int32 [T, k], topk_w fp32 [T, k]; logits fp32
- * [T, E] is caller memory the router writes (and the caller may read). */
+ * [T, E] is caller memory the router writes (and the caller may read).  The
+ * arithmetic is that of nvfp4_moe_forward's router (same logits bit for
+ * bit); its split-H partial sums go to stream-ordered scratch
+ * (cudaMallocAsync on `stream`) when the split is used. */
 int nvfp4_moe_route(const nvfp4_moe_desc *desc, const float *router, const void *x, int64_t T,
                     int32_t *topk_ids, float *topk_w, float *logits, void *stream);
 
@@ -275,6 +278,21 @@ int nvfp4_ep_dispatch_plan(const int32_t *topk_ids, int64_t T, int32_t k,
                            int32_t experts_per_rank, int32_t world, int32_t *send_counts,
                            int32_t *send_token, int32_t *send_expert, int32_t *slot_pos,
                            void *stream);
+
+/*
+ * Fixed-capacity form of the dispatch (after nvfp4_ep_dispatch_plan): lays
+ * the send order out as `world` blocks of `cap` rows (cap >= T*k), block r =
+ * the token rows x[send_token[i]] bound for rank r followed by zero rows;
+ * send_expert_padded [world*cap] = local expert id or -1 for padding;
+ * slot_padded [T*k] = padded position of each slot (-1 if none).  Every
+ * exchange then has the same sizes (cap rows per peer), so a step needs no
+ * host-side count and can be captured in a CUDA graph.
+ */
+int nvfp4_ep_dispatch_padded(const int32_t *send_counts, const int32_t *send_token,
+                             const int32_t *send_expert, const int32_t *slot_pos, int64_t T,
+                             int32_t k, int32_t world, int64_t cap, const void *x,
+                             int64_t row_bytes, void *send_rows, int32_t *send_expert_padded,
+                             int32_t *slot_padded, void *stream);
 
 /* dst[i] = src[row_index[i]] for n rows of row_bytes bytes (multiple of 16). */
 int nvfp4_gather_rows(const void *src, const int32_t *row_index, int64_t n, int64_t row_bytes,

@@ -533,6 +533,78 @@ cudaError_t launch_gather_rows(const void *src, const int32_t *idx, int64_t n, i
 }
 
 // ---------------------------------------------------------------------------
+// Fixed-capacity dispatch: the plan's send order re-laid into `world` blocks
+// of `cap` rows (block r = the rows for rank r, padded with zero rows and
+// expert id -1), so that the exchange has the same sizes on every layer and
+// needs no host-side count (the step can be captured in a CUDA graph).
+// One warp per padded row; slot_pad[s] = padded position of slot s (or -1).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int ep_offset(const int32_t *counts, int r) {
+  int o = 0;
+  for (int q = 0; q < r; ++q) o += counts[q];
+  return o;
+}
+
+__global__ void ep_pad_rows_kernel(const int32_t *__restrict__ counts,
+                                   const int32_t *__restrict__ send_token,
+                                   const int32_t *__restrict__ send_expert, int world, int cap,
+                                   const uint4 *__restrict__ x, int vec, uint4 *__restrict__ out,
+                                   int32_t *__restrict__ out_expert) {
+  const int q = (int)((blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  if (q >= world * cap) return;
+  const int r = q / cap, p = q - r * cap;
+  const int n = min(counts[r], cap);
+  uint4 *dst = out + (int64_t)q * vec;
+  if (p < n) {
+    const int i = ep_offset(counts, r) + p;
+    const uint4 *src = x + (int64_t)send_token[i] * vec;
+    for (int v = lane; v < vec; v += 32) dst[v] = src[v];
+    if (lane == 0) out_expert[q] = send_expert[i];
+  } else {
+    for (int v = lane; v < vec; v += 32) dst[v] = make_uint4(0u, 0u, 0u, 0u);
+    if (lane == 0) out_expert[q] = -1;
+  }
+}
+
+__global__ void ep_slot_pad_kernel(const int32_t *__restrict__ counts,
+                                   const int32_t *__restrict__ slot_pos, int R, int world, int cap,
+                                   int32_t *__restrict__ slot_pad) {
+  const int s = blockIdx.x * blockDim.x + threadIdx.x;
+  if (s >= R) return;
+  const int i = slot_pos[s];
+  int pad = -1;
+  if (i >= 0) {
+    int o = 0;
+    for (int r = 0; r < world; ++r) {
+      const int c = counts[r];
+      if (i < o + c) {
+        if (i - o < cap) pad = r * cap + (i - o);
+        break;
+      }
+      o += c;
+    }
+  }
+  slot_pad[s] = pad;
+}
+
+cudaError_t launch_ep_pad(const int32_t *counts, const int32_t *send_token,
+                          const int32_t *send_expert, const int32_t *slot_pos, int R, int world,
+                          int cap, const void *x, int64_t row_bytes, void *out, int32_t *out_expert,
+                          int32_t *slot_pad, cudaStream_t st) {
+  const int vec = (int)(row_bytes / 16);
+  const int64_t rows = (int64_t)world * cap;
+  if (rows > 0) {
+    ep_pad_rows_kernel<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, st>>>(
+        counts, send_token, send_expert, world, cap, static_cast<const uint4 *>(x), vec,
+        static_cast<uint4 *>(out), out_expert);
+  }
+  if (R > 0)
+    ep_slot_pad_kernel<<<(R + 255) / 256, 256, 0, st>>>(counts, slot_pos, R, world, cap, slot_pad);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
 // Combine: y[t, :] = sum_j w[t, j] * ys[t*k + j, :] (+ residual[t, :]), fp32
 // sums in j order, residual added last, one bf16 rounding at the end.  Slot
 // outputs are fp32 (or bf16).  8 features per thread.

@@ -59,5 +59,9 @@ cudaError_t launch_ep_plan(const int32_t *ids, int R, int k, int epr, int world,
                            cudaStream_t st);
 cudaError_t launch_gather_rows(const void *src, const int32_t *idx, int64_t n, int64_t row_bytes,
                                void *dst, cudaStream_t st);
+cudaError_t launch_ep_pad(const int32_t *counts, const int32_t *send_token,
+                          const int32_t *send_expert, const int32_t *slot_pos, int R, int world,
+                          int cap, const void *x, int64_t row_bytes, void *out, int32_t *out_expert,
+                          int32_t *slot_pad, cudaStream_t st);
 
 }  // namespace nvfp4

@@ -239,11 +239,25 @@ extern "C" int nvfp4_moe_route(const nvfp4_moe_desc *d, const float *router, con
   if (T == 0) return NVFP4_OK;
   if (!router || !x || !ids || !w || !logits)
     return fail(NVFP4_ERR_INVALID_ARG, "null router, activation or output pointer");
-  // The caller's logits buffer holds one slice: a single H slice here.
-  return check_launch(launch_router(static_cast<const uint16_t *>(x), router, logits, 1, nullptr,
-                                    (int)T, d->hidden, d->num_experts, d->top_k, d->renormalize,
-                                    ids, w, static_cast<cudaStream_t>(stream)),
-                      "router launch");
+  // Same H slicing (hence the same logits, bit for bit) as nvfp4_moe_forward:
+  // the per-slice partial sums go to stream-ordered scratch.
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int nslices = router_slices((int)T, d->hidden, d->num_experts);
+  if (nslices == 1)
+    return check_launch(launch_router(static_cast<const uint16_t *>(x), router, logits, 1, nullptr,
+                                      (int)T, d->hidden, d->num_experts, d->top_k,
+                                      d->renormalize, ids, w, st),
+                        "router launch");
+  void *part = nullptr;
+  cudaError_t e = cudaMallocAsync(&part, sizeof(float) * nslices * T * d->num_experts, st);
+  if (e != cudaSuccess) return check_launch(e, "router scratch (cudaMallocAsync)");
+  rc = check_launch(launch_router(static_cast<const uint16_t *>(x), router,
+                                  static_cast<float *>(part), nslices, logits, (int)T, d->hidden,
+                                  d->num_experts, d->top_k, d->renormalize, ids, w, st),
+                    "router launch");
+  e = cudaFreeAsync(part, st);
+  if (rc == NVFP4_OK && e != cudaSuccess) return check_launch(e, "router scratch release");
+  return rc;
 }
 
 extern "C" int nvfp4_moe_experts(const nvfp4_moe_desc *d, const nvfp4_moe_weights *w,
@@ -310,6 +324,29 @@ extern "C" int nvfp4_gather_rows(const void *src, const int32_t *row_index, int6
   return check_launch(launch_gather_rows(src, row_index, n, row_bytes, dst,
                                          static_cast<cudaStream_t>(stream)),
                       "gather launch");
+}
+
+extern "C" int nvfp4_ep_dispatch_padded(const int32_t *send_counts, const int32_t *send_token,
+                                        const int32_t *send_expert, const int32_t *slot_pos,
+                                        int64_t T, int32_t k, int32_t world, int64_t cap,
+                                        const void *x, int64_t row_bytes, void *send_rows,
+                                        int32_t *send_expert_padded, int32_t *slot_padded,
+                                        void *stream) {
+  if (T < 0 || k <= 0 || k > 32 || world <= 0 || world > 64 || cap < 0 || T * k > (1 << 24) ||
+      (int64_t)world * cap > (1 << 24) || row_bytes <= 0 || row_bytes % 16)
+    return fail(NVFP4_ERR_INVALID_ARG, "bad padded-dispatch shape");
+  if (cap < T * k)
+    return fail(NVFP4_ERR_INVALID_ARG, "capacity %lld below the %lld slots of this rank",
+                (long long)cap, (long long)(T * k));
+  if (!send_counts || !send_token || !send_expert || !slot_pos || !send_rows ||
+      !send_expert_padded || !slot_padded || (T > 0 && !x))
+    return fail(NVFP4_ERR_INVALID_ARG, "null padded-dispatch pointer");
+  if (!aligned(x, 16) || !aligned(send_rows, 16))
+    return fail(NVFP4_ERR_INVALID_ARG, "row buffers must be 16-byte aligned");
+  return check_launch(launch_ep_pad(send_counts, send_token, send_expert, slot_pos, (int)(T * k),
+                                    world, (int)cap, x, row_bytes, send_rows, send_expert_padded,
+                                    slot_padded, static_cast<cudaStream_t>(stream)),
+                      "padded dispatch launch");
 }
 
 extern "C" int nvfp4_moe_forward(const nvfp4_moe_desc *d, const nvfp4_moe_weights *w,

@@ -106,6 +106,8 @@ SIGNATURES = {
     "nvfp4_ep_dispatch_plan": (_int, [_vp, _i64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                       _vp, _vp, _vp, _vp, _vp]),
     "nvfp4_gather_rows": (_int, [_vp, _vp, _i64, _i64, _vp, _vp]),
+    "nvfp4_ep_dispatch_padded": (_int, [_vp, _vp, _vp, _vp, _i64, ctypes.c_int32, ctypes.c_int32,
+                                        _i64, _vp, _i64, _vp, _vp, _vp, _vp]),
     "nvfp4_quantize_act": (_int, [_vp, _int, _i64, _i64, _i64, _f32, _vp, _vp, _vp]),
     "nvfp4_linear_w4a4": (_int, [ctypes.POINTER(LinearDesc), _vp, _vp, _vp, _vp, _vp, _int, _i64,
                                  _vp]),

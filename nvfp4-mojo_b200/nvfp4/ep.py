@@ -14,7 +14,8 @@ fp32 router.  Per layer, on every rank:
   7. combine them in slot order with the routing weights (+ residual).
 
 Steps 1, 2, 4 (gather), 5 and 7 are libnvfp4 CUDA kernels; steps 3, 4 and 6
-are NCCL collectives.  The kernel calls go through a backend object so the
+are NCCL collectives.  For small batches the exchange uses fixed capacities
+instead (EPMoELayer.forward_static): no step 3, no host synchronisation.  The kernel calls go through a backend object so the
 exchange logic can be exercised with CPU ranks (gloo) in tests.
 """
 from __future__ import annotations
@@ -69,6 +70,21 @@ class CudaBackend:
         _lib.check(rc)
         return counts, send_token, send_expert, slot_pos
 
+    def pad(self, x, counts, send_token, send_expert, slot_pos, cap, world):
+        """Fixed-capacity send layout: rows [world * cap, H], expert ids
+        [world * cap] (-1 = padding) and the padded position of each slot."""
+        T, H = x.shape
+        k = slot_pos.numel() // max(T, 1)
+        rows = torch.empty((world * cap, H), dtype=x.dtype, device=x.device)
+        rows_e = torch.empty(world * cap, dtype=torch.int32, device=x.device)
+        slot_pad = torch.empty(slot_pos.numel(), dtype=torch.int32, device=x.device)
+        rc = _lib.load().nvfp4_ep_dispatch_padded(
+            _ptr(counts), _ptr(send_token), _ptr(send_expert), _ptr(slot_pos), T, k, world, cap,
+            _ptr(x), H * x.element_size(), _ptr(rows), _ptr(rows_e), _ptr(slot_pad),
+            _stream(None))
+        _lib.check(rc)
+        return rows, rows_e, slot_pad
+
     def gather(self, x, idx):
         out = torch.empty((idx.numel(), x.shape[1]), dtype=x.dtype, device=x.device)
         rc = _lib.load().nvfp4_gather_rows(_ptr(x), _ptr(idx), idx.numel(),
@@ -84,11 +100,21 @@ class CudaBackend:
 
 
 class EPMoELayer:
-    """Expert-parallel MoE layer; `backend` defaults to the CUDA kernels."""
+    """Expert-parallel MoE layer; `backend` defaults to the CUDA kernels.
+
+    Two exchange modes.  Variable (the default for large batches): per-peer
+    slot counts are exchanged and read on the host, and only the routed rows
+    cross NVLink.  Fixed capacity (`static=True`; chosen automatically when
+    world * T * k <= static_rows): every peer gets T * k rows (the most any
+    peer can receive from one rank), padded, so no count is read on the host
+    and a step can be captured in a CUDA graph with its NCCL calls; the
+    padding costs NVLink bytes, not expert compute (padded rows carry expert
+    id -1 and are skipped)."""
 
     def __init__(self, local: Optional[MoEWeights], router: torch.Tensor, top_k: int = 8,
                  num_experts: Optional[int] = None, group=None, backend=None,
-                 renormalize: bool = True):
+                 renormalize: bool = True, static: Optional[bool] = None,
+                 static_rows: int = 8192):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.E = num_experts if num_experts is not None else router.shape[1]
@@ -97,6 +123,13 @@ class EPMoELayer:
         self.epr = self.E // self.world
         self.top_k = top_k
         self.backend = backend or CudaBackend(local, router, top_k, renormalize)
+        self.static = static
+        self.static_rows = static_rows
+
+    def uses_static(self, T: int) -> bool:
+        if self.static is not None:
+            return bool(self.static)
+        return self.world * T * self.top_k <= self.static_rows
 
     def _a2a(self, out, inp, out_splits, in_splits):
         if self.world == 1:
@@ -104,7 +137,27 @@ class EPMoELayer:
             return
         dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
 
+    def forward_static(self, x: torch.Tensor,
+                       residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Fixed-capacity exchange: equal splits of T * k rows per peer."""
+        be = self.backend
+        cap = x.shape[0] * self.top_k
+        ids, tw = be.route(x)
+        counts, send_token, send_expert, slot_pos = be.plan(ids, self.epr, self.world)
+        send_x, send_e, slot_pad = be.pad(x, counts, send_token, send_expert, slot_pos, cap,
+                                          self.world)
+        recv_x = torch.empty_like(send_x)
+        recv_e = torch.empty_like(send_e)
+        self._a2a(recv_x, send_x, None, None)
+        self._a2a(recv_e, send_e, None, None)
+        y_recv = be.experts(recv_x, recv_e)
+        y_send = torch.empty_like(y_recv)
+        self._a2a(y_send, y_recv, None, None)
+        return be.combine(y_send, tw, slot_pad, residual)
+
     def forward(self, x: torch.Tensor, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if self.uses_static(x.shape[0]):
+            return self.forward_static(x, residual)
         be = self.backend
         ids, tw = be.route(x)
         counts, send_token, send_expert, slot_pos = be.plan(ids, self.epr, self.world)

@@ -130,13 +130,18 @@ def load_and_dequant_fp4_tile(packed_weights: torch.Tensor, blockscales: torch.T
 
 
 def dequant(packed_weights: torch.Tensor, blockscales: torch.Tensor,
-            out_dtype=torch.float32, stream=None) -> torch.Tensor:
-    """dequant_fp4 over a whole [rows, K/2] matrix -> [rows, K]."""
+            out_dtype=torch.float32, stream=None, out: torch.Tensor = None) -> torch.Tensor:
+    """dequant_fp4 over a whole [rows, K/2] matrix -> [rows, K] (into `out`
+    when given: fp32 or bf16, rows * K elements)."""
     L = _lib.load()
     w = _u8(packed_weights)
     rows, Kh = w.shape
     K = Kh * NVFP4_PACK_FACTOR
-    out = torch.empty((rows, K), dtype=out_dtype, device=w.device)
+    if out is None:
+        out = torch.empty((rows, K), dtype=out_dtype, device=w.device)
+    elif out.numel() != rows * K or out.dtype not in _DT:
+        raise ValueError("out must hold rows * K fp32 or bf16 elements")
+    out_dtype = out.dtype
     rc = L.nvfp4_dequant(_dev(w, "packed_weights"), _dev(_u8(blockscales), "blockscales"),
                          rows, K, _dev(out, "output"), _DT[out_dtype], _stream(stream))
     _lib.check(rc)

@@ -1,8 +1,10 @@
 """Expert-parallel MoE exchange logic on CPU ranks (torch.distributed gloo,
 world size 2): the EPMoELayer host algorithm (route -> dispatch plan ->
 count / row / expert-id all-to-all -> local experts -> reverse all-to-all ->
-combine in slot order) with a CPU backend whose arithmetic is the oracle's.
-The result must equal the single-process oracle MoE on the same tokens."""
+combine in slot order), in both exchange modes (variable counts, and fixed
+capacity with padded rows), with a CPU backend whose arithmetic is the
+oracle's.  The result must equal the single-process oracle MoE on the same
+tokens."""
 import os
 import socket
 
@@ -44,11 +46,32 @@ class CpuBackend:
     def gather(self, x, idx):
         return x[idx.long()]
 
+    def pad(self, x, counts, send_token, send_expert, slot_pos, cap, world):
+        """Numpy restatement of nvfp4_ep_dispatch_padded."""
+        c = counts.numpy()
+        off = np.concatenate([[0], np.cumsum(c)[:-1]])
+        rows = torch.zeros((world * cap, x.shape[1]), dtype=x.dtype)
+        rows_e = torch.full((world * cap,), -1, dtype=torch.int32)
+        for r in range(world):
+            for p in range(min(int(c[r]), cap)):
+                i = off[r] + p
+                rows[r * cap + p] = x[int(send_token[i])]
+                rows_e[r * cap + p] = send_expert[i]
+        sp = slot_pos.numpy()
+        slot_pad = np.full(sp.shape, -1, np.int32)
+        for s_, i in enumerate(sp):
+            if i >= 0:
+                r = int(np.searchsorted(np.cumsum(c), i, side="right"))
+                slot_pad[s_] = r * cap + (i - off[r])
+        return rows, rows_e, torch.from_numpy(slot_pad)
+
     def experts(self, rows, local_ids):
         O, wd = self.O, self.wd
         out = np.zeros((rows.shape[0], H), np.float32)
         xs = rows.float().numpy()
         for r, le in enumerate(local_ids.numpy()):
+            if le < 0:
+                continue  # padding row
             e = self.lo + int(le)
             h = O.matvec(wd["gu_w"][e], wd["gu_sf"][e], xs[r], ws2_rows=wd["gu_ws2"][e])
             a = np.array([O.silu(float(v)) for v in h[:I]], np.float32) * h[I:]
@@ -65,7 +88,7 @@ class CpuBackend:
         return torch.from_numpy(y)
 
 
-def _worker(rank, world, port, ret):
+def _worker(rank, world, port, static, ret):
     import sys
     from pathlib import Path
 
@@ -84,7 +107,8 @@ def _worker(rank, world, port, ret):
         x_all = synthetic.bf16_round(synthetic.activations(6 * world, H, seed=6))
         x = torch.from_numpy(x_all[6 * rank:6 * (rank + 1)])
         layer = EPMoELayer(None, torch.from_numpy(wd["router"]), top_k=K_TOP, num_experts=E,
-                           backend=CpuBackend(wd, rank, world))
+                           backend=CpuBackend(wd, rank, world), static=static)
+        assert layer.uses_static(x.shape[0]) == static
         y = layer(x).numpy()
         ret[rank] = y.tolist()
     finally:
@@ -99,13 +123,14 @@ def _port():
     return p
 
 
-def test_ep_exchange_matches_single_process_oracle(O):
+@pytest.mark.parametrize("static", [False, True])
+def test_ep_exchange_matches_single_process_oracle(O, static):
     from nvfp4 import synthetic
 
     world = 2
     mgr = mp.Manager()
     ret = mgr.dict()
-    mp.spawn(_worker, args=(world, _port(), ret), nprocs=world, join=True)
+    mp.spawn(_worker, args=(world, _port(), static, ret), nprocs=world, join=True)
     wd = synthetic.moe_weights(E, H, I, seed=5)
     x_all = synthetic.bf16_round(synthetic.activations(6 * world, H, seed=6))
     ref, _, _ = O.moe(x_all, wd, top_k=K_TOP)

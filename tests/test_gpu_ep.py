@@ -1,7 +1,9 @@
 """Expert-parallel MoE on 2 GPUs (NCCL all-to-all over NVLink) against the
 single-GPU layer: every row an expert computes is the same arithmetic in
 both, and the combine sums in the same slot order, so the outputs must be
-bitwise equal.  Skipped on a host with fewer than 2 GPUs."""
+bitwise equal.  Both exchange modes; the fixed-capacity one also replayed
+from a CUDA graph that holds its NCCL calls.  Skipped on a host with fewer
+than 2 GPUs."""
 import os
 import socket
 
@@ -15,7 +17,7 @@ pytestmark = pytest.mark.gpu
 E, H, I, K_TOP, T_RANK = 16, 256, 128, 4, 40
 
 
-def _worker(rank, world, port, ret):
+def _worker(rank, world, port, static, ret):
     import datetime
     import sys
     from pathlib import Path
@@ -41,10 +43,20 @@ def _worker(rank, world, port, ret):
         local = MoEWeights.from_dict({k: (v[sl] if k != "router" else v) for k, v in wd.items()})
         x_all = synthetic.bf16_round(synthetic.activations(T_RANK * world, H, seed=12))
         x = torch.from_numpy(x_all[T_RANK * rank:T_RANK * (rank + 1)]).cuda().to(torch.bfloat16)
-        layer = EPMoELayer(local, local.router, top_k=K_TOP, num_experts=E)
+        layer = EPMoELayer(local, local.router, top_k=K_TOP, num_experts=E, static=static)
         y = layer(x)
         torch.cuda.synchronize()
         ret[rank] = y.view(torch.int16).cpu().numpy().tolist()
+        if static:
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                yg = layer(x)
+            g.replay()
+            torch.cuda.synchronize()
+            ret[f"graph{rank}"] = bool(torch.equal(yg, y))
+            del g
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -58,7 +70,8 @@ def _port():
     return p
 
 
-def test_ep_two_gpus_equals_single_gpu(cuda):
+@pytest.mark.parametrize("static", [False, True])
+def test_ep_two_gpus_equals_single_gpu(cuda, static):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     from nvfp4 import synthetic
@@ -67,7 +80,9 @@ def test_ep_two_gpus_equals_single_gpu(cuda):
     world = 2
     mgr = mp.get_context("spawn").Manager()
     ret = mgr.dict()
-    mp.spawn(_worker, args=(world, _port(), ret), nprocs=world, join=True)
+    mp.spawn(_worker, args=(world, _port(), static, ret), nprocs=world, join=True)
+    if static:
+        assert ret["graph0"] and ret["graph1"]
     wd = synthetic.moe_weights(E, H, I, seed=11)
     x_all = synthetic.bf16_round(synthetic.activations(T_RANK * world, H, seed=12))
     layer = MoELayer(MoEWeights.from_dict(wd), top_k=K_TOP)
