@@ -59,19 +59,6 @@ static __device__ int g_gemv_status;  // DeviceStatus of the last failing CTA
 constexpr int kGvChunk = 256;  // k per row chunk (128 bytes of codes)
 constexpr int kGvTok = 8;      // tokens per MMA (n = 8)
 
-__device__ __forceinline__ void ldg_v8(const uint8_t *p, uint32_t (&r)[8]) {
-  asm("ld.global.nc.L1::no_allocate.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7])
-      : "l"(p));
-}
-
-__device__ __forceinline__ uint32_t ldg_u32(const uint8_t *p) {
-  uint32_t v;
-  asm("ld.global.nc.L1::no_allocate.b32 %0, [%1];" : "=r"(v) : "l"(p));
-  return v;
-}
-
 // Four f16x2 from the four bytes of w: d_i = (lo: low nibble, hi: high nibble of byte i).
 __device__ __forceinline__ void e2m1x8_to_f16x2(uint32_t w, uint32_t (&d)[4]) {
   asm("{\n"
@@ -119,19 +106,33 @@ __device__ __forceinline__ float *cluster_map(float *p, int rank) {
 // Physical 16-byte unit of logical unit u in a token row of x (XOR swizzle).
 __device__ __forceinline__ int xs_unit(int u) { return u ^ ((u >> 3) & 3); }
 
+// Kernel modes: the plain linear, and the two grouped MoE expert GEMMs over
+// work items (expert, up to 8 token slots) from the MoE permutation.
+enum GemvMode : int {
+  kGvPlain = 0,
+  kGvGateUp = 1,  // W = [gate; up] rows of the expert, out = silu(gate) * up, bf16 hi + lo
+  kGvDown = 2,    // x = bf16 hi + lo parts (two f16 B operands), out rows scattered
+};
+
 struct GemvArgs {
   const uint8_t *w;
   const uint8_t *sf;
   AlphaSpec al;
   const uint16_t *x;
+  const uint16_t *x_lo;  // kGvDown: low parts of x
   int64_t x_ld;
   void *y;
+  uint16_t *y_lo;        // kGvGateUp: low parts of the output
   int y_dtype;
   int64_t y_ld;
-  int M, N, K;
-  int ks;       // K per CTA (multiple of kGvChunk)
-  int xstride;  // bytes per token row of the f16 x slice in shared memory
-  int stages;   // TMA ring stages
+  int M, N, K;           // N: rows of one weight matrix (an expert's, in grouped modes)
+  int ks;                // K per CTA (multiple of kGvChunk)
+  int xstride;           // bytes per token row of the f16 x slice in shared memory
+  int stages;            // TMA ring stages
+  const SkinnyWork *work;  // grouped modes: items (expert, first slot, slots <= 8)
+  const int *n_work;
+  const int32_t *x_rows;   // kGvGateUp: slot -> activation row
+  const int32_t *y_rows;   // kGvDown: slot -> output row
 };
 
 // Consumer view of one staged chunk: codes of rows g and g+8 of the warp's
@@ -156,8 +157,10 @@ __device__ __forceinline__ void gemv_fetch(GemvChunk &b, uint32_t codes, uint32_
   b.sh = lds_u32(scales + 16u * (rl + 8) + 4u * c);
 }
 
+// One 256-k chunk of a warp's tile; SPLIT adds the MMAs of the low parts.
+template <bool SPLIT>
 __device__ __forceinline__ void gemv_compute(const GemvChunk &b, float (&acc)[4], uint32_t xrow,
-                                             bool has_x, int ch, int c) {
+                                             uint32_t xrow_lo, bool has_x, int ch, int c) {
   // This lane's x units for the chunk: logical 32*ch + 8c + p, p = 0..7.
   const int ub = 32 * ch + 8 * c;
 #pragma unroll
@@ -166,15 +169,22 @@ __device__ __forceinline__ void gemv_compute(const GemvChunk &b, float (&acc)[4]
 #pragma unroll
     for (int p4 = 0; p4 < 4; ++p4) {  // code word p = 4hh + p4: MMAs j = 2p, 2p+1
       const int p = 4 * hh + p4, hi = p4 >> 1;  // blockscale q = p / 2 = 2hh + hi
-      const uint4 xv = has_x ? lds_v4(xrow + 16u * (uint32_t)xs_unit(ub + p))
-                             : make_uint4(0u, 0u, 0u, 0u);
+      const uint32_t xo = 16u * (uint32_t)xs_unit(ub + p);
+      const uint4 xv = has_x ? lds_v4(xrow + xo) : make_uint4(0u, 0u, 0u, 0u);
       uint32_t dg[4], dh[4];
       e2m1x8_to_f16x2(b.wg[p], dg);
       e2m1x8_to_f16x2(b.wh[p], dh);
-      mma_f16_16816(acc, hmul2_bcast(dg[0], s_g, hi), hmul2_bcast(dh[0], s_h, hi),
-                    hmul2_bcast(dg[1], s_g, hi), hmul2_bcast(dh[1], s_h, hi), xv.x, xv.y);
-      mma_f16_16816(acc, hmul2_bcast(dg[2], s_g, hi), hmul2_bcast(dh[2], s_h, hi),
-                    hmul2_bcast(dg[3], s_g, hi), hmul2_bcast(dh[3], s_h, hi), xv.z, xv.w);
+      const uint32_t a0 = hmul2_bcast(dg[0], s_g, hi), a1 = hmul2_bcast(dh[0], s_h, hi);
+      const uint32_t a2 = hmul2_bcast(dg[1], s_g, hi), a3 = hmul2_bcast(dh[1], s_h, hi);
+      const uint32_t a4 = hmul2_bcast(dg[2], s_g, hi), a5 = hmul2_bcast(dh[2], s_h, hi);
+      const uint32_t a6 = hmul2_bcast(dg[3], s_g, hi), a7 = hmul2_bcast(dh[3], s_h, hi);
+      mma_f16_16816(acc, a0, a1, a2, a3, xv.x, xv.y);
+      mma_f16_16816(acc, a4, a5, a6, a7, xv.z, xv.w);
+      if constexpr (SPLIT) {
+        const uint4 xl = has_x ? lds_v4(xrow_lo + xo) : make_uint4(0u, 0u, 0u, 0u);
+        mma_f16_16816(acc, a0, a1, a2, a3, xl.x, xl.y);
+        mma_f16_16816(acc, a4, a5, a6, a7, xl.z, xl.w);
+      }
     }
   }
 }
@@ -186,48 +196,61 @@ constexpr int kGvMaxKs = 2048;     // K per CTA (f16 x slice in shared memory)
 constexpr int kGvSmemCap = 110 * 1024;  // dynamic shared memory per CTA (two per SM)
 
 // Shared memory of a CTA with `w` consumer warps, `stages` ring stages, `m`
-// token rows of x and a K split of `cs`: the ring, the f16 x slice, the
-// receive buffer of the cluster reduction ([cs][per rows][8 tokens] fp32,
-// per = ceil(16 w / cs)), per-token scales and exponents, alpha of the rows
+// token rows of x (twice for hi + lo), a K split of `cs` and `parts` partial
+// sums per owned row (2 for gate + up): the ring, the f16 x slice(s), the
+// receive buffer of the cluster reduction ([cs][per][parts][8] fp32, per =
+// ceil(16 w / parts / cs)), per-token scales and exponents, alpha of the rows
 // this CTA finalises, the mbarriers.
 struct GemvSmem {
-  int stage, codes, ring, xs, recv, inv, emax, alpha, bars, total;
-  __host__ __device__ GemvSmem(int w, int stages, int xstride, int m, int cs) {
+  int stage, codes, ring, xs, xs_lo, recv, inv, emax, alpha, bars, total;
+  __host__ __device__ GemvSmem(int w, int stages, int xstride, int m, int cs, int parts,
+                               bool split) {
     codes = w * kGvTileCodes;
     stage = (codes + w * kGvTileScales + 1023) & ~1023;
     ring = 0;
     xs = stages * stage;
-    recv = xs + m * xstride;
-    inv = recv + (int)sizeof(float) * cs * ((16 * w + cs - 1) / cs) * kGvTok;
+    xs_lo = xs + m * xstride;
+    recv = xs_lo + (split ? m * xstride : 0);
+    const int per = (16 * w / parts + cs - 1) / cs;
+    inv = recv + (int)sizeof(float) * cs * per * parts * kGvTok;
     emax = inv + (int)sizeof(float) * kGvTok;
     alpha = emax + (int)sizeof(int) * kGvTok;
-    bars = (alpha + (int)sizeof(float) * ((16 * w + cs - 1) / cs) + 7) & ~7;
+    bars = (alpha + (int)sizeof(float) * parts * per + 7) & ~7;
     total = bars + 16 * stages;
   }
 };
 
 // Cluster q of a K split into gridDim.x slices owns row tiles
 // [q * nt / nq, (q + 1) * nt / nq) (nq = gridDim.y clusters, nt = 16-row
-// tiles): tile counts differ by at most one, so every SM gets the same
-// weight bytes to within one tile.  CTA = one consumer warp per tile of the
-// cluster + a producer warp that streams the CTA's 256-k chunks of those
-// tiles with TMA (per stage: a 128-byte-swizzled box of the tiles' rows x
-// 128 B of codes and one of their rows x 16 B of blockscales) through an
-// S-stage ring.
+// tiles; in kGvGateUp a "tile" is a pair: gate rows and the matching up
+// rows): tile counts differ by at most one, so every SM gets the same weight
+// bytes to within one tile.  CTA = one consumer warp per 16-row tile + a
+// producer warp that streams the CTA's 256-k chunks of those tiles with TMA
+// (per stage: a 128-byte-swizzled box of the tiles' rows x 128 B of codes and
+// one of their rows x 16 B of blockscales, twice in kGvGateUp) through an
+// S-stage ring.  Grouped modes: blockIdx.z = work item.
+//
+// Everything the previous kernel wrote (activations, work items) is read with
+// L2-coherent loads after griddepcontrol.wait: under programmatic dependent
+// launch the CTAs start before that kernel has finished, and the read-only
+// (non-coherent) cache path could return lines cached before its writes.
+template <int MODE>
 __global__ void __launch_bounds__(32 * (kGvMaxWarps + 1), 2)
     gemv_kernel(const __grid_constant__ CUtensorMap tmW_hi, const __grid_constant__ CUtensorMap tmS_hi,
                 const __grid_constant__ CUtensorMap tmW_lo, const __grid_constant__ CUtensorMap tmS_lo,
                 GemvArgs a) {
-  constexpr int kRedLd = kGvTok + 1;
+  constexpr bool kSplit = MODE == kGvDown;
+  constexpr int kParts = MODE == kGvGateUp ? 2 : 1;
   extern __shared__ __align__(1024) uint8_t gsm_raw[];
   uint8_t *gsm = reinterpret_cast<uint8_t *>(((uintptr_t)gsm_raw + 1023) & ~(uintptr_t)1023);
   __shared__ int abort_flag;
 
   const int W = (int)(blockDim.x >> 5) - 1;  // consumer warps
   const int S = a.stages;
-  const GemvSmem L(W, S, a.xstride, a.M, gridDim.x);
+  const GemvSmem L(W, S, a.xstride, a.M, gridDim.x, kParts, kSplit);
   uint8_t *ring = gsm + L.ring;
   uint8_t *xs = gsm + L.xs;
+  uint8_t *xs_lo = gsm + L.xs_lo;
   float *recv = reinterpret_cast<float *>(gsm + L.recv);
   float *inv_scale = reinterpret_cast<float *>(gsm + L.inv);
   int *emax = reinterpret_cast<int *>(gsm + L.emax);
@@ -235,10 +258,13 @@ __global__ void __launch_bounds__(32 * (kGvMaxWarps + 1), 2)
   uint64_t *bars = reinterpret_cast<uint64_t *>(gsm + L.bars);  // full[S], empty[S]
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int g = lane >> 2, c = lane & 3;
+  const int gq = lane >> 2, c = lane & 3;
   const int Cn = gridDim.x, slice = blockIdx.x;
-  const int nt = (a.N + 15) / 16, nq = gridDim.y, q = blockIdx.y;
+  // Tiles (pairs in kGvGateUp) of one weight matrix and this cluster's share.
+  const int nt = (MODE == kGvGateUp ? a.N / 2 : a.N + 15) / 16;
+  const int nq = gridDim.y, q = blockIdx.y;
   const int tile0 = (int)((int64_t)q * nt / nq), ntiles = (int)((int64_t)(q + 1) * nt / nq) - tile0;
+  const int nwarps_used = kParts * ntiles;  // consumer warps with a tile
   const int k0 = slice * a.ks;
   const int nch = a.ks / kGvChunk;
   const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + S);
@@ -247,7 +273,7 @@ __global__ void __launch_bounds__(32 * (kGvMaxWarps + 1), 2)
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(full0 + 8 * s, 1);
-      mbar_init(empty0 + 8 * s, ntiles);
+      mbar_init(empty0 + 8 * s, nwarps_used);
     }
     abort_flag = 0;
     mbar_fence_init();
@@ -257,20 +283,37 @@ __global__ void __launch_bounds__(32 * (kGvMaxWarps + 1), 2)
   // Programmatic dependent launch: everything above overlapped the previous
   // kernel; inputs are read only after it has completed.
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  // Rows this CTA finalises: [lo, lo + nr) of the cluster's 16 * ntiles.
+  // Work item (grouped modes): expert g, token slots [slot0, slot0 + M).
+  // The whole cluster shares blockIdx.z, so it leaves together.
+  int g = 0, slot0 = 0, M = a.M;
+  if constexpr (MODE != kGvPlain) {
+    if ((int)blockIdx.z >= __ldcg(a.n_work)) return;
+    const int *it = reinterpret_cast<const int *>(a.work + blockIdx.z);
+    g = __ldcg(it);
+    slot0 = __ldcg(it + 1);
+    M = __ldcg(it + 2);
+  }
+  const int64_t grow0 = (int64_t)g * a.N;  // first row of the expert in the stacked matrix
+  // Rows this CTA finalises: [lo, lo + nr) of the cluster's 16 * ntiles
+  // (pair rows in kGvGateUp).
   const int rows = 16 * ntiles;
   const int per = (rows + Cn - 1) / Cn;
   const int lo = min(slice * per, rows), nr = min(lo + per, rows) - lo;
-  for (int i = tid; i < nr; i += blockDim.x)
-    alpha_s[i] = 16 * tile0 + lo + i < a.N ? alpha_of(a.al, 0, 16 * tile0 + lo + i) : 0.0f;
+  for (int i = tid; i < kParts * nr; i += blockDim.x) {
+    const int part = i / nr, r = i - part * nr;
+    const int n = 16 * tile0 + lo + r + (part ? a.N / 2 : 0);  // row within the matrix
+    alpha_s[i] = (MODE == kGvGateUp || n < a.N) ? alpha_of(a.al, g, n) : 0.0f;
+  }
 
   if (warp == W) {
     // Producer: one thread issues the TMA loads, S stages ahead of use; one
-    // box per stage for all of the CTA's tiles (maps with W and W-1 tiles).
+    // box per stage (per part) for all of the CTA's tiles (maps with W and
+    // W-1 tiles per part).
     if (lane == 0) {
+      const bool full_count = kParts * ntiles == W;
+      const CUtensorMap *tmW = full_count ? &tmW_hi : &tmW_lo;
+      const CUtensorMap *tmS = full_count ? &tmS_hi : &tmS_lo;
       const uint64_t pol = l2_evict_first_policy();
-      const CUtensorMap *tmW = ntiles == W ? &tmW_hi : &tmW_lo;
-      const CUtensorMap *tmS = ntiles == W ? &tmS_hi : &tmS_lo;
       prefetch_tmap(tmW);
       prefetch_tmap(tmS);
       int issued = 0;
@@ -280,10 +323,15 @@ __global__ void __launch_bounds__(32 * (kGvMaxWarps + 1), 2)
                                 abort))
           break;
         const uint32_t st = smem_u32(ring + s * L.stage);
-        mbar_arrive_expect_tx(full0 + 8 * s, ntiles * (kGvTileCodes + kGvTileScales));
+        mbar_arrive_expect_tx(full0 + 8 * s, kParts * ntiles * (kGvTileCodes + kGvTileScales));
         const int xc = (k0 + ch * kGvChunk) / 2, xsf = (k0 + ch * kGvChunk) / kGroup;
-        tma_load_2d_hint(st, tmW, xc, 16 * tile0, full0 + 8 * s, pol);
-        tma_load_2d_hint(st + L.codes, tmS, xsf, 16 * tile0, full0 + 8 * s, pol);
+#pragma unroll
+        for (int part = 0; part < kParts; ++part) {
+          const int row = (int)(grow0 + 16 * tile0 + (part ? a.N / 2 : 0));
+          tma_load_2d_hint(st + part * ntiles * kGvTileCodes, tmW, xc, row, full0 + 8 * s, pol);
+          tma_load_2d_hint(st + L.codes + part * ntiles * kGvTileScales, tmS, xsf, row,
+                           full0 + 8 * s, pol);
+        }
         issued = ch + 1;
       }
       // After an abort, wait (bounded) for the copies still in flight before exit.
@@ -296,113 +344,158 @@ __global__ void __launch_bounds__(32 * (kGvMaxWarps + 1), 2)
   } else {
     // x slice -> f16 with a per-token power-of-two scale.  The M * ks / 8
     // 16-byte units of the slice are spread over all consumer threads: the
-    // largest bf16 exponent per token is taken with shared atomicMax, then
-    // the units are converted.  Up to 4 units per thread stay in registers
-    // (one read of x); beyond that x is read twice (through L1).
-    const int nunits = a.ks / 8, total_units = a.M * nunits, nthr = 32 * W;
-    auto load_units = [&](int base, uint4 (&v)[4]) {
+    // largest exponent per token is taken with shared atomicMax, then the
+    // units are converted (kGvDown: x = hi + lo, kept as f16 hi + f16 lo).
+    // Up to 4 units per thread stay in registers (one read of x); beyond
+    // that x is read twice.
+    const int nunits = a.ks / 8, total_units = M * nunits, nthr = 32 * W;
+    auto xrow_of = [&](int tt) -> int64_t {
+      if constexpr (MODE == kGvGateUp) return a.x_rows ? __ldcg(a.x_rows + slot0 + tt) : slot0 + tt;
+      if constexpr (MODE == kGvDown) return slot0 + tt;
+      return tt;
+    };
+    auto load_units = [&](int base, uint4 (&v)[4], uint4 (&vl)[4]) {
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int i = base + j * nthr;
         v[j] = make_uint4(0u, 0u, 0u, 0u);
+        vl[j] = make_uint4(0u, 0u, 0u, 0u);
         if (i < total_units) {
           const int tt = i / nunits, u = i - tt * nunits;
-          v[j] = __ldg(reinterpret_cast<const uint4 *>(a.x + (int64_t)tt * a.x_ld + k0 + 8 * u));
+          const int64_t off = xrow_of(tt) * a.x_ld + k0 + 8 * u;
+          v[j] = __ldcg(reinterpret_cast<const uint4 *>(a.x + off));
+          if constexpr (kSplit) vl[j] = __ldcg(reinterpret_cast<const uint4 *>(a.x_lo + off));
         }
       }
     };
-    auto max_units = [&](int base, const uint4 (&v)[4]) {
+    // fp32 values of a unit (x, or hi + lo).
+    auto unit_f32 = [&](const uint4 &v, const uint4 &vl, float (&f)[8]) {
+      const uint32_t in[4] = {v.x, v.y, v.z, v.w};
+      const uint32_t il[4] = {vl.x, vl.y, vl.z, vl.w};
+#pragma unroll
+      for (int q2 = 0; q2 < 4; ++q2) {
+        f[2 * q2] = bf16lo(in[q2]);
+        f[2 * q2 + 1] = bf16hi(in[q2]);
+        if constexpr (kSplit) {
+          f[2 * q2] += bf16lo(il[q2]);
+          f[2 * q2 + 1] += bf16hi(il[q2]);
+        }
+      }
+    };
+    auto max_units = [&](int base, const uint4 (&v)[4], const uint4 (&vl)[4]) {
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int i = base + j * nthr;
         if (i < total_units) {
-          uint32_t m = __vmaxu2(__vmaxu2(v[j].x & 0x7F807F80u, v[j].y & 0x7F807F80u),
-                                __vmaxu2(v[j].z & 0x7F807F80u, v[j].w & 0x7F807F80u));
-          m = max(m & 0xFFFFu, m >> 16);
-          atomicMax(&emax[i / nunits], (int)(m >> 7));
+          uint32_t m;
+          if constexpr (kSplit) {
+            float f[8];
+            unit_f32(v[j], vl[j], f);
+            float mx = 0.0f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) mx = fmaxf(mx, fabsf(f[e]));
+            m = (__float_as_uint(mx) >> 23) & 0xFFu;  // biased f32 exponent = bf16's
+          } else {
+            m = __vmaxu2(__vmaxu2(v[j].x & 0x7F807F80u, v[j].y & 0x7F807F80u),
+                         __vmaxu2(v[j].z & 0x7F807F80u, v[j].w & 0x7F807F80u));
+            m = max(m & 0xFFFFu, m >> 16) >> 7;
+          }
+          atomicMax(&emax[i / nunits], (int)m);
         }
       }
     };
-    auto convert_units = [&](int base, const uint4 (&v)[4]) {
+    auto convert_units = [&](int base, const uint4 (&v)[4], const uint4 (&vl)[4]) {
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int i = base + j * nthr;
         if (i < total_units) {
           const int tt = i / nunits, u = i - tt * nunits;
-          const int e = max(emax[tt], 1);  // biased bf16 exponent of max|x|
+          const int e = max(emax[tt], 1);  // biased exponent of max|x|
           const int sc = min(max(141 - e, -126), 127);
-          const float f = __int_as_float((sc + 127) << 23);
-          const uint32_t in[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-          uint32_t o[4];
+          const float fs = __int_as_float((sc + 127) << 23);
+          float f[8];
+          unit_f32(v[j], vl[j], f);
+          uint32_t o[4], ol[4];
 #pragma unroll
           for (int q2 = 0; q2 < 4; ++q2) {
-            const __half2 h2 = __floats2half2_rn(bf16lo(in[q2]) * f, bf16hi(in[q2]) * f);
+            const float x0 = f[2 * q2] * fs, x1 = f[2 * q2 + 1] * fs;
+            const __half2 h2 = __floats2half2_rn(x0, x1);
             o[q2] = *reinterpret_cast<const uint32_t *>(&h2);
+            if constexpr (kSplit) {
+              const __half2 l2 =
+                  __floats2half2_rn(x0 - __low2float(h2), x1 - __high2float(h2));
+              ol[q2] = *reinterpret_cast<const uint32_t *>(&l2);
+            }
           }
-          *reinterpret_cast<uint4 *>(xs + tt * a.xstride + 16 * xs_unit(u)) =
-              make_uint4(o[0], o[1], o[2], o[3]);
+          const int off = tt * a.xstride + 16 * xs_unit(u);
+          *reinterpret_cast<uint4 *>(xs + off) = make_uint4(o[0], o[1], o[2], o[3]);
+          if constexpr (kSplit)
+            *reinterpret_cast<uint4 *>(xs_lo + off) = make_uint4(ol[0], ol[1], ol[2], ol[3]);
         }
       }
     };
     if (total_units <= 4 * nthr) {
-      uint4 v[4];
-      load_units(tid, v);
-      max_units(tid, v);
+      uint4 v[4], vl[4];
+      load_units(tid, v, vl);
+      max_units(tid, v, vl);
       asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
-      convert_units(tid, v);
+      convert_units(tid, v, vl);
     } else {
       for (int base = tid; base < total_units; base += 4 * nthr) {
-        uint4 v[4];
-        load_units(base, v);
-        max_units(base, v);
+        uint4 v[4], vl[4];
+        load_units(base, v, vl);
+        max_units(base, v, vl);
       }
       asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
       for (int base = tid; base < total_units; base += 4 * nthr) {
-        uint4 v[4];
-        load_units(base, v);
-        convert_units(base, v);
+        uint4 v[4], vl[4];
+        load_units(base, v, vl);
+        convert_units(base, v, vl);
       }
     }
     if (tid < kGvTok) {
       const int e = max(emax[tid], 1);
       const int sc = min(max(141 - e, -126), 127);
-      inv_scale[tid] = tid < a.M ? __frcp_rn(__int_as_float((sc + 127) << 23)) : 0.0f;
+      inv_scale[tid] = tid < M ? __frcp_rn(__int_as_float((sc + 127) << 23)) : 0.0f;
     }
     asm volatile("bar.sync 1, %0;" ::"r"(32 * W) : "memory");  // consumer warps only
     // The next kernel in the stream may start its prologue now.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
-    if (warp < ntiles) {
+    if (warp < nwarps_used) {
       float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-      const bool has_x = g < a.M;  // tokens >= M: zero B fragments
-      const uint32_t xrow = smem_u32(xs + (has_x ? g : 0) * a.xstride);
+      const bool has_x = gq < M;  // tokens >= M: zero B fragments
+      const uint32_t xrow = smem_u32(xs + (has_x ? gq : 0) * a.xstride);
+      const uint32_t xrow_lo = smem_u32(xs_lo + (has_x ? gq : 0) * a.xstride);
       for (int ch = 0; ch < nch; ++ch) {
         const int s = ch % S, u = ch / S;
         const bool ok = mbar_wait(full0 + 8 * s, u & 1, &g_gemv_status, kDevTimeoutFull, abort);
         if (!__all_sync(0xffffffffu, ok)) break;
         const uint32_t st = smem_u32(ring + s * L.stage);
         GemvChunk b;
-        gemv_fetch(b, st + warp * kGvTileCodes, st + L.codes + warp * kGvTileScales, g, c);
+        gemv_fetch(b, st + warp * kGvTileCodes, st + L.codes + warp * kGvTileScales, gq, c);
         __syncwarp();
         if (lane == 0) mbar_arrive(empty0 + 8 * s);  // operands are in registers
         // The MMA's fp32 accumulation is not IEEE round-to-nearest: chains are
-        // kept to one chunk (16 MMAs) and chunk sums added with fp32 adds.
+        // kept to one chunk (16 or 32 MMAs) and chunk sums added with fp32 adds.
         float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        gemv_compute(b, part, xrow, has_x, ch, c);
+        gemv_compute<kSplit>(b, part, xrow, xrow_lo, has_x, ch, c);
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[i] += part[i];
       }
       // Partial sums (times 2^-s per token) go straight to the CTA of the
-      // cluster that owns the row: slot [slice][row - owner's first row].
+      // cluster that owns the row: slot [slice][row - owner's first row][part].
       const float is0 = inv_scale[2 * c], is1 = inv_scale[2 * c + 1];
+      const int part = warp / ntiles;  // kGvGateUp: warps [0, ntiles) gate, then up
+      const int wt = warp - part * ntiles;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        const int r = warp * 16 + g + 8 * h;
+        const int r = wt * 16 + gq + 8 * h;
         const int owner = r / per, local = r - owner * per;
-        float *dst = recv + ((size_t)slice * per + local) * kGvTok + 2 * c;
+        float *dst = recv + (((size_t)slice * per + local) * kParts + part) * kGvTok + 2 * c;
         if (Cn > 1) dst = cluster_map(dst, owner);
-        if (2 * c < a.M) dst[0] = acc[2 * h] * is0;
-        if (2 * c + 1 < a.M) dst[1] = acc[2 * h + 1] * is1;
+        if (2 * c < M) dst[0] = acc[2 * h] * is0;
+        if (2 * c + 1 < M) dst[1] = acc[2 * h + 1] * is1;
       }
     }
   }
@@ -415,46 +508,48 @@ __global__ void __launch_bounds__(32 * (kGvMaxWarps + 1), 2)
   } else {
     __syncthreads();
   }
-  for (int i = tid; i < nr * a.M; i += blockDim.x) {
+  for (int i = tid; i < nr * M; i += blockDim.x) {
     const int r = i % nr, tok = i / nr;
-    float v = 0.0f;
-    for (int qq = 0; qq < Cn; ++qq) v += recv[((size_t)qq * per + r) * kGvTok + tok];
+    float v[kParts];
+#pragma unroll
+    for (int part = 0; part < kParts; ++part) {
+      float sum = 0.0f;
+      for (int qq = 0; qq < Cn; ++qq)
+        sum += recv[(((size_t)qq * per + r) * kParts + part) * kGvTok + tok];
+      v[part] = sum * alpha_s[part * nr + r];
+    }
     const int n = 16 * tile0 + lo + r;
-    if (n < a.N) {
-      v *= alpha_s[r];
-      if (a.y_dtype == kBF16)
-        reinterpret_cast<uint16_t *>(a.y)[(int64_t)tok * a.y_ld + n] = f32_to_bf16_bits(v);
-      else
-        reinterpret_cast<float *>(a.y)[(int64_t)tok * a.y_ld + n] = v;
+    if constexpr (MODE == kGvGateUp) {
+      // silu(gate) * up as bf16 hi + lo (the down projection's operand).
+      const float o = silu_f32(v[0]) * v[1];
+      const uint16_t h = f32_to_bf16_bits(o);
+      const float hf = __uint_as_float((uint32_t)h << 16);
+      const int64_t idx = (int64_t)(slot0 + tok) * a.y_ld + n;
+      reinterpret_cast<uint16_t *>(a.y)[idx] = h;
+      a.y_lo[idx] = f32_to_bf16_bits(o - hf);
+    } else {
+      if (n < a.N) {
+        int64_t row = tok;
+        if constexpr (MODE == kGvDown)
+          row = a.y_rows ? __ldcg(a.y_rows + slot0 + tok) : slot0 + tok;
+        if (a.y_dtype == kBF16)
+          reinterpret_cast<uint16_t *>(a.y)[row * a.y_ld + n] = f32_to_bf16_bits(v[0]);
+        else
+          reinterpret_cast<float *>(a.y)[row * a.y_ld + n] = v[0];
+      }
     }
   }
 }
 
-}  // namespace
-
-bool gemv_supported(int M, int K, const void *w, const void *sf, const void *x, int64_t x_ld) {
-  return M >= 1 && M <= kGvTok && K % kGvChunk == 0 && K <= 8 * kGvMaxKs &&
-         ((uintptr_t)w & 15) == 0 && ((uintptr_t)sf & 15) == 0 && ((uintptr_t)x & 15) == 0 &&
-         x_ld % 8 == 0 && tc_gemm_supported(K, w, x, x_ld);
-}
-
-int read_gemv_device_status() {
-  int v = 0, zero = 0;
-  if (cudaMemcpyFromSymbol(&v, g_gemv_status, sizeof(int)) != cudaSuccess) return -1;
-  if (v) cudaMemcpyToSymbol(g_gemv_status, &zero, sizeof(int));
-  return v;
-}
-
-namespace {
-
 // Ring stages that fit in the per-CTA budget (two CTAs per SM).
-int gemv_stages(int w, int xstride, int m, int cs) {
+int gemv_stages(int w, int xstride, int m, int cs, int parts, bool split) {
   int s = 4;
-  while (s > 2 && GemvSmem(w, s, xstride, m, cs).total + 1024 > kGvSmemCap) --s;
-  return GemvSmem(w, s, xstride, m, cs).total + 1024 <= kGvSmemCap ? s : 0;
+  while (s > 2 && GemvSmem(w, s, xstride, m, cs, parts, split).total + 1024 > kGvSmemCap) --s;
+  return GemvSmem(w, s, xstride, m, cs, parts, split).total + 1024 <= kGvSmemCap ? s : 0;
 }
 
 // Clusters of C CTAs (w consumer warps, smem bytes) the GPU holds at once.
+template <int MODE>
 int gemv_cluster_capacity(int C, int w, size_t smem) {
   static std::mutex mu;
   static std::map<std::tuple<int, int, int, size_t>, int> cache;
@@ -478,7 +573,7 @@ int gemv_cluster_capacity(int C, int w, size_t smem) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, gemv_kernel, &cfg) != cudaSuccess) {
+  if (cudaOccupancyMaxActiveClusters(&n, gemv_kernel<MODE>, &cfg) != cudaSuccess) {
     cudaGetLastError();
     n = 0;
   }
@@ -487,99 +582,102 @@ int gemv_cluster_capacity(int C, int w, size_t smem) {
   return n;
 }
 
-}  // namespace
-
-cudaError_t launch_gemv(const WeightSpec &ws, const AlphaSpec &al, const uint16_t *x,
-                        int64_t x_ld, void *y, int y_dtype, int64_t y_ld, int M,
-                        cudaStream_t st) {
-  if (M == 0 || ws.N == 0) return cudaSuccess;
-  GemvArgs a;
-  a.w = ws.w;
-  a.sf = ws.sf;
-  a.al = al;
-  a.x = x;
-  a.x_ld = x_ld;
-  a.y = y;
-  a.y_dtype = y_dtype;
-  a.y_ld = y_ld;
-  a.M = M;
-  a.N = ws.N;
-  a.K = ws.K;
-  // Two CTAs per SM.  K split C (cluster size): a divisor of the chunk count,
-  // at most 8, with K / C <= kGvMaxKs.  Clusters: two CTAs per SM / C, or
-  // fewer when the GPU cannot hold that many clusters of C at once (a cluster
-  // must fit in one GPC); consumer warps W = the largest tile count of a
-  // cluster (at most kGvMaxWarps).  The C taken minimises the work of the
-  // busiest CTA times the waves of clusters, ks * (W + 0.16 M) * waves: W
-  // tiles of decode + MMA plus the conversion of M activation rows (about
-  // 0.16 of a tile's instructions per row of x).
-  {
-    static std::mutex mu;
-    static bool attr_set[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    std::lock_guard<std::mutex> lock(mu);
-    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    if (!attr_set[dev]) {
-      cudaError_t e = cudaFuncSetAttribute(
-          gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGvSmemCap + 1024);
-      if (e != cudaSuccess) return e;
-      attr_set[dev] = true;
-    }
+template <int MODE>
+cudaError_t set_smem_attr() {
+  static std::mutex mu;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<MODE>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kGvSmemCap + 1024);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
   }
-  const int nck = ws.K / kGvChunk;
-  const int nt = (ws.N + 15) / 16;
+  return cudaSuccess;
+}
+
+// Plans (K split C, clusters, warps, stages) and launches a GEMV of `items`
+// weight matrices of N rows (grid.z = items; 1 in plain mode).
+//
+// Two CTAs per SM.  K split C (cluster size): a divisor of the chunk count,
+// at most 8, with K / C <= kGvMaxKs.  Clusters per matrix: two CTAs per SM /
+// (C * items), or fewer when the GPU cannot hold that many clusters of C at
+// once (a cluster must fit in one GPC); consumer warps W = the largest tile
+// count of a cluster (at most kGvMaxWarps).  The C taken minimises the work of
+// the busiest CTA times the waves of clusters, ks * (W + 0.16 M) * waves: W
+// tiles of decode + MMA plus the conversion of M activation rows (about 0.16
+// of a tile's instructions per row of x).
+template <int MODE>
+cudaError_t launch_mode(GemvArgs a, int items, int64_t total_rows, cudaStream_t st) {
+  constexpr int kParts = MODE == kGvGateUp ? 2 : 1;
+  constexpr bool kSplit = MODE == kGvDown;
+  cudaError_t e = set_smem_attr<MODE>();
+  if (e != cudaSuccess) return e;
+  const int M = a.M;
+  const int nck = a.K / kGvChunk;
+  const int nt = (MODE == kGvGateUp ? a.N / 2 : a.N + 15) / 16;
+  const int max_tiles = kGvMaxWarps / kParts;
   const int ctas_target = 2 * tc_sm_count();
   int bestC = 0, bestW = 0, bestNq = 0, bestS = 0;
   double best_cost = 0.0;
   for (int C = 1; C <= 8; ++C) {
-    if (nck % C || ws.K / C > kGvMaxKs) continue;
-    const int xstride = 2 * (ws.K / C) + 64;
-    int nq = ctas_target / C;
+    if (nck % C || a.K / C > kGvMaxKs) continue;
+    const int xstride = 2 * (a.K / C) + 64;
+    int nq = ctas_target / (C * items);
     if (nq > nt) nq = nt;
     if (nq < 1) nq = 1;
-    int w = 0, stages = 0, waves = 1;
+    int tiles = 0, stages = 0, waves = 1;
     for (int it = 0; it < 2; ++it) {
-      w = (nt + nq - 1) / nq;
-      if (w > kGvMaxWarps) {
-        w = kGvMaxWarps;
-        nq = (nt + w - 1) / w;
-        w = (nt + nq - 1) / nq;
+      tiles = (nt + nq - 1) / nq;
+      if (tiles > max_tiles) {
+        tiles = max_tiles;
+        nq = (nt + tiles - 1) / tiles;
+        tiles = (nt + nq - 1) / nq;
       }
-      stages = gemv_stages(w, xstride, M, C);
-      const int cap =
-          gemv_cluster_capacity(C, w, 1024 + GemvSmem(w, stages, xstride, M, C).total);
+      stages = gemv_stages(kParts * tiles, xstride, M, C, kParts, kSplit);
+      const int cap = gemv_cluster_capacity<MODE>(
+          C, kParts * tiles,
+          1024 + GemvSmem(kParts * tiles, stages, xstride, M, C, kParts, kSplit).total);
       if (cap <= 0) break;
-      waves = (nq + cap - 1) / cap;
-      if (waves == 1 || it == 1) break;
+      waves = (nq * items + cap - 1) / cap;
+      if (waves == 1 || it == 1 || items > 1) break;
       nq = cap;  // one wave of the clusters that fit, with more tiles each
     }
-    if (w <= 0 || stages <= 0) continue;
-    const double cost = (double)(ws.K / C) * (w + 0.16 * M) * waves * (1.0 + 0.01 * (waves - 1));
+    if (tiles <= 0 || stages <= 0) continue;
+    const double cost =
+        (double)(a.K / C) * (kParts * tiles + 0.16 * M) * waves * (1.0 + 0.01 * (waves - 1));
     if (bestC == 0 || cost < best_cost) {
       bestC = C;
-      bestW = w;
+      bestW = kParts * tiles;
       bestNq = nq;
       bestS = stages;
       best_cost = cost;
     }
   }
   if (bestC == 0) return cudaErrorInvalidValue;
-  a.ks = ws.K / bestC;
+  a.ks = a.K / bestC;
   a.xstride = 2 * a.ks + 64;
   a.stages = bestS;
+  // Boxes of W and W-1 tiles per part (clusters own one or the other count).
   CUtensorMap tm[4];
   for (int i = 0; i < 2; ++i) {
-    const int rows = 16 * (bestW - i > 0 ? bestW - i : 1);
-    if (!make_tmap_2d(&tm[2 * i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.w, a.N, a.K / 2, a.K / 2,
-                      kGvChunk / 2, rows, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_tmap_2d(&tm[2 * i + 1], CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.sf, a.N, a.K / kGroup,
-                      a.K / kGroup, kGvChunk / kGroup, rows, CU_TENSOR_MAP_SWIZZLE_NONE))
+    const int t = bestW / kParts - i;
+    const int rows = 16 * (t > 0 ? t : 1);
+    if (!make_tmap_2d(&tm[2 * i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.w, total_rows, a.K / 2,
+                      a.K / 2, kGvChunk / 2, rows, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_tmap_2d(&tm[2 * i + 1], CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.sf, total_rows,
+                      a.K / kGroup, a.K / kGroup, kGvChunk / kGroup, rows,
+                      CU_TENSOR_MAP_SWIZZLE_NONE))
       return cudaErrorInvalidValue;
   }
-  const size_t smem = 1024 + (size_t)GemvSmem(bestW, a.stages, a.xstride, M, bestC).total;
+  const size_t smem =
+      1024 + (size_t)GemvSmem(bestW, a.stages, a.xstride, M, bestC, kParts, kSplit).total;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(bestC, bestNq, 1);
+  cfg.gridDim = dim3(bestC, bestNq, items);
   cfg.blockDim = dim3(32 * (bestW + 1), 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -592,7 +690,77 @@ cudaError_t launch_gemv(const WeightSpec &ws, const AlphaSpec &al, const uint16_
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, gemv_kernel, tm[0], tm[1], tm[2], tm[3], a);
+  return cudaLaunchKernelEx(&cfg, gemv_kernel<MODE>, tm[0], tm[1], tm[2], tm[3], a);
+}
+
+}  // namespace
+
+bool gemv_supported(int M, int K, const void *w, const void *sf, const void *x, int64_t x_ld) {
+  return M >= 1 && M <= kGvTok && K % kGvChunk == 0 && K <= 8 * kGvMaxKs &&
+         ((uintptr_t)w & 15) == 0 && ((uintptr_t)sf & 15) == 0 && ((uintptr_t)x & 15) == 0 &&
+         x_ld % 8 == 0 && tc_gemm_supported(K, w, x, x_ld);
+}
+
+int read_gemv_device_status() {
+  int v = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&v, g_gemv_status, sizeof(int)) != cudaSuccess) return -1;
+  if (v) cudaMemcpyToSymbol(g_gemv_status, &zero, sizeof(int));
+  return v;
+}
+
+cudaError_t launch_gemv(const WeightSpec &ws, const AlphaSpec &al, const uint16_t *x,
+                        int64_t x_ld, void *y, int y_dtype, int64_t y_ld, int M,
+                        cudaStream_t st) {
+  if (M == 0 || ws.N == 0) return cudaSuccess;
+  GemvArgs a = {};
+  a.w = ws.w;
+  a.sf = ws.sf;
+  a.al = al;
+  a.x = x;
+  a.x_ld = x_ld;
+  a.y = y;
+  a.y_dtype = y_dtype;
+  a.y_ld = y_ld;
+  a.M = M;
+  a.N = ws.N;
+  a.K = ws.K;
+  return launch_mode<kGvPlain>(a, 1, ws.N, st);
+}
+
+bool moe_gemv_supported(int H, int I, const void *gate_up, const void *gate_up_sf,
+                        const void *down, const void *down_sf) {
+  auto al16 = [](const void *p) { return ((uintptr_t)p & 15) == 0; };
+  // K % 256 for both GEMMs (whole chunks), 16-row tiles of gate and up rows,
+  // 16-byte aligned TMA bases; tc_gemm_supported also confirms the TMA
+  // descriptor encoder is available.
+  return H % kGvChunk == 0 && I % kGvChunk == 0 && H <= 8 * kGvMaxKs && I <= 8 * kGvMaxKs &&
+         al16(gate_up) && al16(gate_up_sf) && al16(down) && al16(down_sf) &&
+         tc_gemm_supported(H, gate_up, down, H);
+}
+
+cudaError_t launch_moe_gemv(const MoeGemvLaunch &m, cudaStream_t st) {
+  if (m.items == 0) return cudaSuccess;
+  GemvArgs a = {};
+  a.w = m.w;
+  a.sf = m.sf;
+  a.al = m.al;
+  a.x = m.x;
+  a.x_lo = m.x_lo;
+  a.x_ld = m.x_ld;
+  a.y = m.y;
+  a.y_lo = m.y_lo;
+  a.y_dtype = m.y_dtype;
+  a.y_ld = m.y_ld;
+  a.M = kGvTok;  // items hold up to 8 slots; shared memory is sized for 8
+  a.N = m.N;
+  a.K = m.K;
+  a.work = m.work;
+  a.n_work = m.n_work;
+  a.x_rows = m.x_rows;
+  a.y_rows = m.y_rows;
+  const int64_t total_rows = (int64_t)m.groups * m.N;
+  return m.gate_up ? launch_mode<kGvGateUp>(a, m.items, total_rows, st)
+                   : launch_mode<kGvDown>(a, m.items, total_rows, st);
 }
 
 }  // namespace nvfp4

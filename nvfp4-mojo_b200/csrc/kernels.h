@@ -92,6 +92,32 @@ cudaError_t launch_gemv(const WeightSpec &ws, const AlphaSpec &al, const uint16_
                         int64_t x_ld, void *y, int y_dtype, int64_t y_ld, int M,
                         cudaStream_t st);
 
+// Grouped MoE expert GEMMs on the decode GEMV kernel (work items of at most
+// 8 token slots): gate_up -> silu(gate) * up as bf16 hi + lo [R, I] (rows in
+// slot order), down on those hi + lo rows -> y rows (dst_row scatter).
+struct MoeGemvLaunch {
+  const uint8_t *w = nullptr;   // stacked [groups * N, K/2]
+  const uint8_t *sf = nullptr;  // stacked [groups * N, K/16]
+  AlphaSpec al;                 // per group: input_scales[g], ws2_rows + g * N
+  const uint16_t *x = nullptr;
+  const uint16_t *x_lo = nullptr;  // down: low parts
+  int64_t x_ld = 0;
+  void *y = nullptr;
+  uint16_t *y_lo = nullptr;        // gate_up: low parts
+  int y_dtype = kBF16;
+  int64_t y_ld = 0;
+  int N = 0, K = 0, groups = 0;
+  int items = 0;                   // host upper bound of the work items
+  const SkinnyWork *work = nullptr;
+  const int *n_work = nullptr;
+  const int32_t *x_rows = nullptr;  // gate_up: slot -> x row
+  const int32_t *y_rows = nullptr;  // down: slot -> y row
+  bool gate_up = false;
+};
+bool moe_gemv_supported(int H, int I, const void *gate_up, const void *gate_up_sf,
+                        const void *down, const void *down_sf);
+cudaError_t launch_moe_gemv(const MoeGemvLaunch &m, cudaStream_t st);
+
 // tcgen05 W4A16 GEMM (token-major x [M, K] bf16 with row stride x_ld).
 bool tc_gemm_supported(int K, const void *w, const void *x, int64_t x_ld);
 cudaError_t launch_w4a16_tc(const WeightSpec &ws, const AlphaSpec &al, const uint16_t *x,

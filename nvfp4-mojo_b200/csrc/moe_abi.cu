@@ -13,16 +13,44 @@ constexpr size_t kAlign = 256;
 size_t up(size_t v) { return (v + kAlign - 1) & ~(kAlign - 1); }
 
 // Grouped-GEMM path: tcgen05 tiles when experts get many rows on average
-// (prefill), the register-decode skinny kernel otherwise (decode).
+// (prefill); the TMA-fed decode GEMV kernel (work items of <= 8 slots) when
+// they get few; the register-decode skinny kernel in between, or when the
+// shapes or alignments do not suit the GEMV kernel.
+enum class ExpertPath { kTc, kGemv, kSkinny };
+
 bool use_tc(const nvfp4_moe_desc &d, int64_t R) {
   return R >= 64LL * d.num_experts && moe_tc_supported(d.hidden, d.intermediate);
 }
 
+// GEMV path by shape: at most 32 rows per expert on average (items of 8
+// slots re-read an expert's weights once per item).
+bool gemv_shape_ok(const nvfp4_moe_desc &d, int64_t R) {
+  return !use_tc(d, R) && R <= 32LL * d.num_experts && d.hidden % 256 == 0 &&
+         d.intermediate % 256 == 0;
+}
+
+ExpertPath choose_path(const nvfp4_moe_desc &d, const nvfp4_moe_weights &w, int64_t R) {
+  if (use_tc(d, R)) return ExpertPath::kTc;
+  if (gemv_shape_ok(d, R) &&
+      moe_gemv_supported(d.hidden, d.intermediate, w.gate_up, w.gate_up_scale, w.down,
+                         w.down_scale))
+    return ExpertPath::kGemv;
+  return ExpertPath::kSkinny;
+}
+
 // Rows per grouped-GEMM work item.
-int choose_tpi(const nvfp4_moe_desc &d, int64_t R) {
-  if (use_tc(d, R)) return moe_tc_rows_per_item();
+int path_tpi(const nvfp4_moe_desc &d, int64_t R, ExpertPath p) {
+  if (p == ExpertPath::kTc) return moe_tc_rows_per_item();
+  if (p == ExpertPath::kGemv) return 8;
   const int64_t avg = (R + d.num_experts - 1) / d.num_experts;
   return avg <= 8 ? 8 : (avg <= 16 ? 16 : 32);
+}
+
+// Workspace sizing knows the shapes only: it takes the largest item count
+// any path could need (items of 8 slots unless the tensor-core path runs).
+int choose_tpi(const nvfp4_moe_desc &d, int64_t R) {
+  if (use_tc(d, R)) return moe_tc_rows_per_item();
+  return gemv_shape_ok(d, R) ? 8 : path_tpi(d, R, ExpertPath::kSkinny);
 }
 
 int64_t work_capacity(int64_t R, int E, int tpi) { return (R + tpi - 1) / tpi + E; }
@@ -109,7 +137,8 @@ int run_experts(const nvfp4_moe_desc &d, const nvfp4_moe_weights &w, const uint1
   if (R == 0) return NVFP4_OK;
   const ExpertsLayout L = experts_layout(d, R);
   const int E = d.num_experts, H = d.hidden, I = d.intermediate;
-  const int tpi = choose_tpi(d, R);
+  const ExpertPath path = choose_path(d, w, R);
+  const int tpi = path_tpi(d, R, path);
   MoePlan plan;
   plan.offsets = reinterpret_cast<int32_t *>(ws + L.offsets);
   plan.n_work = reinterpret_cast<int32_t *>(ws + L.n_work);
@@ -126,7 +155,51 @@ int run_experts(const nvfp4_moe_desc &d, const nvfp4_moe_weights &w, const uint1
                         "MoE permutation launch");
   if (rc) return rc;
 
-  if (use_tc(d, R)) {
+  if (path == ExpertPath::kGemv) {
+    MoeGemvLaunch gu;
+    gu.w = w.gate_up;
+    gu.sf = w.gate_up_scale;
+    gu.al.input_scales = w.gate_up_input_scale;
+    gu.al.ws2_rows = w.gate_up_scale_2;
+    gu.al.ws2_group_stride = 2 * I;
+    gu.x = x;
+    gu.x_ld = H;
+    gu.x_rows = plan.src_row;
+    gu.y = inter;
+    gu.y_lo = inter_lo;
+    gu.y_ld = I;
+    gu.N = 2 * I;
+    gu.K = H;
+    gu.groups = E;
+    gu.items = (int)work_capacity(R, E, tpi);
+    gu.work = plan.work;
+    gu.n_work = plan.n_work;
+    gu.gate_up = true;
+    rc = check_launch(launch_moe_gemv(gu, st), "MoE gate_up (GEMV) launch");
+    if (rc) return rc;
+    MoeGemvLaunch dn = gu;
+    dn.w = w.down;
+    dn.sf = w.down_scale;
+    dn.al = AlphaSpec();
+    dn.al.input_scales = w.down_input_scale;
+    dn.al.ws2_rows = w.down_scale_2;
+    dn.al.ws2_group_stride = H;
+    dn.x = inter;
+    dn.x_lo = inter_lo;
+    dn.x_ld = I;
+    dn.x_rows = nullptr;
+    dn.y = y_rows;
+    dn.y_lo = nullptr;
+    dn.y_dtype = y_dtype;
+    dn.y_ld = H;
+    dn.y_rows = plan.dst_row;
+    dn.N = H;
+    dn.K = I;
+    dn.gate_up = false;
+    return check_launch(launch_moe_gemv(dn, st), "MoE down (GEMV) launch");
+  }
+
+  if (path == ExpertPath::kTc) {
     uint16_t *x_perm = reinterpret_cast<uint16_t *>(ws + L.x_perm);
     rc = check_launch(launch_gather_rows(x, plan.src_row, R, (int64_t)H * 2, x_perm, st),
                       "MoE activation gather launch");

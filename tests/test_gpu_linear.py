@@ -147,6 +147,40 @@ def test_decode_gemv_shapes(O, cuda, N, K, M):
     assert rel_err(ybf.float().cpu().numpy(), ref) <= TOL_BF16
 
 
+def test_decode_gemv_chained_layers(O, cuda):
+    """Two decode GEMVs in a chain (the second reads the first's output),
+    three times in a row on one stream with new inputs and reused buffers:
+    the kernel starts before its predecessor has finished (programmatic
+    dependent launch), so it must never see a previous iteration's data."""
+    import nvfp4
+    from nvfp4 import synthetic
+
+    M, K, N = 4, 2048, 1536
+    wa = synthetic.linear_weights(N, K, seed=61)
+    wb = synthetic.linear_weights(K, N, seed=62)
+    la = nvfp4.NvFp4Linear(K, N, weight_scale_2_rows=dev(wa["ws2"]))
+    lb = nvfp4.NvFp4Linear(N, K, weight_scale_2_rows=dev(wb["ws2"]))
+    Wa, Sa, Wb, Sb = dev(wa["w"]), dev(wa["sf"]), dev(wb["w"]), dev(wb["sf"])
+    X = torch.empty((M, K), dtype=torch.bfloat16, device=cuda)
+    Y1 = torch.empty((M, N), dtype=torch.bfloat16, device=cuda)
+    Y2 = torch.empty((M, K), dtype=torch.float32, device=cuda)
+    xs = [synthetic.bf16_round(synthetic.activations(M, K, seed=70 + i)) * (1 + 3 * i)
+          for i in range(3)]
+    y1s, y2s = [], []
+    for x in xs:
+        X.copy_(torch.from_numpy(x).to(torch.bfloat16))
+        nvfp4.nvfp4_linear_forward(la, Wa, Sa, X, Y1, M)
+        nvfp4.nvfp4_linear_forward(lb, Wb, Sb, Y1, Y2, M)
+        y1s.append(Y1.clone())
+        y2s.append(Y2.clone())
+    torch.cuda.synchronize()
+    for i, x in enumerate(xs):
+        y1 = y1s[i].float().cpu().numpy()
+        assert rel_err(y1, O.linear(wa["w"], wa["sf"], x, ws2_rows=wa["ws2"])) <= TOL_BF16, i
+        ref2 = O.linear(wb["w"], wb["sf"], y1, ws2_rows=wb["ws2"])
+        assert rel_err(y2s[i].cpu().numpy(), ref2) <= 1e-5, i
+
+
 def test_decode_gemv_activation_range(O, cuda):
     """Per-token power-of-two scaling of the f16 activations: tokens far
     outside the f16 range (|x| ~ 1e30, 1e-30), an all-zero token, and

@@ -142,6 +142,45 @@ def test_experts_rows_and_invalid_ids(O, cuda):
         assert rel_err(got[r], y) <= TOL, r
 
 
+@pytest.mark.parametrize("E,H,I", [(16, 512, 256), (128, 2048, 768)])
+def test_experts_gemv_path_repeated(O, cuda, E, H, I):
+    """Expert GEMMs on the decode GEMV path (shapes with H, I % 256 == 0 and
+    few rows per expert): one expert with 3 full items of 8 rows, others with
+    1-2 rows, rows with expert id -1; called twice in a row on fresh inputs
+    with the same workspace (the second call must not see the first's
+    data).  fp32 rows within 1e-3 RMS of the oracle's expert chain."""
+    from nvfp4.moe import moe_experts
+
+    R = 64
+    wd, _, w = setup(E=E, H=H, I=I, T=1, seed=31)
+    rng = np.random.default_rng(32)
+    ws = torch.empty(1 << 26, dtype=torch.uint8, device="cuda")
+    for call in range(2):
+        x = synthetic_x(R, H, seed=40 + call, scale=1 + 5 * call)
+        ids = rng.integers(0, E, R).astype(np.int32)
+        ids[:24] = 3
+        ids[[30, 41]] = -1
+        out = torch.full((R, H), 7.0, dtype=torch.float32, device="cuda")
+        moe_experts(w, torch.from_numpy(x).cuda().to(torch.bfloat16),
+                    torch.from_numpy(ids).cuda(), out=out, top_k=2, workspace=ws)
+        got = out.cpu().numpy()
+        assert np.all(got[[30, 41]] == 7.0)
+        for r in range(R):
+            if ids[r] < 0:
+                continue
+            e = ids[r]
+            h = O.matvec(wd["gu_w"][e], wd["gu_sf"][e], x[r], ws2_rows=wd["gu_ws2"][e])
+            a = np.array([O.silu(float(v)) for v in h[:I]], np.float32) * h[I:]
+            y = O.matvec(wd["dn_w"][e], wd["dn_sf"][e], a, ws2_rows=wd["dn_ws2"][e])
+            assert rel_err(got[r], y) <= 1e-3, (call, r)
+
+
+def synthetic_x(R, H, seed, scale=1.0):
+    from nvfp4 import synthetic
+
+    return synthetic.bf16_round(synthetic.activations(R, H, seed=seed) * scale)
+
+
 def test_workspace_too_small_is_an_error(cuda):
     import ctypes
 
