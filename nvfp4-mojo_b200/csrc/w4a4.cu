@@ -130,7 +130,9 @@ struct FqSmem {
   static constexpr int bytes = offTmem + 16;
   static constexpr int alloc = bytes + 1024;
   static_assert(kStage % 1024 == 0, "stages stay 1024-byte aligned");
+  static_assert(alloc <= 227 * 1024, "shared memory per CTA");
 };
+static_assert(2 * kFqBN + kFqStages * kFqSfCols <= kFqTmemCols, "TMEM columns");
 
 // Instruction descriptor, kind::mxf4nvf4: E2M1 x E2M1, UE4M3 scales per 16,
 // fp32 accumulate, both operands K-major, scale-factor ids 0.

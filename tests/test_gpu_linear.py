@@ -53,6 +53,10 @@ def test_dequant_fp32_bit_exact_all_codes(O, cuda):
     got = nvfp4.dequant(dev(w), dev(sf), torch.float32).cpu().numpy()
     assert np.array_equal(bits32(got), bits32(ref))
     assert np.signbit(got[0, 8]) and got[0, 8] == 0.0  # code 8 -> -0.0
+    # Into a caller buffer (the form the dequant microbenchmark uses).
+    out = torch.full(ref.shape, float("nan"), dtype=torch.float32, device=cuda)
+    nvfp4.dequant(dev(w), dev(sf), out=out)
+    assert np.array_equal(bits32(out.cpu().numpy()), bits32(ref))
 
 
 def test_dequant_bf16_bit_exact_all_codes(O, cuda):
