@@ -238,6 +238,38 @@ int nvfp4_moe_forward_noalloc(const nvfp4_moe_desc *desc, const nvfp4_moe_weight
                               const void *x, const void *residual, void *y, int y_dtype,
                               int64_t T, int32_t *topk_ids, float *topk_w, void *stream);
 
+/*
+ * Shared expert.  The reference loads it
+ * (`model.layers.{l}.mlp.shared_expert.{gate,up,down}_proj`,
+ * nvfp4/weight_loader.mojo:771, :788-790, :881-884) but computes nothing with
+ * it.  nvfp4_moe_forward_shared is nvfp4_moe_forward plus one always-on
+ * expert: y = sum_j w_j * expert_{e_j}(x) + shared(x) (+ residual), the
+ * shared expert's output added with weight 1 after the routed sum.  `shared`
+ * describes a one-expert stack (E = 1) in the layout above, gate_up rows
+ * [0, 2*shared_intermediate), down rows [0, H); its router is ignored.  The
+ * workspace is nvfp4_moe_shared_workspace_size() bytes (more than
+ * nvfp4_moe_workspace_size: the shared expert's rows and fp32 output).
+ */
+size_t nvfp4_moe_shared_workspace_size(const nvfp4_moe_desc *desc, int32_t shared_intermediate,
+                                       int64_t T);
+int nvfp4_moe_forward_shared(const nvfp4_moe_desc *desc, const nvfp4_moe_weights *weights,
+                             const nvfp4_moe_weights *shared, int32_t shared_intermediate,
+                             const void *x, const void *residual, void *y, int y_dtype,
+                             int64_t T, int32_t *topk_ids, float *topk_w, void *workspace,
+                             size_t workspace_bytes, void *stream);
+
+/*
+ * Row-concatenation prepack: dst = srcs[0] rows ++ srcs[1] rows ++ ..., each
+ * source rows[i] rows of row_bytes bytes (device or host memory; one
+ * stream-ordered copy per source).  Turns the reference's separate per-expert
+ * gate_proj / up_proj linears (nvfp4/weight_loader.mojo:876-877) into the
+ * stacked gate_up layout above: for each expert, gate rows then up rows, for
+ * the packed codes (row_bytes K/2), the block scales (K/16) and the per-row
+ * weight_scale_2 (4).
+ */
+int nvfp4_stack_rows(const void *const *srcs, const int64_t *rows, int32_t n,
+                     int64_t row_bytes, void *dst, void *stream);
+
 /* Router alone: topk_ids int32 [T, k], topk_w fp32 [T, k]; logits fp32
  * [T, E] is caller memory the router writes (and the caller may read).  The
  * arithmetic is that of nvfp4_moe_forward's router (same logits bit for

@@ -632,7 +632,8 @@ __device__ __forceinline__ void load8<uint16_t>(const uint16_t *p, float (&v)[8]
 template <typename SlotT, typename OutT>
 __global__ void moe_combine_kernel(const SlotT *__restrict__ ys, const float *__restrict__ w,
                                    const uint16_t *__restrict__ residual,
-                                   const int32_t *__restrict__ slot_pos, OutT *__restrict__ y,
+                                   const int32_t *__restrict__ slot_pos,
+                                   const float *__restrict__ extra, OutT *__restrict__ y,
                                    int T, int k, int H) {
   const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;  // vector index
   const int hv = H / 8;
@@ -649,6 +650,12 @@ __global__ void moe_combine_kernel(const SlotT *__restrict__ ys, const float *__
     load8<SlotT>(ys + row * H + 8 * h8, v);
 #pragma unroll
     for (int q = 0; q < 8; ++q) s[q] = fmaf(wj, v[q], s[q]);
+  }
+  if (extra) {  // fp32 rows added after the routed sum (the shared expert)
+    float e[8];
+    load8<float>(extra + (int64_t)t * H + 8 * h8, e);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) s[q] += e[q];
   }
   if (residual) {
     float r[8];
@@ -669,21 +676,22 @@ __global__ void moe_combine_kernel(const SlotT *__restrict__ ys, const float *__
 }
 
 cudaError_t launch_moe_combine(const void *ys, int ys_dtype, const float *w,
-                               const uint16_t *residual, const int32_t *slot_pos, void *y,
-                               int y_dtype, int T, int k, int H, cudaStream_t st) {
+                               const uint16_t *residual, const int32_t *slot_pos,
+                               const float *extra, void *y, int y_dtype, int T, int k, int H,
+                               cudaStream_t st) {
   const int64_t n = (int64_t)T * (H / 8);
   if (n == 0) return cudaSuccess;
   const unsigned blocks = (unsigned)((n + 255) / 256);
   const float *yf = static_cast<const float *>(ys);
   const uint16_t *yb = static_cast<const uint16_t *>(ys);
   if (ys_dtype == kF32 && y_dtype == kF32)
-    moe_combine_kernel<float, float><<<blocks, 256, 0, st>>>(yf, w, residual, slot_pos, static_cast<float *>(y), T, k, H);
+    moe_combine_kernel<float, float><<<blocks, 256, 0, st>>>(yf, w, residual, slot_pos, extra, static_cast<float *>(y), T, k, H);
   else if (ys_dtype == kF32)
-    moe_combine_kernel<float, uint16_t><<<blocks, 256, 0, st>>>(yf, w, residual, slot_pos, static_cast<uint16_t *>(y), T, k, H);
+    moe_combine_kernel<float, uint16_t><<<blocks, 256, 0, st>>>(yf, w, residual, slot_pos, extra, static_cast<uint16_t *>(y), T, k, H);
   else if (y_dtype == kF32)
-    moe_combine_kernel<uint16_t, float><<<blocks, 256, 0, st>>>(yb, w, residual, slot_pos, static_cast<float *>(y), T, k, H);
+    moe_combine_kernel<uint16_t, float><<<blocks, 256, 0, st>>>(yb, w, residual, slot_pos, extra, static_cast<float *>(y), T, k, H);
   else
-    moe_combine_kernel<uint16_t, uint16_t><<<blocks, 256, 0, st>>>(yb, w, residual, slot_pos, static_cast<uint16_t *>(y), T, k, H);
+    moe_combine_kernel<uint16_t, uint16_t><<<blocks, 256, 0, st>>>(yb, w, residual, slot_pos, extra, static_cast<uint16_t *>(y), T, k, H);
   return cudaGetLastError();
 }
 

@@ -51,9 +51,12 @@ cudaError_t launch_router(const uint16_t *x, const float *router, float *part, i
 cudaError_t launch_moe_permute(const int32_t *row_expert, const int32_t *x_row_index, int R, int E,
                                int tpi, const MoePlan &plan, cudaStream_t st);
 cudaError_t launch_slot_token(int32_t *idx, int R, int k, cudaStream_t st);
+// extra (nullable): fp32 rows [T, H] added after the routed sum, before the
+// residual (the shared expert's output).
 cudaError_t launch_moe_combine(const void *ys, int ys_dtype, const float *w,
-                               const uint16_t *residual, const int32_t *slot_pos, void *y,
-                               int y_dtype, int T, int k, int H, cudaStream_t st);
+                               const uint16_t *residual, const int32_t *slot_pos,
+                               const float *extra, void *y, int y_dtype, int T, int k, int H,
+                               cudaStream_t st);
 cudaError_t launch_ep_plan(const int32_t *ids, int R, int k, int epr, int world, int32_t *counts,
                            int32_t *send_token, int32_t *send_expert, int32_t *slot_pos,
                            cudaStream_t st);

@@ -367,8 +367,9 @@ extern "C" int nvfp4_moe_combine(const void *y_slots, int slot_dtype, const floa
   if (!aligned(y_slots, 16) || !aligned(y, 16) || (residual && !aligned(residual, 16)))
     return fail(NVFP4_ERR_INVALID_ARG, "combine buffers must be 16-byte aligned");
   return check_launch(launch_moe_combine(y_slots, slot_dtype, topk_w,
-                                         static_cast<const uint16_t *>(residual), slot_pos, y,
-                                         y_dtype, (int)T, k, H, static_cast<cudaStream_t>(stream)),
+                                         static_cast<const uint16_t *>(residual), slot_pos,
+                                         nullptr, y, y_dtype, (int)T, k, H,
+                                         static_cast<cudaStream_t>(stream)),
                       "combine launch");
 }
 
@@ -422,15 +423,56 @@ extern "C" int nvfp4_ep_dispatch_padded(const int32_t *send_counts, const int32_
                       "padded dispatch launch");
 }
 
-extern "C" int nvfp4_moe_forward(const nvfp4_moe_desc *d, const nvfp4_moe_weights *w,
-                                 const void *x, const void *residual, void *y, int y_dtype,
-                                 int64_t T,
-                                 int32_t *topk_ids, float *topk_w, void *ws, size_t ws_bytes,
-                                 void *stream) {
+namespace nvfp4 {
+namespace {
+
+// The shared expert's part of the workspace: its fp32 output rows [T, H], the
+// expert id (0) and the x row (t) of each of its T slots, and its own expert
+// workspace.
+struct SharedLayout {
+  size_t y_shared, ids0, idx, experts, total;
+};
+
+nvfp4_moe_desc shared_desc(const nvfp4_moe_desc &d, int32_t shared_intermediate) {
+  nvfp4_moe_desc s = d;
+  s.num_experts = 1;
+  s.top_k = 1;
+  s.intermediate = shared_intermediate;
+  s.renormalize = 0;
+  return s;
+}
+
+SharedLayout shared_layout(const nvfp4_moe_desc &ds, int64_t T) {
+  SharedLayout L;
+  size_t o = 0;
+  L.y_shared = o;
+  o = up(o + sizeof(float) * T * ds.hidden);
+  L.ids0 = o;
+  o = up(o + sizeof(int32_t) * T);
+  L.idx = o;
+  o = up(o + sizeof(int32_t) * T);
+  L.experts = o;
+  o = up(o + experts_layout(ds, T).total);
+  L.total = o;
+  return L;
+}
+
+// One MoE layer; with `shared` (nullable) the shared expert's output (every
+// token, weight 1) is added after the routed sum, before the residual.
+int moe_forward_impl(const nvfp4_moe_desc *d, const nvfp4_moe_weights *w,
+                     const nvfp4_moe_weights *shared, int32_t shared_intermediate, const void *x,
+                     const void *residual, void *y, int y_dtype, int64_t T, int32_t *topk_ids,
+                     float *topk_w, void *ws, size_t ws_bytes, void *stream) {
   int rc = check_desc(d);
   if (rc) return rc;
   if ((rc = check_weights(w))) return rc;
   if (!w->router) return fail(NVFP4_ERR_INVALID_ARG, "null router pointer");
+  nvfp4_moe_desc ds = {};
+  if (shared) {
+    ds = shared_desc(*d, shared_intermediate);
+    if ((rc = check_desc(&ds))) return rc;
+    if ((rc = check_weights(shared))) return rc;
+  }
   if (T < 0 || T * d->top_k > (1 << 24)) return fail(NVFP4_ERR_INVALID_ARG, "bad token count");
   if (T == 0) return NVFP4_OK;
   if (!x || !y || !ws) return fail(NVFP4_ERR_INVALID_ARG, "null activation, output or workspace");
@@ -440,8 +482,9 @@ extern "C" int nvfp4_moe_forward(const nvfp4_moe_desc *d, const nvfp4_moe_weight
       !aligned(ws, kAlign))
     return fail(NVFP4_ERR_INVALID_ARG, "x/y/residual must be 16-byte and workspace 256-byte aligned");
   const ForwardLayout L = forward_layout(*d, T);
-  if (ws_bytes < L.total)
-    return fail(NVFP4_ERR_WORKSPACE, "workspace of %zu bytes, %zu needed", ws_bytes, L.total);
+  const size_t need = L.total + (shared ? shared_layout(ds, T).total : 0);
+  if (ws_bytes < need)
+    return fail(NVFP4_ERR_WORKSPACE, "workspace of %zu bytes, %zu needed", ws_bytes, need);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint8_t *base = static_cast<uint8_t *>(ws);
   int32_t *ids = topk_ids ? topk_ids : reinterpret_cast<int32_t *>(base + L.ids);
@@ -461,7 +504,73 @@ extern "C" int nvfp4_moe_forward(const nvfp4_moe_desc *d, const nvfp4_moe_weight
   rc = run_experts(*d, *w, static_cast<const uint16_t *>(x), slot_tok, ids, R, y_slot, kF32,
                    base + L.experts, st);
   if (rc) return rc;
+  float *y_shared = nullptr;
+  if (shared) {
+    // Every token is one slot of expert 0 of the one-expert "layer".
+    uint8_t *sb = base + L.total;
+    const SharedLayout SL = shared_layout(ds, T);
+    y_shared = reinterpret_cast<float *>(sb + SL.y_shared);
+    int32_t *ids0 = reinterpret_cast<int32_t *>(sb + SL.ids0);
+    int32_t *idx = reinterpret_cast<int32_t *>(sb + SL.idx);
+    rc = check_launch(cudaMemsetAsync(ids0, 0, sizeof(int32_t) * T, st), "shared expert ids");
+    if (rc) return rc;
+    rc = check_launch(launch_slot_token(idx, (int)T, 1, st), "shared expert rows");
+    if (rc) return rc;
+    rc = run_experts(ds, *shared, static_cast<const uint16_t *>(x), idx, ids0, T, y_shared, kF32,
+                     sb + SL.experts, st);
+    if (rc) return rc;
+  }
   return check_launch(launch_moe_combine(y_slot, kF32, tw, static_cast<const uint16_t *>(residual),
-                                         nullptr, y, y_dtype, (int)T, d->top_k, d->hidden, st),
+                                         nullptr, y_shared, y, y_dtype, (int)T, d->top_k,
+                                         d->hidden, st),
                       "combine launch");
+}
+
+}  // namespace
+}  // namespace nvfp4
+
+extern "C" int nvfp4_moe_forward(const nvfp4_moe_desc *d, const nvfp4_moe_weights *w,
+                                 const void *x, const void *residual, void *y, int y_dtype,
+                                 int64_t T, int32_t *topk_ids, float *topk_w, void *ws,
+                                 size_t ws_bytes, void *stream) {
+  return moe_forward_impl(d, w, nullptr, 0, x, residual, y, y_dtype, T, topk_ids, topk_w, ws,
+                          ws_bytes, stream);
+}
+
+extern "C" size_t nvfp4_moe_shared_workspace_size(const nvfp4_moe_desc *d,
+                                                  int32_t shared_intermediate, int64_t T) {
+  if (check_desc(d) || T < 0) return 0;
+  const nvfp4_moe_desc ds = shared_desc(*d, shared_intermediate);
+  if (check_desc(&ds)) return 0;
+  return forward_layout(*d, T).total + shared_layout(ds, T).total;
+}
+
+extern "C" int nvfp4_moe_forward_shared(const nvfp4_moe_desc *d, const nvfp4_moe_weights *w,
+                                        const nvfp4_moe_weights *shared,
+                                        int32_t shared_intermediate, const void *x,
+                                        const void *residual, void *y, int y_dtype, int64_t T,
+                                        int32_t *topk_ids, float *topk_w, void *ws,
+                                        size_t ws_bytes, void *stream) {
+  if (!shared) return fail(NVFP4_ERR_INVALID_ARG, "null shared-expert weights");
+  return moe_forward_impl(d, w, shared, shared_intermediate, x, residual, y, y_dtype, T,
+                          topk_ids, topk_w, ws, ws_bytes, stream);
+}
+
+extern "C" int nvfp4_stack_rows(const void *const *srcs, const int64_t *rows, int32_t n,
+                                int64_t row_bytes, void *dst, void *stream) {
+  if (n < 0 || row_bytes <= 0) return fail(NVFP4_ERR_INVALID_ARG, "bad stack shape");
+  if (n == 0) return NVFP4_OK;
+  if (!srcs || !rows || !dst) return fail(NVFP4_ERR_INVALID_ARG, "null stack pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t *o = static_cast<uint8_t *>(dst);
+  for (int32_t i = 0; i < n; ++i) {
+    if (rows[i] < 0) return fail(NVFP4_ERR_INVALID_ARG, "negative row count at %d", (int)i);
+    if (rows[i] == 0) continue;
+    if (!srcs[i]) return fail(NVFP4_ERR_INVALID_ARG, "null source %d", (int)i);
+    const size_t bytes = (size_t)rows[i] * (size_t)row_bytes;
+    const cudaError_t e = cudaMemcpyAsync(o, srcs[i], bytes, cudaMemcpyDefault, st);
+    if (e != cudaSuccess) return check_launch(e, "row stack copy");
+    o += bytes;
+  }
+  return NVFP4_OK;
 }

@@ -98,6 +98,12 @@ SIGNATURES = {
                                  _vp, _int, _i64, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
     "nvfp4_moe_forward_noalloc": (_int, [ctypes.POINTER(MoEDesc), ctypes.POINTER(MoEWeightPtrs),
                                          _vp, _vp, _vp, _int, _i64, _vp, _vp, _vp]),
+    "nvfp4_moe_shared_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(MoEDesc), ctypes.c_int32,
+                                                          _i64]),
+    "nvfp4_moe_forward_shared": (_int, [ctypes.POINTER(MoEDesc), ctypes.POINTER(MoEWeightPtrs),
+                                        ctypes.POINTER(MoEWeightPtrs), ctypes.c_int32, _vp, _vp,
+                                        _vp, _int, _i64, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
+    "nvfp4_stack_rows": (_int, [_vp, _vp, ctypes.c_int32, _i64, _vp, _vp]),
     "nvfp4_moe_route": (_int, [ctypes.POINTER(MoEDesc), _vp, _vp, _i64, _vp, _vp, _vp, _vp]),
     "nvfp4_moe_experts": (_int, [ctypes.POINTER(MoEDesc), ctypes.POINTER(MoEWeightPtrs), _vp, _vp,
                                  _vp, _i64, _vp, _int, _vp, ctypes.c_size_t, _vp]),

@@ -56,6 +56,34 @@ def test_validation_errors_without_gpu():
         _lib.check(_lib.NVFP4_ERR_INVALID_ARG)
 
 
+def test_shared_expert_and_stack_validation_without_gpu():
+    from nvfp4 import _lib
+
+    L = _lib.load()
+    desc = _lib.MoEDesc(128, 8, 2048, 768, 1)
+    w = _lib.MoEWeightPtrs(16, 16, 16, None, None, 16, 16, None, None)
+    # The shared expert's workspace adds its rows to the routed layer's.
+    for T in (1, 16, 4096):
+        routed = L.nvfp4_moe_workspace_size(ctypes.byref(desc), T)
+        assert L.nvfp4_moe_shared_workspace_size(ctypes.byref(desc), 1024, T) > routed
+    assert L.nvfp4_moe_shared_workspace_size(ctypes.byref(desc), 1000, 16) == 0  # I % 128
+    rc = L.nvfp4_moe_forward_shared(ctypes.byref(desc), ctypes.byref(w), None, 1024, 16, None,
+                                    16, 1, 4, None, None, 256, 1 << 30, None)
+    assert rc == _lib.NVFP4_ERR_INVALID_ARG and b"shared" in L.nvfp4_last_error_string()
+    bad = _lib.MoEWeightPtrs(None, None, 16, None, None, 16, 16, None, None)
+    rc = L.nvfp4_moe_forward_shared(ctypes.byref(desc), ctypes.byref(w), ctypes.byref(bad), 1024,
+                                    16, None, 16, 1, 4, None, None, 256, 1 << 30, None)
+    assert rc == _lib.NVFP4_ERR_INVALID_ARG
+    rc = L.nvfp4_moe_forward_shared(ctypes.byref(desc), ctypes.byref(w), ctypes.byref(w), 1024,
+                                    16, None, 16, 1, 4, None, None, 256, 1024, None)
+    assert rc == _lib.NVFP4_ERR_WORKSPACE
+    assert L.nvfp4_stack_rows(None, None, 0, 16, None, None) == _lib.NVFP4_OK
+    rows = (ctypes.c_int64 * 1)(-1)
+    srcs = (ctypes.c_void_p * 1)(16)
+    assert L.nvfp4_stack_rows(srcs, rows, 1, 16, 16, None) == _lib.NVFP4_ERR_INVALID_ARG
+    assert L.nvfp4_stack_rows(srcs, rows, 1, 0, 16, None) == _lib.NVFP4_ERR_INVALID_ARG
+
+
 def test_python_api_refuses_host_tensors():
     import torch
     import nvfp4

@@ -213,3 +213,85 @@ def test_moe_tensor_core_path_config3(O, cuda):
     wd, x, w = setup(E=128, H=2048, I=768, T=T, seed=33)
     tok = np.sort(np.random.default_rng(34).choice(T, 64, replace=False))
     check_layer(O, wd, x, w, k=8, tokens=tok)
+
+
+def shared_expert_dict(H, Is, seed):
+    """A one-expert stack whose zero router [H, 1] gives every token weight 1:
+    the oracle's MoE layer over it is the shared expert alone."""
+    from nvfp4 import synthetic
+
+    sd = synthetic.moe_weights(1, H, Is, seed=seed)
+    sd["router"] = np.zeros((H, 1), np.float32)
+    return sd
+
+
+@pytest.mark.parametrize("T,E,H,I,Is,k", [(1, 16, 512, 256, 512, 4),
+                                          (16, 128, 2048, 768, 1024, 8),
+                                          (40, 16, 512, 256, 512, 4),
+                                          (300, 16, 512, 256, 768, 4)])
+def test_moe_shared_expert(O, cuda, T, E, H, I, Is, k):
+    """Routed experts plus the always-on shared expert (weight 1), with a
+    residual: the shared expert's rows take the GEMV (T <= 32), skinny (T = 40)
+    and tensor-core (T = 300) expert paths.  Oracle: the routed layer plus the
+    shared expert as a one-expert layer, summed in fp32 in that order."""
+    from nvfp4.moe import MoELayer, MoEWeights
+
+    wd, x, w = setup(E=E, H=H, I=I, T=T, seed=50 + T)
+    sd = shared_expert_dict(H, Is, seed=60 + T)
+    shared = MoEWeights.from_dict({kk: v for kk, v in sd.items() if kk != "router"})
+    res = synthetic_x(T, H, seed=70 + T)
+    layer = MoELayer(w, top_k=k, shared=shared)
+    X = torch.from_numpy(x).cuda().to(torch.bfloat16)
+    Rz = torch.from_numpy(res).cuda().to(torch.bfloat16)
+    ids = torch.empty((T, k), dtype=torch.int32, device="cuda")
+    y = layer(X, residual=Rz, topk_ids=ids).float().cpu().numpy()
+    y32 = layer(X, residual=Rz, out=torch.empty((T, H), dtype=torch.float32, device="cuda"))
+    y32 = y32.cpu().numpy()
+    ids = ids.cpu().numpy()
+    _, probs = O.router(x, wd["router"])
+    ties = near_ties(probs, k)
+    routed, ref_ids, _ = O.moe(x, wd, top_k=k, n_threads=8)
+    mismatch = [t for t in range(T) if not np.array_equal(ref_ids[t], ids[t])]
+    assert all(ties[t] for t in mismatch), mismatch[:5]
+    if mismatch:
+        routed, _, _ = O.moe(x, wd, top_k=k, force_ids=ids, n_threads=8)
+    sh, sh_ids, sh_w = O.moe(x, sd, top_k=1, n_threads=8)
+    assert np.all(sh_ids == 0) and np.all(sh_w == 1.0)
+    ref = (routed + sh) + res
+    rms = np.sqrt(np.mean(ref.astype(np.float64) ** 2))
+    assert (np.abs(y - ref) - (TOL * rms + 2.0 ** -8 * np.abs(ref))).max() <= 0.0
+    assert rel_err(y32, ref) <= 1e-3
+    # The shared expert's contribution is not lost in the residual.
+    assert rel_err(y32 - (routed + res), sh) <= 1e-2
+
+
+def test_stack_gate_up_prepack(O, cuda):
+    """Separate per-expert gate_proj / up_proj linears (different input scales,
+    one of them a per-tensor weight_scale_2) stacked by nvfp4_stack_rows give
+    the stacked layout bit for bit, with the input scales folded into the
+    per-row scales; the layer over them matches the oracle."""
+    from nvfp4.moe import MoEWeights, stack_gate_up
+
+    E, H, I, T, k = 4, 256, 128, 24, 2
+    wd, x, _ = setup(E=E, H=H, I=I, T=T, seed=81)
+    rng = np.random.default_rng(82)
+    ins = rng.uniform(0.5, 2.0, (E, 2)).astype(np.float32)
+    wd["gu_ws2"][2, :I] = wd["gu_ws2"][2, 0]  # expert 2's gate_proj: one scale
+    gates, ups = [], []
+    for e in range(E):
+        g_ws2 = np.float32(wd["gu_ws2"][e, 0]) if e == 2 else torch.from_numpy(wd["gu_ws2"][e, :I])
+        gates.append({"w": torch.from_numpy(wd["gu_w"][e, :I]).cuda(),
+                      "sf": torch.from_numpy(wd["gu_sf"][e, :I]),
+                      "ws2": g_ws2, "in": ins[e, 0]})
+        ups.append({"w": torch.from_numpy(wd["gu_w"][e, I:]),
+                    "sf": torch.from_numpy(wd["gu_sf"][e, I:]).cuda(),
+                    "ws2": torch.from_numpy(wd["gu_ws2"][e, I:]), "in": ins[e, 1]})
+    gw, gsf, gws2 = stack_gate_up(gates, ups)
+    torch.cuda.synchronize()
+    assert np.array_equal(gw.cpu().numpy(), wd["gu_w"])
+    assert np.array_equal(gsf.cpu().numpy(), wd["gu_sf"])
+    folded = wd["gu_ws2"] * np.repeat(ins, I, axis=1)
+    assert np.array_equal(gws2.cpu().numpy(), folded)
+    wd["gu_ws2"] = folded
+    w = MoEWeights.from_dict(dict(wd, gu_w=gw, gu_sf=gsf, gu_ws2=gws2))
+    check_layer(O, wd, x, w, k=k)
