@@ -155,7 +155,7 @@ class GemvSweep:
         self.bytes_per_step = sum(c[5] for c in self.calls[0])
         self.launches_per_step = len(self.calls[0])
         self.dominant_bytes = gemv_bytes(4096, 14336)
-        self.dominant_name = "skinny_kernel (decode GEMV, K=4096 N=14336)"
+        self.dominant_name = "gemv_kernel (decode GEMV, K=4096 N=14336)"
         self.config = {"workload": self.workload, "shapes_KN": GEMV_SHAPES, "M": GEMV_MS,
                        "l2": "inputs larger than L2: two weight sets (2 x 143 MB) alternate per step"}
 

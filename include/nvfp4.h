@@ -105,6 +105,11 @@ int nvfp4_device_status(void);
  * activations are quantized to NVFP4 with input_scale (nvfp4_quantize_act,
  * into stream-ordered scratch from cudaMallocAsync) and multiplied on the
  * block-scaled FP4 tensor cores (nvfp4_linear_w4a4); in_features % 256 == 0.
+ * The decode GEMV is launched with programmatic dependent launch and starts
+ * reading the weights, blockscales and weight_scale_2 before the preceding
+ * kernel in the stream has finished (activations and output only after it):
+ * do not write those weight buffers with the kernel launched immediately
+ * before this call on the same stream.
  */
 int nvfp4_linear_forward(const nvfp4_linear_desc *linear, const uint8_t *packed_weights,
                          const uint8_t *blockscales, const void *activations,

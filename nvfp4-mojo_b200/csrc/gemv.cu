@@ -189,6 +189,104 @@ __device__ __forceinline__ void gemv_compute(const GemvChunk &b, float (&acc)[4]
   }
 }
 
+// E2M1x2 -> f16x2 of byte i (0..3) of w (low nibble -> low half).
+template <int I>
+__device__ __forceinline__ uint32_t e2m1_byte_to_f16x2(uint32_t w) {
+  uint32_t d;
+  if constexpr (I == 0)
+    asm("{.reg .b8 b0, b1, b2, b3;\n mov.b32 {b0, b1, b2, b3}, %1;\n cvt.rn.f16x2.e2m1x2 %0, b0;}"
+        : "=r"(d) : "r"(w));
+  else if constexpr (I == 1)
+    asm("{.reg .b8 b0, b1, b2, b3;\n mov.b32 {b0, b1, b2, b3}, %1;\n cvt.rn.f16x2.e2m1x2 %0, b1;}"
+        : "=r"(d) : "r"(w));
+  else if constexpr (I == 2)
+    asm("{.reg .b8 b0, b1, b2, b3;\n mov.b32 {b0, b1, b2, b3}, %1;\n cvt.rn.f16x2.e2m1x2 %0, b2;}"
+        : "=r"(d) : "r"(w));
+  else
+    asm("{.reg .b8 b0, b1, b2, b3;\n mov.b32 {b0, b1, b2, b3}, %1;\n cvt.rn.f16x2.e2m1x2 %0, b3;}"
+        : "=r"(d) : "r"(w));
+  return d;
+}
+
+// The four blockscales of a scale word as fp32 (E4M3 -> f16 is exact, f16 -> f32 too).
+__device__ __forceinline__ void scale_word_f32(uint32_t sw, float (&f)[4]) {
+  const uint32_t lo = scale_pair_f16x2(sw, 0), hi = scale_pair_f16x2(sw, 1);
+  const __half2 l = *reinterpret_cast<const __half2 *>(&lo);
+  const __half2 h = *reinterpret_cast<const __half2 *>(&hi);
+  f[0] = __low2float(l);
+  f[1] = __high2float(l);
+  f[2] = __low2float(h);
+  f[3] = __high2float(h);
+}
+
+__device__ __forceinline__ uint2 lds_v2(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+  return v;
+}
+
+// One 256-k chunk for a single token (M = 1), with the blockscales applied
+// after the MMAs instead of to every weight.  The MMA's 8 columns carry 8
+// different 16-k blocks ("block-diagonal" B): in MMA j (0..15) lane quad c
+// supplies byte j/2 of its block 4c + (j & 1) as k pair slot 0 (column 2c)
+// and of its block 4c + 2 + (j & 1) as slot 1 (column 2c + 1); the B fragment
+// of lane (g, c) is the token's x pair of that byte where g is the slot's
+// column (g = 2c: slot 0, g = 2c + 1: slot 1) and zero elsewhere.  Each
+// column then accumulates one block's products over the 8 MMAs of equal
+// parity, and the lane's own D columns are exactly its own blocks, so the
+// lane scales them with its own blockscales (8 FMAs per chunk).  Slot 0 of
+// lane quad c reads x units ub + {0..3} (ub = 32 ch + 8c: its blocks 4c,
+// 4c + 1), slot 1 units ub + {4..7} (blocks 4c + 2, 4c + 3); lanes that own
+// neither read the 64-byte zero row.  The codes of rows rl and rl + 8 are
+// read from the staged 128-byte-swizzled tile per parity (8 words at a
+// time); `release` runs once all of the chunk's operands are in registers.
+template <class Release>
+__device__ __forceinline__ void gemv_compute_m1(uint32_t codes, uint32_t sgw, uint32_t shw,
+                                                int rl, int c, float (&tot)[2],
+                                                uint32_t xrow, uint32_t zero, bool own_a,
+                                                bool own_b, int ub, Release release) {
+  const int sw = rl & 7;
+  const uint32_t rg = codes + 128u * rl, rh = rg + 128u * 8;
+  const uint32_t u0 = 16u * ((2 * c) ^ sw), u1 = 16u * ((2 * c + 1) ^ sw);
+  float e[4] = {0.0f, 0.0f, 0.0f, 0.0f}, o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+  for (int par = 0; par < 2; ++par) {
+    // Words 2q + hf of a row's 8 hold bytes 4 hf .. 4 hf + 3 of its block q:
+    // block par is in the first 16-byte unit, block 2 + par in the second.
+    const uint2 g01 = lds_v2(rg + u0 + 8u * par), g23 = lds_v2(rg + u1 + 8u * par);
+    const uint2 h01 = lds_v2(rh + u0 + 8u * par), h23 = lds_v2(rh + u1 + 8u * par);
+    if (par == 1) release();
+    float(&d)[4] = par ? o : e;
+    // Not unrolled: unrolling both halves lets the compiler hoist the
+    // conversions of both, which needs ~25 more registers than the launch
+    // bound leaves.
+#pragma unroll 1
+    for (int hf = 0; hf < 2; ++hf) {
+      // Unit v = 2 par + hf of the lane's four: x pairs of bytes 4 hf .. 4 hf + 3
+      // of its block par (slot 0) and 2 + par (slot 1).
+      const int v = 2 * par + hf;
+      const uint32_t za = zero + 16u * (uint32_t)v;
+      const uint4 va = lds_v4(own_a ? xrow + 16u * (uint32_t)xs_unit(ub + v) : za);
+      const uint4 vb = lds_v4(own_b ? xrow + 16u * (uint32_t)xs_unit(ub + 4 + v) : za);
+      const uint32_t g0 = hf ? g01.y : g01.x, g1 = hf ? g23.y : g23.x;
+      const uint32_t h0 = hf ? h01.y : h01.x, h1 = hf ? h23.y : h23.x;
+      mma_f16_16816(d, e2m1_byte_to_f16x2<0>(g0), e2m1_byte_to_f16x2<0>(h0),
+                    e2m1_byte_to_f16x2<0>(g1), e2m1_byte_to_f16x2<0>(h1), va.x, vb.x);
+      mma_f16_16816(d, e2m1_byte_to_f16x2<1>(g0), e2m1_byte_to_f16x2<1>(h0),
+                    e2m1_byte_to_f16x2<1>(g1), e2m1_byte_to_f16x2<1>(h1), va.y, vb.y);
+      mma_f16_16816(d, e2m1_byte_to_f16x2<2>(g0), e2m1_byte_to_f16x2<2>(h0),
+                    e2m1_byte_to_f16x2<2>(g1), e2m1_byte_to_f16x2<2>(h1), va.z, vb.z);
+      mma_f16_16816(d, e2m1_byte_to_f16x2<3>(g0), e2m1_byte_to_f16x2<3>(h0),
+                    e2m1_byte_to_f16x2<3>(g1), e2m1_byte_to_f16x2<3>(h1), va.w, vb.w);
+    }
+  }
+  float sg[4], sh[4];
+  scale_word_f32(sgw, sg);
+  scale_word_f32(shw, sh);
+  tot[0] += sg[0] * e[0] + sg[2] * e[1] + sg[1] * o[0] + sg[3] * o[1];
+  tot[1] += sh[0] * e[2] + sh[2] * e[3] + sh[1] * o[2] + sh[3] * o[3];
+}
+
 constexpr int kGvMaxWarps = 13;    // consumer warps: 2 CTAs of 14 warps per SM
 constexpr int kGvTileCodes = 16 * (kGvChunk / 2);       // 2 KB: one 16-row tile
 constexpr int kGvTileScales = 16 * (kGvChunk / kGroup);  // 256 B
@@ -197,12 +295,13 @@ constexpr int kGvSmemCap = 110 * 1024;  // dynamic shared memory per CTA (two pe
 
 // Shared memory of a CTA with `w` consumer warps, `stages` ring stages, `m`
 // token rows of x (twice for hi + lo), a K split of `cs` and `parts` partial
-// sums per owned row (2 for gate + up): the ring, the f16 x slice(s), the
-// receive buffer of the cluster reduction ([cs][per][parts][8] fp32, per =
+// sums per owned row (2 for gate + up): the ring, the f16 x slice(s), 64 zero
+// bytes (single-token B fragments), the receive buffer of the cluster
+// reduction ([cs][per][parts][8] fp32, per =
 // ceil(16 w / parts / cs)), per-token scales and exponents, alpha of the rows
 // this CTA finalises, the mbarriers.
 struct GemvSmem {
-  int stage, codes, ring, xs, xs_lo, recv, inv, emax, alpha, bars, total;
+  int stage, codes, ring, xs, xs_lo, zero, recv, inv, emax, alpha, bars, total;
   __host__ __device__ GemvSmem(int w, int stages, int xstride, int m, int cs, int parts,
                                bool split) {
     codes = w * kGvTileCodes;
@@ -210,7 +309,8 @@ struct GemvSmem {
     ring = 0;
     xs = stages * stage;
     xs_lo = xs + m * xstride;
-    recv = xs_lo + (split ? m * xstride : 0);
+    zero = xs_lo + (split ? m * xstride : 0);
+    recv = zero + 64;
     const int per = (16 * w / parts + cs - 1) / cs;
     inv = recv + (int)sizeof(float) * cs * per * parts * kGvTok;
     emax = inv + (int)sizeof(float) * kGvTok;
@@ -251,6 +351,7 @@ __global__ void __launch_bounds__(32 * (kGvMaxWarps + 1), 2)
   uint8_t *ring = gsm + L.ring;
   uint8_t *xs = gsm + L.xs;
   uint8_t *xs_lo = gsm + L.xs_lo;
+  uint32_t *zero_row = reinterpret_cast<uint32_t *>(gsm + L.zero);
   float *recv = reinterpret_cast<float *>(gsm + L.recv);
   float *inv_scale = reinterpret_cast<float *>(gsm + L.inv);
   int *emax = reinterpret_cast<int *>(gsm + L.emax);
@@ -279,10 +380,16 @@ __global__ void __launch_bounds__(32 * (kGvMaxWarps + 1), 2)
     mbar_fence_init();
   }
   if (tid < kGvTok) emax[tid] = 0;
+  if (tid < 16) zero_row[tid] = 0u;
   __syncthreads();
   // Programmatic dependent launch: everything above overlapped the previous
-  // kernel; inputs are read only after it has completed.
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // kernel.  What that kernel may have written (activations, work items,
+  // outputs it still reads) is touched only after griddepcontrol.wait.  In
+  // plain mode the weights are not among it: the producer streams them
+  // before waiting, so that a launch which follows another (it can start on
+  // the SMs that kernel leaves free) has its first stages in flight while
+  // the previous layer finishes.
+  if constexpr (MODE != kGvPlain) asm volatile("griddepcontrol.wait;" ::: "memory");
   // Work item (grouped modes): expert g, token slots [slot0, slot0 + M).
   // The whole cluster shares blockIdx.z, so it leaves together.
   int g = 0, slot0 = 0, M = a.M;
@@ -341,7 +448,10 @@ __global__ void __launch_bounds__(32 * (kGvMaxWarps + 1), 2)
                   &no_abort);
     }
     __syncwarp();
+    // Plain mode: the output stores below come after the previous kernel.
+    if constexpr (MODE == kGvPlain) asm volatile("griddepcontrol.wait;" ::: "memory");
   } else {
+    if constexpr (MODE == kGvPlain) asm volatile("griddepcontrol.wait;" ::: "memory");
     // x slice -> f16 with a per-token power-of-two scale.  The M * ks / 8
     // 16-byte units of the slice are spread over all consumer threads: the
     // largest exponent per token is taken with shared atomicMax, then the
@@ -467,21 +577,57 @@ __global__ void __launch_bounds__(32 * (kGvMaxWarps + 1), 2)
       const bool has_x = gq < M;  // tokens >= M: zero B fragments
       const uint32_t xrow = smem_u32(xs + (has_x ? gq : 0) * a.xstride);
       const uint32_t xrow_lo = smem_u32(xs_lo + (has_x ? gq : 0) * a.xstride);
-      for (int ch = 0; ch < nch; ++ch) {
-        const int s = ch % S, u = ch / S;
-        const bool ok = mbar_wait(full0 + 8 * s, u & 1, &g_gemv_status, kDevTimeoutFull, abort);
-        if (!__all_sync(0xffffffffu, ok)) break;
-        const uint32_t st = smem_u32(ring + s * L.stage);
-        GemvChunk b;
-        gemv_fetch(b, st + warp * kGvTileCodes, st + L.codes + warp * kGvTileScales, gq, c);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(empty0 + 8 * s);  // operands are in registers
-        // The MMA's fp32 accumulation is not IEEE round-to-nearest: chains are
-        // kept to one chunk (16 or 32 MMAs) and chunk sums added with fp32 adds.
-        float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        gemv_compute<kSplit>(b, part, xrow, xrow_lo, has_x, ch, c);
+      if (MODE == kGvPlain && M == 1) {
+        // One token: blockscales applied per block after the MMAs
+        // (gemv_compute_m1); per lane, sums over its own blocks of rows g
+        // and g + 8, added over the lane quad at the end.
+        const uint32_t x0 = smem_u32(xs), zero = smem_u32(zero_row);
+        const bool own_a = gq == 2 * c, own_b = gq == 2 * c + 1;
+        float tot[2] = {0.0f, 0.0f};
+        for (int ch = 0; ch < nch; ++ch) {
+          const int s = ch % S, u = ch / S;
+          const bool ok = mbar_wait(full0 + 8 * s, u & 1, &g_gemv_status, kDevTimeoutFull, abort);
+          if (!__all_sync(0xffffffffu, ok)) break;
+          const uint32_t st = smem_u32(ring + s * L.stage);
+          const uint32_t scales = st + L.codes + warp * kGvTileScales;
+          const uint32_t sgw = lds_u32(scales + 16u * gq + 4u * c);
+          const uint32_t shw = lds_u32(scales + 16u * (gq + 8) + 4u * c);
+          gemv_compute_m1(st + warp * kGvTileCodes, sgw, shw, gq, c, tot, x0, zero, own_a, own_b,
+                          32 * ch + 8 * c, [&] {
+                            fence_proxy_async_smem();  // as in the general path below
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(empty0 + 8 * s);
+                          });
+        }
 #pragma unroll
-        for (int i = 0; i < 4; ++i) acc[i] += part[i];
+        for (int h = 0; h < 2; ++h) {
+          tot[h] += __shfl_xor_sync(0xffffffffu, tot[h], 1);
+          tot[h] += __shfl_xor_sync(0xffffffffu, tot[h], 2);
+        }
+        acc[0] = tot[0];
+        acc[2] = tot[1];
+      } else {
+        for (int ch = 0; ch < nch; ++ch) {
+          const int s = ch % S, u = ch / S;
+          const bool ok = mbar_wait(full0 + 8 * s, u & 1, &g_gemv_status, kDevTimeoutFull, abort);
+          if (!__all_sync(0xffffffffu, ok)) break;
+          const uint32_t st = smem_u32(ring + s * L.stage);
+          GemvChunk b;
+          gemv_fetch(b, st + warp * kGvTileCodes, st + L.codes + warp * kGvTileScales, gq, c);
+          // The stage is refilled by TMA (async proxy) once released: order
+          // these generic-proxy reads before that write.  Without the fence
+          // the refill was seen to overtake the reads (rows of one tile
+          // decoded from the next chunk's codes, a few calls in a hundred).
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(empty0 + 8 * s);  // operands are in registers
+          // The MMA's fp32 accumulation is not IEEE round-to-nearest: chains are
+          // kept to one chunk (16 or 32 MMAs) and chunk sums added with fp32 adds.
+          float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+          gemv_compute<kSplit>(b, part, xrow, xrow_lo, has_x, ch, c);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[i] += part[i];
+        }
       }
       // Partial sums (times 2^-s per token) go straight to the CTA of the
       // cluster that owns the row: slot [slice][row - owner's first row][part].
@@ -621,7 +767,12 @@ cudaError_t launch_mode(GemvArgs a, int items, int64_t total_rows, cudaStream_t 
   const int nck = a.K / kGvChunk;
   const int nt = (MODE == kGvGateUp ? a.N / 2 : a.N + 15) / 16;
   const int max_tiles = kGvMaxWarps / kParts;
-  const int ctas_target = 2 * tc_sm_count();
+  // Plain linear: one CTA per SM (a CTA takes at most half of an SM's shared
+  // memory), so that the CTAs of the next launch in the stream fit beside
+  // this one's and start streaming their weights before it ends.  Grouped
+  // modes read their work items before any load and gain nothing from that:
+  // two CTAs per SM.
+  const int ctas_target = (MODE == kGvPlain ? 1 : 2) * tc_sm_count();
   int bestC = 0, bestW = 0, bestNq = 0, bestS = 0;
   double best_cost = 0.0;
   for (int C = 1; C <= 8; ++C) {

@@ -326,6 +326,10 @@ __global__ void __launch_bounds__(kFqThreads, 1)
         }
         tmem_st_wait();
         tc_fence_before();
+        // The stage's scale factors were read through the generic proxy and
+        // the stage is refilled by TMA (async proxy) after the MMAs: order
+        // the reads before that write.
+        fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar_sf + 8 * s);
       }

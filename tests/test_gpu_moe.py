@@ -295,3 +295,31 @@ def test_stack_gate_up_prepack(O, cuda):
     wd["gu_ws2"] = folded
     w = MoEWeights.from_dict(dict(wd, gu_w=gw, gu_sf=gsf, gu_ws2=gws2))
     check_layer(O, wd, x, w, k=k)
+
+
+def test_experts_gemv_path_repeatable(cuda):
+    """The grouped-GEMV expert path at the config-3 layer with T = 256
+    (2048 slots, items of up to 8 slots): 25 calls with the same routing give
+    bitwise identical expert outputs, although the slot order inside each
+    expert's group (shared-memory atomics) differs from call to call.  Each
+    staged weight chunk must be read before TMA refills its buffer; a refill
+    that overtook the reads corrupted rows of one item in a few calls of 60."""
+    from nvfp4.moe import moe_experts, moe_route
+
+    E, H, I, T, k = 128, 2048, 768, 256, 8
+    R = T * k
+    wd, x, w = setup(E=E, H=H, I=I, T=T, seed=100 + T)
+    X = torch.from_numpy(x).cuda().to(torch.bfloat16)
+    ids, _, _ = moe_route(w, X, top_k=k)
+    row_expert = ids.reshape(-1).contiguous()
+    slot_tok = (torch.arange(R, device="cuda", dtype=torch.int32) // k).contiguous()
+    ws = torch.empty(1 << 26, dtype=torch.uint8, device="cuda")
+    first = None
+    for i in range(25):
+        y = torch.full((R, H), float("nan"), dtype=torch.float32, device="cuda")
+        moe_experts(w, X, row_expert, x_row_index=slot_tok, out=y, top_k=k, workspace=ws)
+        if first is None:
+            first = y
+            assert not torch.isnan(first).any()
+        else:
+            assert torch.equal(y, first), f"call {i} differs"

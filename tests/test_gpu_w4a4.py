@@ -111,3 +111,25 @@ def test_w4a4_prefill_config2_sampled(O, cuda):
                         n_threads=8)
     got = y.cpu().numpy()[np.ix_(rows, cols)]
     assert rel_err(got, ref) <= 1e-4
+
+
+def test_w4a4_repeatable(cuda):
+    """Ten W4A4 GEMMs at M = 512, K = 4096, N = 14336 are bitwise identical
+    (the scale factors staged by TMA are read before the stage is refilled)."""
+    import nvfp4
+    from nvfp4 import synthetic
+
+    M, K, N = 512, 4096, 14336
+    wd = synthetic.linear_weights_cuda(N, K, seed=91)
+    x = torch.randn((M, K), device=cuda).to(torch.bfloat16)
+    ins = float(x.float().abs().max().item() / (6 * 448))
+    lin = nvfp4.NvFp4Linear(K, N, input_scale=ins, weight_scale_2_rows=wd["ws2"])
+    first = None
+    for i in range(10):
+        y = nvfp4.nvfp4_linear(lin, wd["w"], wd["sf"], x, out_dtype=torch.float32,
+                               flags=nvfp4._lib.FLAG_W4A4)
+        if first is None:
+            first = y
+            assert not torch.isnan(first).any()
+        else:
+            assert torch.equal(y, first), f"call {i} differs"
