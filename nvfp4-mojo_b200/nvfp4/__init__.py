@@ -32,6 +32,17 @@ from .nvfp4_gemm_gpu import (
     nvfp4_linear_w4a4,
     quantize_act,
 )
+from .weight_loader import (
+    LoadedWeight,
+    SafetensorsFile,
+    TensorInfo,
+    discover_safetensor_shards,
+    load_linear_safetensors,
+    load_moe_experts,
+    load_qwen35_layer,
+    open_model_shards,
+    open_safetensors,
+)
 from ._lib import LIB_PATH, Nvfp4Error
 
 __all__ = [
@@ -40,5 +51,7 @@ __all__ = [
     "unpack_fp4_pair", "nvfp4_matvec", "sigmoid", "silu", "BK", "BM", "BN", "WM", "WN",
     "FP8_SCALE_DTYPE", "dequant", "load_and_dequant_fp4_tile", "nvfp4_gemm_kernel",
     "nvfp4_linear", "nvfp4_linear_forward", "nvfp4_linear_w4a4", "quantize_act", "LIB_PATH",
-    "Nvfp4Error",
+    "Nvfp4Error", "LoadedWeight", "SafetensorsFile", "TensorInfo", "discover_safetensor_shards",
+    "load_linear_safetensors", "load_moe_experts", "load_qwen35_layer", "open_model_shards",
+    "open_safetensors",
 ]

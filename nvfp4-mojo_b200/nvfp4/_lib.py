@@ -75,6 +75,24 @@ class MoEWeightPtrs(ctypes.Structure):
                 ("down_input_scale", ctypes.c_void_p)]
 
 
+class StTensorInfo(ctypes.Structure):
+    """struct nvfp4_st_tensor_info (include/nvfp4_loader.h)."""
+
+    _fields_ = [("dtype", ctypes.c_char * 16), ("ndim", ctypes.c_int32),
+                ("shape", ctypes.c_int64 * 8), ("data_offset", ctypes.c_int64),
+                ("data_size", ctypes.c_int64)]
+
+
+class StLinearInfo(ctypes.Structure):
+    """struct nvfp4_st_linear_info (include/nvfp4_loader.h)."""
+
+    _fields_ = [("out_features", ctypes.c_int64), ("in_features", ctypes.c_int64),
+                ("weight_scale_2", ctypes.c_float), ("input_scale", ctypes.c_float),
+                ("weight_scale_2_rows", ctypes.c_int32), ("shard", ctypes.c_int32)]
+
+
+ST_FOLD_INPUT_SCALE = 0x1
+
 _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
 _int = ctypes.c_int
@@ -114,6 +132,31 @@ SIGNATURES = {
     "nvfp4_gather_rows": (_int, [_vp, _vp, _i64, _i64, _vp, _vp]),
     "nvfp4_ep_dispatch_padded": (_int, [_vp, _vp, _vp, _vp, _i64, ctypes.c_int32, ctypes.c_int32,
                                         _i64, _vp, _i64, _vp, _vp, _vp, _vp]),
+    # include/nvfp4_loader.h
+    "nvfp4_st_open": (_int, [ctypes.c_char_p, ctypes.POINTER(_vp)]),
+    "nvfp4_st_close": (None, [_vp]),
+    "nvfp4_st_num_tensors": (_i64, [_vp]),
+    "nvfp4_st_tensor_name": (ctypes.c_char_p, [_vp, _i64]),
+    "nvfp4_st_find": (_i64, [_vp, ctypes.c_char_p]),
+    "nvfp4_st_get_tensor_info": (_int, [_vp, _i64, ctypes.POINTER(StTensorInfo)]),
+    "nvfp4_st_read_host": (_i64, [_vp, _i64, _vp, _i64]),
+    "nvfp4_st_read_device": (_int, [_vp, _i64, _vp, _vp]),
+    "nvfp4_st_f32_from_bytes": (_f32, [_vp, _i64]),
+    "nvfp4_st_open_model": (_int, [ctypes.c_char_p, ctypes.POINTER(_vp)]),
+    "nvfp4_st_open_files": (_int, [ctypes.POINTER(ctypes.c_char_p), ctypes.c_int32,
+                                   ctypes.POINTER(_vp)]),
+    "nvfp4_st_close_model": (None, [_vp]),
+    "nvfp4_st_model_num_shards": (ctypes.c_int32, [_vp]),
+    "nvfp4_st_model_shard_path": (ctypes.c_char_p, [_vp, ctypes.c_int32]),
+    "nvfp4_st_model_shard": (_vp, [_vp, ctypes.c_int32]),
+    "nvfp4_st_model_find": (_int, [_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int32),
+                                   ctypes.POINTER(_i64)]),
+    "nvfp4_st_get_linear_info": (_int, [_vp, ctypes.c_char_p, ctypes.POINTER(StLinearInfo)]),
+    "nvfp4_st_load_linear": (_int, [_vp, ctypes.c_char_p, _vp, _vp, _vp, _u32, _vp]),
+    "nvfp4_st_load_experts": (_int, [_vp, ctypes.c_char_p, ctypes.c_int32, ctypes.c_int32,
+                                     ctypes.c_int32, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "nvfp4_st_load_router": (_int, [_vp, ctypes.c_char_p, _vp, ctypes.POINTER(ctypes.c_int32),
+                                    ctypes.POINTER(ctypes.c_int32), _vp]),
     "nvfp4_quantize_act": (_int, [_vp, _int, _i64, _i64, _i64, _f32, _vp, _vp, _vp]),
     "nvfp4_linear_w4a4": (_int, [ctypes.POINTER(LinearDesc), _vp, _vp, _vp, _vp, _vp, _int, _i64,
                                  _vp]),
