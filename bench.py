@@ -528,6 +528,133 @@ class MoELayerBench:
 
 
 # ---------------------------------------------------------------------------
+# Workload: gated DeltaNet decode step (the reference's default layer) with
+# NVFP4 projections, B sequences.
+# ---------------------------------------------------------------------------
+def deltanet_weight_bytes():
+    from nvfp4.deltanet import DeltaNetConfig
+
+    c = DeltaNetConfig()
+    rows = {"qkv": (c.total_qkv_dim(), c.d_model), "z": (c.z_dim(), c.d_model),
+            "b": (c.num_value_heads, c.d_model), "a": (c.num_value_heads, c.d_model),
+            "out": (c.d_model, c.z_dim())}
+    return rows, sum(n * k // 2 + n * k // 16 + 4 * n for (n, k) in rows.values())
+
+
+class DeltaNetBench:
+    name = "deltanet"
+    unit = "tokens/s"
+
+    @staticmethod
+    def describe(tokens, layers=None, world=1):
+        return (f"one gated DeltaNet decode step of the reference's default layer (d_model "
+                f"2048, 16 key / 32 value heads of 128 x 128, conv kernel 4) with NVFP4 "
+                f"projections qkv [8192, 2048], z [4096, 2048], beta / alpha [32, 2048], out "
+                f"[2048, 4096]; {tokens} sequences with their own fp32 state; bf16 activations "
+                f"on the decode GEMV")
+
+    def __init__(self, device, seed=0, tokens=4, layers=8):
+        import torch
+        import nvfp4
+        from nvfp4 import synthetic
+        from nvfp4.deltanet import DeltaNetConfig, DeltaNetState, DeltaNetWeights
+
+        self.torch, self.B = torch, tokens
+        self.cfg = DeltaNetConfig()
+        self.workload = self.describe(tokens)
+        rows, wbytes = deltanet_weight_bytes()
+        c = self.cfg
+        self.layers = []
+        for l in range(layers):
+            g = torch.Generator(device=device)
+            g.manual_seed(seed + 31 * l)
+            proj = {}
+            for i, (name, (n, k)) in enumerate(rows.items()):
+                wd = synthetic.linear_weights_cuda(n, k, seed=seed + 31 * l + i, device=device)
+                proj[name] = (nvfp4.NvFp4Linear(k, n, weight_scale_2_rows=wd["ws2"]),
+                              wd["w"], wd["sf"])
+            r = lambda *shape: torch.randn(shape, generator=g, device=device) * 0.5
+            w = DeltaNetWeights(**proj, a_log=r(c.num_value_heads), dt_bias=r(c.num_value_heads),
+                                conv_q=r(c.q_dim(), c.conv_kernel), conv_k=r(c.k_dim(), c.conv_kernel),
+                                conv_v=r(c.v_dim(), c.conv_kernel))
+            self.layers.append((w, DeltaNetState(c, batch=tokens, device=device)))
+        self.x = torch.randn((tokens, c.d_model), device=device).to(torch.bfloat16)
+        self.y = torch.empty_like(self.x)
+        self.ws = torch.empty(64 << 20, dtype=torch.uint8, device=device)
+        self.sets = layers
+        self.launches_per_step = 7  # 4 projections, conv, recurrence, out projection
+        state_bytes = 2 * 4 * tokens * (c.total_state_floats()
+                                       + (c.q_dim() + c.k_dim() + c.v_dim()) * (c.conv_kernel - 1))
+        self.dominant_bytes = wbytes + state_bytes
+        self.dominant_name = (f"DeltaNet step (B={tokens}): NVFP4 projection weights "
+                              f"{wbytes / 1e6:.1f} MB + fp32 state read and written")
+        self.config = {"workload": self.workload, "B": tokens, "d_model": c.d_model,
+                       "heads": [c.num_key_heads, c.num_value_heads],
+                       "head_dims": [c.key_dim, c.value_dim],
+                       "l2": f"inputs larger than L2: {layers} distinct layers "
+                             f"({(wbytes + state_bytes / 2) / 1e6:.0f} MB each) cycle per step"}
+
+    def _step(self, i):
+        from nvfp4.deltanet import deltanet_forward
+
+        w, st = self.layers[i % self.sets]
+        deltanet_forward(self.x, self.y, w, st, self.cfg, proj_dtype=self.torch.bfloat16,
+                         workspace=self.ws)
+
+    def run_step(self, i):
+        self._step(i)
+
+    def run_dominant(self, i):
+        self._step(i)
+        return 1
+
+    def units(self, steps):
+        return self.B * steps  # tokens
+
+    def e2e_setup(self):
+        torch = self.torch
+        self.h_x = torch.randn(self.x.shape).to(torch.bfloat16).pin_memory()
+        self.h_y = torch.empty(self.y.shape, dtype=torch.bfloat16).pin_memory()
+        self.h2d = self.h_x.numel() * 2
+        self.d2h = self.h_y.numel() * 2
+
+    def e2e_step(self, i):
+        self.x.copy_(self.h_x, non_blocking=True)
+        self._step(i)
+        self.h_y.copy_(self.y, non_blocking=True)
+
+    def cpu_sample(self, threads):
+        import numpy as np
+        from nvfp4 import synthetic
+        from nvfp4.deltanet import DeltaNetConfig
+        from oracle import oracle as O
+
+        c = DeltaNetConfig()
+        rows, _ = deltanet_weight_bytes()
+        rng = np.random.default_rng(5)
+        w = {}
+        for i, (name, (n, k)) in enumerate(rows.items()):
+            wd = synthetic.linear_weights(n, k, seed=40 + i)
+            w[name] = O.dequant(wd["w"], wd["sf"]) * wd["ws2"][:, None]
+        f = lambda *sh: (rng.standard_normal(sh) * 0.5).astype(np.float32)
+        w.update(a_log=f(c.num_value_heads), dt_bias=f(c.num_value_heads),
+                 conv_q=f(c.q_dim(), c.conv_kernel), conv_k=f(c.k_dim(), c.conv_kernel),
+                 conv_v=f(c.v_dim(), c.conv_kernel))
+        cd = dict(d_model=c.d_model, num_key_heads=c.num_key_heads,
+                  num_value_heads=c.num_value_heads, key_dim=c.key_dim, value_dim=c.value_dim,
+                  conv_kernel=c.conv_kernel, rms_eps=c.rms_eps)
+        st = O.deltanet_state(cd)
+        x = rng.standard_normal(c.d_model).astype(np.float32)
+
+        def run():
+            O.deltanet_forward(cd, x, w, st)
+
+        desc = ("one token through the layer: the reference's deltanet_forward restated "
+                "(fp32, dequantized projection weights; single thread)")
+        return run, 1.0, desc, 1
+
+
+# ---------------------------------------------------------------------------
 # Workload: 48-layer stack of the MoE layer, expert-parallel over the ranks.
 # ---------------------------------------------------------------------------
 class EPStackBench:
@@ -632,7 +759,8 @@ def synthetic_local_experts(epr, seed, device):
 
 
 WORKLOADS = {"gemv": GemvSweep, "prefill": PrefillSweep, "prefill_w4a4": PrefillW4A4Sweep,
-             "dequant": DequantBench, "moe": MoELayerBench, "ep": EPStackBench}
+             "dequant": DequantBench, "moe": MoELayerBench, "ep": EPStackBench,
+             "deltanet": DeltaNetBench}
 
 
 # ---------------------------------------------------------------------------
@@ -733,12 +861,13 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--tokens", type=int, default=None,
-                    help="MoE: tokens per step (default 4096); EP stack: global tokens (default 64)")
+                    help="MoE: tokens per step (default 4096); EP stack: global tokens (default "
+                         "64); DeltaNet: sequences per step (default 4)")
     ap.add_argument("--layers", type=int, default=48, help="EP stack: number of MoE layers")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.tokens is None:
-        args.tokens = 64 if args.workload == "ep" else 4096
+        args.tokens = {"ep": 64, "deltanet": 4}.get(args.workload, 4096)
 
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -751,7 +880,7 @@ def main():
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     peaks = load_peaks()
-    kw = {"tokens": args.tokens} if args.workload in ("moe", "ep") else {}
+    kw = {"tokens": args.tokens} if args.workload in ("moe", "ep", "deltanet") else {}
     if args.workload == "ep":
         kw["layers"] = args.layers
     wl = WORKLOADS[args.workload](device, seed=17 * rank, **kw)

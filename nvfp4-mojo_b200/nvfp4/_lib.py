@@ -93,6 +93,41 @@ class StLinearInfo(ctypes.Structure):
 
 ST_FOLD_INPUT_SCALE = 0x1
 
+
+class DeltaNetDesc(ctypes.Structure):
+    """struct nvfp4_deltanet_desc (include/nvfp4_deltanet.h)."""
+
+    _fields_ = [("d_model", ctypes.c_int32), ("num_key_heads", ctypes.c_int32),
+                ("num_value_heads", ctypes.c_int32), ("key_dim", ctypes.c_int32),
+                ("value_dim", ctypes.c_int32), ("conv_kernel", ctypes.c_int32),
+                ("rms_eps", ctypes.c_float)]
+
+
+class DeltaNetProj(ctypes.Structure):
+    """struct nvfp4_deltanet_proj."""
+
+    _fields_ = [("packed_weights", ctypes.c_void_p), ("blockscales", ctypes.c_void_p),
+                ("input_scale", ctypes.c_float), ("weight_scale_2", ctypes.c_float),
+                ("weight_scale_2_rows", ctypes.c_void_p)]
+
+
+class DeltaNetWeightPtrs(ctypes.Structure):
+    """struct nvfp4_deltanet_weights."""
+
+    _fields_ = [("qkv", DeltaNetProj), ("z", DeltaNetProj), ("b", DeltaNetProj),
+                ("a", DeltaNetProj), ("out", DeltaNetProj), ("a_log", ctypes.c_void_p),
+                ("dt_bias", ctypes.c_void_p), ("conv_q", ctypes.c_void_p),
+                ("conv_k", ctypes.c_void_p), ("conv_v", ctypes.c_void_p),
+                ("conv_bias_q", ctypes.c_void_p), ("conv_bias_k", ctypes.c_void_p),
+                ("conv_bias_v", ctypes.c_void_p)]
+
+
+class DeltaNetStatePtrs(ctypes.Structure):
+    """struct nvfp4_deltanet_state."""
+
+    _fields_ = [("s", ctypes.c_void_p), ("conv_q", ctypes.c_void_p),
+                ("conv_k", ctypes.c_void_p), ("conv_v", ctypes.c_void_p)]
+
 _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
 _int = ctypes.c_int
@@ -132,6 +167,12 @@ SIGNATURES = {
     "nvfp4_gather_rows": (_int, [_vp, _vp, _i64, _i64, _vp, _vp]),
     "nvfp4_ep_dispatch_padded": (_int, [_vp, _vp, _vp, _vp, _i64, ctypes.c_int32, ctypes.c_int32,
                                         _i64, _vp, _i64, _vp, _vp, _vp, _vp]),
+    # include/nvfp4_deltanet.h
+    "nvfp4_deltanet_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(DeltaNetDesc), _i64]),
+    "nvfp4_deltanet_forward": (_int, [ctypes.POINTER(DeltaNetDesc),
+                                      ctypes.POINTER(DeltaNetWeightPtrs), _vp, _int, _vp, _int,
+                                      _i64, ctypes.POINTER(DeltaNetStatePtrs), _int, _vp,
+                                      ctypes.c_size_t, _vp]),
     # include/nvfp4_loader.h
     "nvfp4_st_open": (_int, [ctypes.c_char_p, ctypes.POINTER(_vp)]),
     "nvfp4_st_close": (None, [_vp]),

@@ -331,3 +331,129 @@ void oracle_moe(int64_t T, int64_t H, int64_t I, int64_t E, int64_t top_k,
   }
   (void)n_threads;
 }
+
+/* ------------------------------------------------------------------------
+ * Gated DeltaNet decode step (nvfp4/deltanet.mojo:51-542), fp32, the
+ * reference's loops as written.
+ * ---------------------------------------------------------------------- */
+
+/* nvfp4/deltanet.mojo:56-63 */
+float oracle_softplus(float x) {
+  if (x > 20.0f) return x;
+  if (x < -20.0f) return 0.0f;
+  return logf(1.0f + expf(x));
+}
+
+/* matvec (:239-254): result[r] = sum_c mat[r, c] * vec[c], sequential c. */
+void oracle_dn_matvec(const float *mat, const float *vec, float *result, int64_t rows,
+                      int64_t cols) {
+  for (int64_t r = 0; r < rows; ++r) {
+    float acc = 0.0f;
+    for (int64_t c = 0; c < cols; ++c) acc += mat[r * cols + c] * vec[c];
+    result[r] = acc;
+  }
+}
+
+/* matvec_transposed (:221-236): result[c] = sum_r mat[r, c] * vec[r], sequential r. */
+void oracle_dn_matvec_t(const float *mat, const float *vec, float *result, int64_t rows,
+                        int64_t cols) {
+  for (int64_t c = 0; c < cols; ++c) {
+    float acc = 0.0f;
+    for (int64_t r = 0; r < rows; ++r) acc += mat[r * cols + c] * vec[r];
+    result[c] = acc;
+  }
+}
+
+/* rms_norm_inplace (:270-284) */
+void oracle_rms_norm(float *x, int64_t n, float eps) {
+  float sum_sq = 0.0f;
+  for (int64_t i = 0; i < n; ++i) sum_sq += x[i] * x[i];
+  const float scale = 1.0f / sqrtf(sum_sq / (float)n + eps);
+  for (int64_t i = 0; i < n; ++i) x[i] = x[i] * scale;
+}
+
+/* conv1d_step (:287-328): history oldest first, weight[:, kernel-1] on the
+ * new input, then the window shifts by one. */
+void oracle_conv1d_step(const float *new_input, float *buf, const float *w, float *result,
+                        int64_t channels, int64_t kernel, const float *bias) {
+  const int64_t hist = kernel - 1;
+  for (int64_t ch = 0; ch < channels; ++ch) {
+    float acc = 0.0f;
+    for (int64_t t = 0; t < hist; ++t) acc += buf[ch * hist + t] * w[ch * kernel + t];
+    acc += new_input[ch] * w[ch * kernel + hist];
+    if (bias) acc += bias[ch];
+    result[ch] = acc;
+  }
+  for (int64_t ch = 0; ch < channels; ++ch) {
+    for (int64_t t = 0; t < hist - 1; ++t) buf[ch * hist + t] = buf[ch * hist + t + 1];
+    if (hist > 0) buf[ch * hist + hist - 1] = new_input[ch];
+  }
+}
+
+/* deltanet_forward (:335-542), one token. */
+void oracle_deltanet_forward(int64_t d, int64_t nkh, int64_t nvh, int64_t kd, int64_t vd,
+                             int64_t conv_k, float eps, const float *hidden, float *out,
+                             const float *w_qkv, const float *w_z, const float *w_b,
+                             const float *w_a, const float *w_out, const float *a_log,
+                             const float *dt_bias, const float *wc_q, const float *wc_k,
+                             const float *wc_v, const float *cb_q, const float *cb_k,
+                             const float *cb_v, float *s_matrix, float *buf_q, float *buf_k,
+                             float *buf_v) {
+  const int64_t vg = nvh / nkh, q_dim = nkh * kd, k_dim = nkh * kd, v_dim = nvh * vd;
+  const int64_t qkv_dim = q_dim + k_dim + v_dim, z_dim = nvh * vd;
+  float *qkv = (float *)calloc((size_t)qkv_dim, sizeof(float));
+  float *z = (float *)calloc((size_t)z_dim, sizeof(float));
+  float *braw = (float *)calloc((size_t)nvh, sizeof(float));
+  float *araw = (float *)calloc((size_t)nvh, sizeof(float));
+  float *q = (float *)calloc((size_t)q_dim, sizeof(float));
+  float *k = (float *)calloc((size_t)k_dim, sizeof(float));
+  float *v = (float *)calloc((size_t)v_dim, sizeof(float));
+  float *beta = (float *)calloc((size_t)nvh, sizeof(float));
+  float *decay = (float *)calloc((size_t)nvh, sizeof(float));
+  float *o = (float *)calloc((size_t)z_dim, sizeof(float));
+  float *vc = (float *)calloc((size_t)vd, sizeof(float));
+  float *stk = (float *)calloc((size_t)vd, sizeof(float));
+  /* Step 1: projections (:404-426). */
+  oracle_dn_matvec(w_qkv, hidden, qkv, qkv_dim, d);
+  oracle_dn_matvec(w_z, hidden, z, z_dim, d);
+  oracle_dn_matvec(w_b, hidden, braw, nvh, d);
+  oracle_dn_matvec(w_a, hidden, araw, nvh, d);
+  /* Step 2: causal conv1d on q, k, v (:431-469). */
+  oracle_conv1d_step(qkv, buf_q, wc_q, q, q_dim, conv_k, cb_q);
+  oracle_conv1d_step(qkv + q_dim, buf_k, wc_k, k, k_dim, conv_k, cb_k);
+  oracle_conv1d_step(qkv + q_dim + k_dim, buf_v, wc_v, v, v_dim, conv_k, cb_v);
+  /* Step 3: SiLU (:471-479). */
+  for (int64_t i = 0; i < q_dim; ++i) q[i] = oracle_silu(q[i]);
+  for (int64_t i = 0; i < k_dim; ++i) k[i] = oracle_silu(k[i]);
+  for (int64_t i = 0; i < v_dim; ++i) v[i] = oracle_silu(v[i]);
+  /* Step 4: beta, decay, per-head recurrence (:481-532). */
+  for (int64_t h = 0; h < nvh; ++h) beta[h] = oracle_sigmoid(braw[h]);
+  for (int64_t h = 0; h < nvh; ++h) {
+    const float a_val = oracle_softplus(a_log[h]);
+    const float dt_val = oracle_softplus(araw[h] + dt_bias[h]);
+    decay[h] = expf(-a_val * dt_val);
+  }
+  for (int64_t h = 0; h < nvh; ++h) {
+    const int64_t kh = h / vg;
+    const float *q_h = q + kh * kd, *k_h = k + kh * kd, *v_h = v + h * vd;
+    float *o_h = o + h * vd, *s_h = s_matrix + h * kd * vd;
+    oracle_dn_matvec_t(s_h, k_h, stk, kd, vd);
+    for (int64_t i = 0; i < vd; ++i) vc[i] = v_h[i] - stk[i];
+    const float d_h = decay[h], b_h = beta[h];
+    for (int64_t r = 0; r < kd; ++r) {
+      const float k_r = k_h[r];
+      for (int64_t c = 0; c < vd; ++c) {
+        const int64_t idx = r * vd + c;
+        s_h[idx] = d_h * s_h[idx] + b_h * k_r * vc[c];
+      }
+    }
+    oracle_dn_matvec_t(s_h, q_h, o_h, kd, vd);
+  }
+  /* Step 5: output gate (:534-541). */
+  for (int64_t h = 0; h < nvh; ++h) oracle_rms_norm(o + h * vd, vd, eps);
+  for (int64_t i = 0; i < z_dim; ++i) o[i] = oracle_silu(z[i]) * o[i];
+  /* Step 6: output projection (:543-546). */
+  oracle_dn_matvec(w_out, o, out, d, z_dim);
+  free(qkv); free(z); free(braw); free(araw); free(q); free(k); free(v);
+  free(beta); free(decay); free(o); free(vc); free(stk);
+}

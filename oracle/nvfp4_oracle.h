@@ -133,6 +133,28 @@ void oracle_moe(int64_t T, int64_t H, int64_t I, int64_t E, int64_t top_k,
 void oracle_router(int64_t T, int64_t H, int64_t E, const float *x,
                    const float *router, float *logits, float *probs);
 
+/* Gated DeltaNet decode step (nvfp4/deltanet.mojo:51-542), fp32.  Shapes:
+ * hidden/out [d]; w_qkv [(2 nkh kd + nvh vd), d]; w_z [nvh vd, d]; w_b, w_a
+ * [nvh, d]; w_out [d, nvh vd]; a_log, dt_bias [nvh]; conv weights [dim,
+ * conv_k]; conv biases [dim] or NULL; state s_matrix [nvh, kd, vd] and conv
+ * windows [dim, conv_k - 1], both updated in place. */
+float oracle_softplus(float x);
+void oracle_dn_matvec(const float *mat, const float *vec, float *result, int64_t rows,
+                      int64_t cols);
+void oracle_dn_matvec_t(const float *mat, const float *vec, float *result, int64_t rows,
+                        int64_t cols);
+void oracle_rms_norm(float *x, int64_t n, float eps);
+void oracle_conv1d_step(const float *new_input, float *buf, const float *w, float *result,
+                        int64_t channels, int64_t kernel, const float *bias);
+void oracle_deltanet_forward(int64_t d, int64_t nkh, int64_t nvh, int64_t kd, int64_t vd,
+                             int64_t conv_k, float eps, const float *hidden, float *out,
+                             const float *w_qkv, const float *w_z, const float *w_b,
+                             const float *w_a, const float *w_out, const float *a_log,
+                             const float *dt_bias, const float *wc_q, const float *wc_k,
+                             const float *wc_v, const float *cb_q, const float *cb_k,
+                             const float *cb_v, float *s_matrix, float *buf_q, float *buf_k,
+                             float *buf_v);
+
 #ifdef __cplusplus
 }
 #endif

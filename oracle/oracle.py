@@ -79,6 +79,20 @@ def lib():
                                  _f32p, _f32p, _u8p, _u8p, _f32p, _f32p,
                                  _u8p, _u8p, _f32p, _f32p, _f32p,
                                  _i64p, _i64, _i32p, _f32p, _i32p, ctypes.c_int]
+        L.oracle_softplus.restype = ctypes.c_float
+        L.oracle_softplus.argtypes = [ctypes.c_float]
+        L.oracle_dn_matvec.restype = None
+        L.oracle_dn_matvec.argtypes = [_f32p, _f32p, _f32p, _i64, _i64]
+        L.oracle_dn_matvec_t.restype = None
+        L.oracle_dn_matvec_t.argtypes = [_f32p, _f32p, _f32p, _i64, _i64]
+        L.oracle_rms_norm.restype = None
+        L.oracle_rms_norm.argtypes = [_f32p, _i64, ctypes.c_float]
+        L.oracle_conv1d_step.restype = None
+        L.oracle_conv1d_step.argtypes = [_f32p, _f32p, _f32p, _f32p, _i64, _i64, _f32p]
+        L.oracle_deltanet_forward.restype = None
+        L.oracle_deltanet_forward.argtypes = ([_i64] * 6 + [ctypes.c_float] + [_f32p] * 2
+                                              + [_f32p] * 5 + [_f32p] * 2 + [_f32p] * 6
+                                              + [_f32p] * 4)
         _lib = L
     return _lib
 
@@ -268,3 +282,80 @@ def host_cores() -> int:
         return len(os.sched_getaffinity(0))
     except AttributeError:  # pragma: no cover
         return os.cpu_count() or 1
+
+
+# ---------------------------------------------------------------------------
+# Gated DeltaNet decode step (nvfp4/deltanet.mojo:51-542)
+# ---------------------------------------------------------------------------
+
+def softplus(x: float) -> float:
+    """nvfp4/deltanet.mojo:56-63."""
+    return lib().oracle_softplus(x)
+
+
+def dn_matvec(mat, vec):
+    """matvec (nvfp4/deltanet.mojo:239-254): mat [rows, cols] @ vec [cols]."""
+    mat, vec = _f32(mat), _f32(vec)
+    out = np.empty(mat.shape[0], dtype=np.float32)
+    lib().oracle_dn_matvec(_p(mat, _f32p), _p(vec, _f32p), _p(out, _f32p), *mat.shape)
+    return out
+
+
+def dn_matvec_t(mat, vec):
+    """matvec_transposed (nvfp4/deltanet.mojo:221-236): mat^T @ vec."""
+    mat, vec = _f32(mat), _f32(vec)
+    out = np.empty(mat.shape[1], dtype=np.float32)
+    lib().oracle_dn_matvec_t(_p(mat, _f32p), _p(vec, _f32p), _p(out, _f32p), *mat.shape)
+    return out
+
+
+def rms_norm(x, eps=1e-6):
+    """rms_norm_inplace (nvfp4/deltanet.mojo:270-284), on a copy."""
+    y = _f32(x).copy()
+    lib().oracle_rms_norm(_p(y, _f32p), y.size, eps)
+    return y
+
+
+def conv1d_step(new_input, buf, w, bias=None):
+    """conv1d_step (nvfp4/deltanet.mojo:287-328); buf [ch, k-1] updated in place."""
+    x, w = _f32(new_input), _f32(w)
+    assert buf.dtype == np.float32 and buf.flags.c_contiguous
+    ch, kernel = w.shape
+    out = np.empty(ch, dtype=np.float32)
+    b = None if bias is None else _f32(bias)
+    lib().oracle_conv1d_step(_p(x, _f32p), _p(buf, _f32p), _p(w, _f32p), _p(out, _f32p), ch,
+                             kernel, _p(b, _f32p))
+    return out
+
+
+def deltanet_state(cfg):
+    """Zero DeltaNetState (nvfp4/deltanet.mojo:181-218): s [nvh, kd, vd] and the
+    conv windows [dim, conv_k - 1] of q, k, v."""
+    nkh, nvh, kd, vd, ck = (cfg["num_key_heads"], cfg["num_value_heads"], cfg["key_dim"],
+                            cfg["value_dim"], cfg["conv_kernel"])
+    z = lambda *s: np.zeros(s, dtype=np.float32)
+    return {"s": z(nvh, kd, vd), "q": z(nkh * kd, ck - 1), "k": z(nkh * kd, ck - 1),
+            "v": z(nvh * vd, ck - 1)}
+
+
+def deltanet_forward(cfg, hidden, w, state):
+    """deltanet_forward (nvfp4/deltanet.mojo:335-546) for one token with fp32
+    weights (for NVFP4 projections, pass their dequantized matrices times
+    alpha: the dequantization is exact in fp32).  `w` keys: qkv, z, b, a,
+    out, a_log, dt_bias, conv_q, conv_k, conv_v and optional conv_bias_q/k/v;
+    `state` (deltanet_state) is updated in place.  Returns out [d_model]."""
+    d = cfg["d_model"]
+    out = np.empty(d, dtype=np.float32)
+    g = {k: (None if v is None else _f32(v)) for k, v in w.items()}
+    for k_ in ("s", "q", "k", "v"):
+        assert state[k_].dtype == np.float32 and state[k_].flags.c_contiguous
+    lib().oracle_deltanet_forward(
+        d, cfg["num_key_heads"], cfg["num_value_heads"], cfg["key_dim"], cfg["value_dim"],
+        cfg["conv_kernel"], cfg.get("rms_eps", 1e-6), _p(_f32(hidden), _f32p), _p(out, _f32p),
+        _p(g["qkv"], _f32p), _p(g["z"], _f32p), _p(g["b"], _f32p), _p(g["a"], _f32p),
+        _p(g["out"], _f32p), _p(g["a_log"], _f32p), _p(g["dt_bias"], _f32p),
+        _p(g["conv_q"], _f32p), _p(g["conv_k"], _f32p), _p(g["conv_v"], _f32p),
+        _p(g.get("conv_bias_q"), _f32p), _p(g.get("conv_bias_k"), _f32p),
+        _p(g.get("conv_bias_v"), _f32p), _p(state["s"], _f32p), _p(state["q"], _f32p),
+        _p(state["k"], _f32p), _p(state["v"], _f32p))
+    return out

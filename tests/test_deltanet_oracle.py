@@ -1,0 +1,109 @@
+"""The DeltaNet oracle (oracle/nvfp4_oracle.c, restating nvfp4/deltanet.mojo)
+pinned against every known answer of the reference's tests/test_deltanet.mojo,
+with that file's tolerance rule (tests/helpers.mojo:7-19: absolute or
+relative difference within tol).  CPU only."""
+import numpy as np
+import pytest
+
+
+def approx_eq(a, b, tol=1e-4):
+    """approx_eq (tests/helpers.mojo:7-19)."""
+    diff = abs(float(a) - float(b))
+    if diff <= tol:
+        return True
+    denom = abs(max(float(a), float(b)))
+    return denom > 0.0 and diff / denom <= tol
+
+
+def expect_close(actual, expected, tol=1e-4):
+    assert approx_eq(np.float32(actual), np.float32(expected), tol), (actual, expected)
+
+
+def test_activations(O):
+    """tests/test_deltanet.mojo:57-80."""
+    expect_close(O.softplus(0.0), 0.6931472)
+    expect_close(O.softplus(30.0), 30.0)
+    expect_close(O.softplus(-30.0), 0.0)
+    expect_close(O.softplus(1.0), 1.3132616)
+    expect_close(O.sigmoid(0.0), 0.5)
+    expect_close(O.sigmoid(10.0), 0.9999546)
+    expect_close(O.sigmoid(-10.0), 4.539787e-05)
+    expect_close(O.silu(0.0), 0.0)
+    expect_close(O.silu(1.0), 0.7310586)
+    expect_close(O.silu(-1.0), -0.26894143)
+
+
+def test_linear_algebra(O):
+    """tests/test_deltanet.mojo:84-159."""
+    a = np.array([[1, 2, 3], [4, 5, 6]], np.float32)
+    y = O.dn_matvec(a, np.ones(3, np.float32))
+    expect_close(y[0], 6.0)
+    expect_close(y[1], 15.0)
+    yt = O.dn_matvec_t(a.reshape(3, 2), np.ones(3, np.float32))
+    expect_close(yt[0], 9.0)
+    expect_close(yt[1], 12.0)
+    x = O.rms_norm(np.array([1, 2, 3, 4], np.float32), 1e-6)
+    r = np.sqrt(np.float32(7.5))
+    for i in range(4):
+        expect_close(x[i], (i + 1) / r)
+
+
+def test_conv1d_step(O):
+    """tests/test_deltanet.mojo:163-215."""
+    buf = np.array([[0.5, 1.0], [0.2, 0.3]], np.float32)
+    w = np.array([[1.0, 2.0, 3.0], [0.5, 1.5, 2.5]], np.float32)
+    out = O.conv1d_step(np.array([2.0, 4.0], np.float32), buf, w)
+    expect_close(out[0], 8.5)
+    expect_close(out[1], 10.55)
+    expect_close(buf[0, 0], 1.0)
+    expect_close(buf[0, 1], 2.0)
+    expect_close(buf[1, 0], 0.3)
+    expect_close(buf[1, 1], 4.0)
+
+
+def identity_like(rows, cols, scale):
+    """make_identity_like (tests/test_deltanet.mojo:41-50)."""
+    m = np.zeros((rows, cols), np.float32)
+    m[np.arange(rows), np.arange(rows) % cols] = scale
+    return m
+
+
+def small_case():
+    """The small configuration and weights of test_forward_small
+    (tests/test_deltanet.mojo:285-346)."""
+    cfg = dict(d_model=8, num_key_heads=2, num_value_heads=2, key_dim=4, value_dim=4,
+               conv_kernel=4, rms_eps=1e-6)
+    d, nvh, qd, kd, vd, ck = 8, 2, 8, 8, 8, 4
+    conv = lambda ch: np.concatenate([np.zeros((ch, ck - 1), np.float32),
+                                      np.ones((ch, 1), np.float32)], 1)
+    w = dict(qkv=identity_like(24, d, 0.1), z=identity_like(8, d, 0.5),
+             b=np.full((nvh, d), 0.1, np.float32), a=np.full((nvh, d), 0.05, np.float32),
+             out=identity_like(d, 8, 1.0), a_log=np.array([0.0, 0.5], np.float32),
+             dt_bias=np.array([0.0, 0.1], np.float32), conv_q=conv(qd), conv_k=conv(kd),
+             conv_v=conv(vd))
+    hidden = (np.float32(0.1) + np.arange(d, dtype=np.float32) * np.float32(0.1))
+    return cfg, w, hidden
+
+
+def test_forward_small_golden(O):
+    """test_forward_small (tests/test_deltanet.mojo:285-425): result[0] and
+    result[7] of the first step, state updated, the second step differs."""
+    cfg, w, hidden = small_case()
+    st = O.deltanet_state(cfg)
+    r1 = O.deltanet_forward(cfg, hidden, w, st)
+    assert np.any(r1 != 0.0)
+    expect_close(r1[0], 5.879743e-05, 1e-6)
+    expect_close(r1[7], 0.0271918, 1e-5)
+    assert np.any(st["s"] != 0.0)
+    r2 = O.deltanet_forward(cfg, hidden, w, st)
+    assert np.any(r1 != r2)
+
+
+def test_config_sizes():
+    """test_config / test_state_init / test_o1_memory
+    (tests/test_deltanet.mojo:219-445): the default layer's dimensions."""
+    nkh, nvh, kd, vd = 16, 32, 128, 128
+    assert 2 * nkh * kd + nvh * vd == 8192      # total_qkv_dim
+    assert nvh * vd == 4096                     # z_dim
+    assert nvh * kd * vd == 524288              # total_state_floats
+    assert nvh * kd * vd * 4 == 2097152         # state bytes per layer
