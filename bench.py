@@ -550,14 +550,14 @@ class DeltaNetBench:
         return (f"one gated DeltaNet decode step of the reference's default layer (d_model "
                 f"2048, 16 key / 32 value heads of 128 x 128, conv kernel 4) with NVFP4 "
                 f"projections qkv [8192, 2048], z [4096, 2048], beta / alpha [32, 2048], out "
-                f"[2048, 4096]; {tokens} sequences with their own fp32 state; bf16 activations "
-                f"on the decode GEMV")
+                f"[2048, 4096] (the four input projections row-stacked into one); {tokens} "
+                f"sequences with their own fp32 state; bf16 activations on the decode GEMV")
 
     def __init__(self, device, seed=0, tokens=4, layers=8):
         import torch
         import nvfp4
         from nvfp4 import synthetic
-        from nvfp4.deltanet import DeltaNetConfig, DeltaNetState, DeltaNetWeights
+        from nvfp4.deltanet import DeltaNetConfig, DeltaNetState, DeltaNetWeights, fuse_in_proj
 
         self.torch, self.B = torch, tokens
         self.cfg = DeltaNetConfig()
@@ -577,12 +577,12 @@ class DeltaNetBench:
             w = DeltaNetWeights(**proj, a_log=r(c.num_value_heads), dt_bias=r(c.num_value_heads),
                                 conv_q=r(c.q_dim(), c.conv_kernel), conv_k=r(c.k_dim(), c.conv_kernel),
                                 conv_v=r(c.v_dim(), c.conv_kernel))
-            self.layers.append((w, DeltaNetState(c, batch=tokens, device=device)))
+            self.layers.append((fuse_in_proj(w), DeltaNetState(c, batch=tokens, device=device)))
         self.x = torch.randn((tokens, c.d_model), device=device).to(torch.bfloat16)
         self.y = torch.empty_like(self.x)
         self.ws = torch.empty(64 << 20, dtype=torch.uint8, device=device)
         self.sets = layers
-        self.launches_per_step = 7  # 4 projections, conv, recurrence, out projection
+        self.launches_per_step = 4  # fused input projection, conv, recurrence, out projection
         state_bytes = 2 * 4 * tokens * (c.total_state_floats()
                                        + (c.q_dim() + c.k_dim() + c.v_dim()) * (c.conv_kernel - 1))
         self.dominant_bytes = wbytes + state_bytes

@@ -49,6 +49,11 @@ typedef struct nvfp4_deltanet_weights {
   nvfp4_deltanet_proj b;    /* [nvh, d_model] (beta) */
   nvfp4_deltanet_proj a;    /* [nvh, d_model] (alpha) */
   nvfp4_deltanet_proj out;  /* [d_model, nvh vd] */
+  /* Optional (packed_weights NULL: unused): the rows of qkv, z, b and a
+   * concatenated in that order, one NVFP4 matrix [2 nkh kd + 2 nvh vd +
+   * 2 nvh, d_model] with one input_scale (nvfp4_stack_rows builds it); one
+   * projection launch instead of four.  qkv, z, b, a are then ignored. */
+  nvfp4_deltanet_proj in_proj;
   const float *a_log;       /* [nvh] */
   const float *dt_bias;     /* [nvh] */
   const float *conv_q, *conv_k, *conv_v;                /* [dim, conv_kernel] */

@@ -15,6 +15,8 @@
 
 #include <algorithm>
 
+#include <cooperative_groups.h>
+
 #include "../../include/nvfp4.h"
 #include "../../include/nvfp4_deltanet.h"
 #include "abi_util.h"
@@ -71,6 +73,7 @@ DnLayout dn_layout(const DnDims &d, int64_t B) {
   size_t o = 0;
   L.hx = o;
   o = dn_up(o + 4 * (size_t)B * d.d);
+  // qkv .. araw also hold the fused projection's [B, qkv + z + 2 nvh] output.
   L.qkv = o;
   o = dn_up(o + 4 * (size_t)B * d.qkv_dim);
   L.z = o;
@@ -79,6 +82,7 @@ DnLayout dn_layout(const DnDims &d, int64_t B) {
   o = dn_up(o + 4 * (size_t)B * d.nvh);
   L.araw = o;
   o = dn_up(o + 4 * (size_t)B * d.nvh);
+  o = std::max(o, dn_up(L.qkv + 4 * (size_t)B * (d.qkv_dim + d.z_dim + 2 * d.nvh)));
   L.post = o;
   o = dn_up(o + 4 * (size_t)B * d.qkv_dim);
   L.og = o;
@@ -100,7 +104,8 @@ __global__ void dn_convert_kernel(const void *in, int in_dt, void *out, int out_
 }
 
 struct ConvArgs {
-  const float *qkv;  // [B, qkv_dim] projection output
+  const float *qkv;  // [B, qkv_ld] projection output (qkv_dim columns used)
+  int64_t qkv_ld;
   float *post;       // [B, qkv_dim] conv + SiLU
   float *buf[3];     // windows of q, k, v: [B, dim, ck - 1]
   const float *w[3], *bias[3];
@@ -119,7 +124,7 @@ __global__ void dn_conv_kernel(ConvArgs a) {
   const int hist = a.ck - 1;
   float *buf = a.buf[seg] + (b * a.dim[seg] + ch) * hist;
   const float *w = a.w[seg] + (int64_t)ch * a.ck;
-  const float x = a.qkv[i];
+  const float x = a.qkv[b * a.qkv_ld + (i - b * a.qkv_dim)];
   float acc = 0.0f;
   for (int t = 0; t < hist; ++t) acc = __fadd_rn(acc, __fmul_rn(buf[t], w[t]));
   acc = __fadd_rn(acc, __fmul_rn(x, w[hist]));
@@ -131,8 +136,10 @@ __global__ void dn_conv_kernel(ConvArgs a) {
 
 struct RecurArgs {
   const float *post;  // [B, qkv_dim]: q | k | v after conv + SiLU
-  const float *z;     // [B, z_dim]
-  const float *braw, *araw;  // [B, nvh]
+  const float *z;     // [B, z_ld] (z_dim columns used)
+  const float *braw, *araw;  // [B, ba_ld] (nvh columns used)
+  int64_t z_ld, ba_ld;
+  int nsplit;         // CTAs (a cluster) per value head, each vd / nsplit columns
   const float *a_log, *dt_bias;
   float *s;           // [B, nvh, kd, vd]
   void *og;           // [B, z_dim] gated output (og_dt)
@@ -141,18 +148,24 @@ struct RecurArgs {
   float eps;
 };
 
-// One CTA of vd x RG threads per (value head h, sequence b); thread (group
-// g, column c) holds the rows r = g, g + RG, ... of column c of the head's
-// state S[kd][vd] (kd = 128, vd = 128: 4 groups, 32 rows per thread).
-// STRIDE: RG * vd when known at compile time (the default 128 x 128 head:
-// row offsets become immediates instead of live 64-bit addresses), else 0.
+// A cluster of NS CTAs per (value head h, sequence b), CTA `part` owning
+// the vl = vd / NS columns [part vl, (part + 1) vl) of the head's state
+// S[kd][vd]: the delta rule and both passes over S are per column, only the
+// head's RMS norm needs all columns (partial sums of squares, added in rank
+// order through distributed shared memory).  Thread (group g, column cl) of
+// the CTA's vl x RG threads holds rows r = g, g + RG, ... of its column in
+// registers (kd = vd = 128: NS = 4, RG = 16, 8 rows per thread).
+// STRIDE: RG * vd when known at compile time (row offsets become
+// immediates), else 0.
 template <int RPT, int STRIDE>
 __global__ void __launch_bounds__(512) dn_recur_kernel(RecurArgs a) {
+  namespace cg = cooperative_groups;
   __shared__ float sq[256], sk[256], red[512], vec[256];
-  __shared__ float scal[2];
-  const int h = blockIdx.x, b = blockIdx.y;
-  const int vd = a.vd, kd = a.kd, RG = a.rg;
-  const int c = threadIdx.x % vd, g = threadIdx.x / vd;
+  __shared__ float scal[3];  // beta, decay, this CTA's sum of squares
+  const int NS = a.nsplit;
+  const int part = blockIdx.x % NS, h = blockIdx.x / NS, b = blockIdx.y;
+  const int vd = a.vd, vl = vd / NS, kd = a.kd, RG = a.rg;
+  const int cl = threadIdx.x % vl, g = threadIdx.x / vl, c = part * vl + cl;
   const int kh = h / a.vg;
   const float *row = a.post + (int64_t)b * a.qkv_dim;
   for (int r = threadIdx.x; r < kd; r += blockDim.x) {
@@ -160,10 +173,11 @@ __global__ void __launch_bounds__(512) dn_recur_kernel(RecurArgs a) {
     sk[r] = row[a.q_dim + kh * kd + r];
   }
   if (threadIdx.x == 0) {
-    const int bh = b * a.nvh + h;
-    scal[0] = dn_sigmoid(a.braw[bh]);  // beta (:484-487)
+    const float braw = a.braw[(int64_t)b * a.ba_ld + h];
+    const float araw = a.araw[(int64_t)b * a.ba_ld + h];
+    scal[0] = dn_sigmoid(braw);  // beta (:484-487)
     const float a_val = dn_softplus(a.a_log[h]);
-    const float dt_val = dn_softplus(__fadd_rn(a.araw[bh], a.dt_bias[h]));
+    const float dt_val = dn_softplus(__fadd_rn(araw, a.dt_bias[h]));
     scal[1] = expf(-__fmul_rn(a_val, dt_val));  // decay (:489-494)
   }
   __syncthreads();
@@ -184,13 +198,13 @@ __global__ void __launch_bounds__(512) dn_recur_kernel(RecurArgs a) {
   __syncthreads();
   if (g == 0) {
     float stk = 0.0f;
-    for (int q = 0; q < RG; ++q) stk = __fadd_rn(stk, red[q * vd + c]);
+    for (int q = 0; q < RG; ++q) stk = __fadd_rn(stk, red[q * vl + cl]);
     const float v = row[a.q_dim + a.k_dim + h * vd + c];
-    vec[c] = __fadd_rn(v, -stk);  // v - S^T k (:515-516)
+    vec[cl] = __fadd_rn(v, -stk);  // v - S^T k (:515-516)
   }
   __syncthreads();
   // S = decay * S + beta * k outer (v - S^T k) (:519-526), then S^T q (:529).
-  const float beta = scal[0], decay = scal[1], vcc = vec[c];
+  const float beta = scal[0], decay = scal[1], vcc = vec[cl];
   p = 0.0f;
 #pragma unroll
   for (int i = 0; i < RPT; ++i) {
@@ -201,25 +215,36 @@ __global__ void __launch_bounds__(512) dn_recur_kernel(RecurArgs a) {
       p = __fadd_rn(p, __fmul_rn(nv, sq[r]));
     }
   }
-  __syncthreads();  // red is reused
+  __syncthreads();  // red and vec are reused
   red[threadIdx.x] = p;
   __syncthreads();
   float o = 0.0f;
   if (g == 0) {
-    for (int q = 0; q < RG; ++q) o = __fadd_rn(o, red[q * vd + c]);
-    vec[c] = __fmul_rn(o, o);
+    for (int q = 0; q < RG; ++q) o = __fadd_rn(o, red[q * vl + cl]);
+    vec[cl] = __fmul_rn(o, o);
   }
   __syncthreads();
   // rms_norm_inplace (:270-284) over the head's vd outputs, then the gate (:537-541).
   if (threadIdx.x == 0) {
     float ss = 0.0f;
-    for (int q = 0; q < vd; ++q) ss = __fadd_rn(ss, vec[q]);
-    scal[0] = 1.0f / sqrtf(__fadd_rn(ss / (float)vd, a.eps));
+    for (int q = 0; q < vl; ++q) ss = __fadd_rn(ss, vec[q]);
+    scal[2] = ss;
   }
-  __syncthreads();
+  float total;
+  if (NS > 1) {
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();  // every part's sum of squares is in place
+    total = 0.0f;
+    for (int q = 0; q < NS; ++q) total = __fadd_rn(total, *cluster.map_shared_rank(&scal[2], q));
+    cluster.sync();  // no part leaves while another may still read its sum
+  } else {
+    __syncthreads();
+    total = scal[2];
+  }
+  const float scale = 1.0f / sqrtf(__fadd_rn(total / (float)vd, a.eps));
   if (g == 0) {
-    const float zc = a.z[(int64_t)b * a.z_dim + h * vd + c];
-    const float out = __fmul_rn(dn_silu(zc), __fmul_rn(o, scal[0]));
+    const float zc = a.z[(int64_t)b * a.z_ld + h * vd + c];
+    const float out = __fmul_rn(dn_silu(zc), __fmul_rn(o, scale));
     const int64_t idx = (int64_t)b * a.z_dim + h * vd + c;
     if (a.og_dt == NVFP4_DTYPE_F32)
       static_cast<float *>(a.og)[idx] = out;
@@ -252,16 +277,29 @@ int check_dn_desc(const nvfp4_deltanet_desc *s) {
   return NVFP4_OK;
 }
 
+template <int RPT, int STRIDE>
+cudaError_t launch_recur_cfg(const RecurArgs &a, int B, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.nvh * a.nsplit, B, 1);
+  cfg.blockDim = dim3((a.vd / a.nsplit) * a.rg, 1, 1);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = a.nsplit;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = a.nsplit > 1 ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, dn_recur_kernel<RPT, STRIDE>, a);
+}
+
 template <int RPT>
 cudaError_t launch_recur(const RecurArgs &a, int B, cudaStream_t st) {
-  if constexpr (RPT == 32) {
-    if (a.kd == 128 && a.vd == 128 && a.rg == 4) {
-      dn_recur_kernel<32, 512><<<dim3(a.nvh, B), a.vd * a.rg, 0, st>>>(a);
-      return cudaGetLastError();
-    }
+  if constexpr (RPT == 8) {
+    if (a.kd == 128 && a.vd == 128 && a.nsplit == 4 && a.rg == 16)
+      return launch_recur_cfg<8, 16 * 128>(a, B, st);
   }
-  dn_recur_kernel<RPT, 0><<<dim3(a.nvh, B), a.vd * a.rg, 0, st>>>(a);
-  return cudaGetLastError();
+  return launch_recur_cfg<RPT, 0>(a, B, st);
 }
 
 }  // namespace
@@ -317,14 +355,27 @@ extern "C" int nvfp4_deltanet_forward(const nvfp4_deltanet_desc *desc,
     if ((rc = check_launch(cudaGetLastError(), "DeltaNet input conversion"))) return rc;
     hx = base + L.hx;
   }
-  if ((rc = run_proj(w->qkv, d.d, d.qkv_dim, hx, proj_dt, qkv, NVFP4_DTYPE_F32, B, st))) return rc;
-  if ((rc = run_proj(w->z, d.d, d.z_dim, hx, proj_dt, z, NVFP4_DTYPE_F32, B, st))) return rc;
-  if ((rc = run_proj(w->b, d.d, d.nvh, hx, proj_dt, braw, NVFP4_DTYPE_F32, B, st))) return rc;
-  if ((rc = run_proj(w->a, d.d, d.nvh, hx, proj_dt, araw, NVFP4_DTYPE_F32, B, st))) return rc;
+  // One GEMV over the fused rows [qkv; z; b; a] when given, else four.
+  int64_t qkv_ld = d.qkv_dim, z_ld = d.z_dim, ba_ld = d.nvh;
+  if (w->in_proj.packed_weights) {
+    const int64_t rows = (int64_t)d.qkv_dim + d.z_dim + 2 * d.nvh;
+    float *all = qkv;  // [B, rows] in the (contiguous) qkv .. araw regions
+    if ((rc = run_proj(w->in_proj, d.d, rows, hx, proj_dt, all, NVFP4_DTYPE_F32, B, st))) return rc;
+    qkv_ld = z_ld = ba_ld = rows;
+    z = all + d.qkv_dim;
+    braw = all + d.qkv_dim + d.z_dim;
+    araw = braw + d.nvh;
+  } else {
+    if ((rc = run_proj(w->qkv, d.d, d.qkv_dim, hx, proj_dt, qkv, NVFP4_DTYPE_F32, B, st))) return rc;
+    if ((rc = run_proj(w->z, d.d, d.z_dim, hx, proj_dt, z, NVFP4_DTYPE_F32, B, st))) return rc;
+    if ((rc = run_proj(w->b, d.d, d.nvh, hx, proj_dt, braw, NVFP4_DTYPE_F32, B, st))) return rc;
+    if ((rc = run_proj(w->a, d.d, d.nvh, hx, proj_dt, araw, NVFP4_DTYPE_F32, B, st))) return rc;
+  }
 
   // Steps 2-3 (:431-479): causal conv1d + SiLU, windows shifted.
   ConvArgs ca;
   ca.qkv = qkv;
+  ca.qkv_ld = qkv_ld;
   ca.post = post;
   ca.buf[0] = state->conv_q;
   ca.buf[1] = state->conv_k;
@@ -350,6 +401,8 @@ extern "C" int nvfp4_deltanet_forward(const nvfp4_deltanet_desc *desc,
   ra.z = z;
   ra.braw = braw;
   ra.araw = araw;
+  ra.z_ld = z_ld;
+  ra.ba_ld = ba_ld;
   ra.a_log = w->a_log;
   ra.dt_bias = w->dt_bias;
   ra.s = state->s;
@@ -364,7 +417,10 @@ extern "C" int nvfp4_deltanet_forward(const nvfp4_deltanet_desc *desc,
   ra.qkv_dim = d.qkv_dim;
   ra.z_dim = d.z_dim;
   ra.eps = desc->rms_eps;
-  ra.rg = std::min(d.kd, 512 / d.vd);  // vd x rg threads, up to 512
+  // vd >= 64: clusters of vd / 32 CTAs of 32 columns each (at most 8).
+  ra.nsplit = d.vd >= 64 ? std::min(8, d.vd / 32) : 1;
+  const int vl = d.vd / ra.nsplit;
+  ra.rg = std::min(d.kd, 512 / vl);  // vl x rg threads, up to 512
   const int rpt = (d.kd + ra.rg - 1) / ra.rg;
   cudaError_t e;
   if (rpt <= 1) e = launch_recur<1>(ra, (int)B, st);

@@ -810,6 +810,20 @@ cudaError_t launch_mode(GemvArgs a, int items, int64_t total_rows, cudaStream_t 
     }
   }
   if (bestC == 0) return cudaErrorInvalidValue;
+  if (MODE == kGvPlain) {
+    // Leave room on each SM for one CTA of the next launch (which then
+    // streams its weights beside this one's tail): fewer ring stages, down
+    // to two, until (CTAs per SM + 1) CTAs fit.  K=4096, N=14336 (clusters
+    // of 4, 276 CTAs): three stages -> two took M = 1 from 12.8 to 11.8 us.
+    const int sms = tc_sm_count();
+    const int per_sm = (bestC * bestNq + sms - 1) / sms;
+    const int xstride = 2 * (a.K / bestC) + 64;
+    while (bestS > 2 &&
+           (size_t)(per_sm + 1) *
+                   (1024 + GemvSmem(bestW, bestS, xstride, M, bestC, kParts, kSplit).total) >
+               (size_t)227 * 1024)
+      --bestS;
+  }
   a.ks = a.K / bestC;
   a.xstride = 2 * a.ks + 64;
   a.stages = bestS;

@@ -115,7 +115,8 @@ class DeltaNetWeightPtrs(ctypes.Structure):
     """struct nvfp4_deltanet_weights."""
 
     _fields_ = [("qkv", DeltaNetProj), ("z", DeltaNetProj), ("b", DeltaNetProj),
-                ("a", DeltaNetProj), ("out", DeltaNetProj), ("a_log", ctypes.c_void_p),
+                ("a", DeltaNetProj), ("out", DeltaNetProj), ("in_proj", DeltaNetProj),
+                ("a_log", ctypes.c_void_p),
                 ("dt_bias", ctypes.c_void_p), ("conv_q", ctypes.c_void_p),
                 ("conv_k", ctypes.c_void_p), ("conv_v", ctypes.c_void_p),
                 ("conv_bias_q", ctypes.c_void_p), ("conv_bias_k", ctypes.c_void_p),

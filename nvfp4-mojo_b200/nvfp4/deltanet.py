@@ -146,15 +146,44 @@ class DeltaNetWeights:
     conv_bias_q: Optional[torch.Tensor] = None
     conv_bias_k: Optional[torch.Tensor] = None
     conv_bias_v: Optional[torch.Tensor] = None
+    in_proj: Optional[tuple] = None  # rows [qkv; z; b; a] fused (fuse_in_proj)
 
     def ptrs(self) -> "_lib.DeltaNetWeightPtrs":
         f = lambda t, n: None if t is None else _dev(t, n)
         return _lib.DeltaNetWeightPtrs(
             _proj(*self.qkv), _proj(*self.z), _proj(*self.b), _proj(*self.a), _proj(*self.out),
+            _proj(*self.in_proj) if self.in_proj is not None else _lib.DeltaNetProj(),
             f(self.a_log, "a_log"), f(self.dt_bias, "dt_bias"), f(self.conv_q, "conv_q"),
             f(self.conv_k, "conv_k"), f(self.conv_v, "conv_v"),
             f(self.conv_bias_q, "conv_bias_q"), f(self.conv_bias_k, "conv_bias_k"),
             f(self.conv_bias_v, "conv_bias_v"))
+
+
+def fuse_in_proj(weights: DeltaNetWeights, stream=None) -> DeltaNetWeights:
+    """The same weights with the qkv, z, b and a projections row-stacked into
+    one NVFP4 matrix (nvfp4_stack_rows), so a step takes one input
+    projection launch instead of four.  The four must share input_scale;
+    their per-row weight_scale_2 are stacked (scalar ones broadcast)."""
+    from .moe import stack_rows
+
+    parts = [weights.qkv, weights.z, weights.b, weights.a]
+    ins = {float(p[0].input_scale) for p in parts}
+    if len(ins) != 1:
+        raise ValueError("the fused projection needs one input_scale")
+    K = parts[0][0].in_features
+    rows = []
+    for lin, _, _ in parts:
+        r = lin.weight_scale_2_rows
+        rows.append(r if r is not None else
+                    torch.full((lin.out_features,), float(lin.weight_scale_2),
+                               dtype=torch.float32, device=parts[0][1].device))
+    w = stack_rows([p[1] for p in parts], stream=stream)
+    sf = stack_rows([_u8(p[2]) for p in parts], stream=stream)
+    ws2 = stack_rows(rows, stream=stream)
+    lin = NvFp4Linear(K, w.shape[0], input_scale=ins.pop(), weight_scale_2_rows=ws2)
+    from dataclasses import replace
+
+    return replace(weights, in_proj=(lin, w, sf))
 
 
 _DT = {torch.float32: _lib.DTYPE_F32, torch.bfloat16: _lib.DTYPE_BF16}

@@ -24,7 +24,7 @@ def rel_err(got, ref):
     return float(np.abs(got - ref).max() / np.sqrt(np.mean(ref * ref)))
 
 
-def build(O, cfg, seed, bias):
+def build(O, cfg, seed, bias, same_ins=False):
     """Random NVFP4 projections + fp32 small weights, for the GPU and the oracle."""
     import nvfp4
     from nvfp4 import synthetic
@@ -38,6 +38,8 @@ def build(O, cfg, seed, bias):
     for i, (name, (n, k)) in enumerate(shapes.items()):
         wd = synthetic.linear_weights(n, k, seed=seed + 10 * i)
         ins = np.float32(rng.uniform(0.5, 1.5))
+        if same_ins and name != "out":
+            ins = np.float32(0.875)
         lin = nvfp4.NvFp4Linear(k, n, input_scale=float(ins),
                                 weight_scale_2_rows=torch.from_numpy(wd["ws2"]).cuda())
         gpu[name] = (lin, torch.from_numpy(wd["w"]).cuda(), torch.from_numpy(wd["sf"]).cuda())
@@ -62,11 +64,13 @@ def cfg_dict(cfg):
                 value_dim=cfg.value_dim, conv_kernel=cfg.conv_kernel, rms_eps=cfg.rms_eps)
 
 
-def run_steps(O, cfg, B, steps, proj, tol, seed, bias, tol_state=None):
+def run_steps(O, cfg, B, steps, proj, tol, seed, bias, tol_state=None, fused=False):
     tol_state = tol if tol_state is None else tol_state
-    from nvfp4.deltanet import DeltaNetState, deltanet_forward
+    from nvfp4.deltanet import DeltaNetState, deltanet_forward, fuse_in_proj
 
-    w, ref = build(O, cfg, seed, bias)
+    w, ref = build(O, cfg, seed, bias, same_ins=fused)
+    if fused:
+        w = fuse_in_proj(w)
     state = DeltaNetState(cfg, batch=B)
     ref_states = [O.deltanet_state(cfg_dict(cfg)) for _ in range(B)]
     rng = np.random.default_rng(seed + 99)
@@ -87,25 +91,40 @@ def run_steps(O, cfg, B, steps, proj, tol, seed, bias, tol_state=None):
 
 @pytest.mark.parametrize("proj,tol,tol_state", [(torch.float32, 1e-4, 1e-3),
                                                 (torch.bfloat16, 2e-2, 2e-2)])
-def test_deltanet_small(O, cuda, proj, tol, tol_state):
+@pytest.mark.parametrize("fused", [False, True])
+def test_deltanet_small(O, cuda, proj, tol, tol_state, fused):
     """d_model 64, 2 key / 4 value heads of 16 x 16, conv kernel 4 with
-    biases, 3 sequences, 3 steps."""
+    biases, 3 sequences, 3 steps; four input projections or one fused."""
     from nvfp4.deltanet import DeltaNetConfig
 
     cfg = DeltaNetConfig(d_model=64, num_key_heads=2, num_value_heads=4, key_dim=16,
                          value_dim=16, conv_kernel=4)
-    run_steps(O, cfg, B=3, steps=3, proj=proj, tol=tol, seed=5, bias=True, tol_state=tol_state)
+    run_steps(O, cfg, B=3, steps=3, proj=proj, tol=tol, seed=5, bias=True, tol_state=tol_state,
+              fused=fused)
+
+
+def test_deltanet_split_heads(O, cuda):
+    """value_dim 64 (each head's columns over a cluster of 2 CTAs), key_dim
+    48, conv kernel 3, 5 sequences, 3 steps, fp32 projections."""
+    from nvfp4.deltanet import DeltaNetConfig
+
+    cfg = DeltaNetConfig(d_model=128, num_key_heads=2, num_value_heads=4, key_dim=48,
+                         value_dim=64, conv_kernel=3)
+    run_steps(O, cfg, B=5, steps=3, proj=torch.float32, tol=1e-4, seed=9, bias=False,
+              tol_state=1e-3)
 
 
 @pytest.mark.parametrize("proj,tol,tol_state", [(torch.float32, 1e-4, 1e-3),
                                                 (torch.bfloat16, 2e-2, 2e-2)])
-def test_deltanet_default_layer(O, cuda, proj, tol, tol_state):
+@pytest.mark.parametrize("fused", [False, True])
+def test_deltanet_default_layer(O, cuda, proj, tol, tol_state, fused):
     """The reference's default layer (d_model 2048, 16 key / 32 value heads of
-    128 x 128, conv kernel 4, no biases), 2 sequences, 2 steps."""
+    128 x 128 -- each head over a cluster of 4 CTAs --, conv kernel 4, no
+    biases), 2 sequences, 2 steps."""
     from nvfp4.deltanet import DeltaNetConfig
 
     run_steps(O, DeltaNetConfig(), B=2, steps=2, proj=proj, tol=tol, seed=7, bias=False,
-              tol_state=tol_state)
+              tol_state=tol_state, fused=fused)
 
 
 def test_deltanet_validation(cuda):
