@@ -115,22 +115,53 @@ struct ConvArgs {
 
 // conv1d_step (nvfp4/deltanet.mojo:287-328) then SiLU, one thread per
 // (sequence, channel): the window of that channel is read, then shifted.
+// Launched with programmatic dependent launch after the input projection:
+// the window (last written by this layer's previous step, which completed
+// before that projection could start) and the weights are read before
+// griddepcontrol.wait, the projection's output after it (L2-coherent).
 __global__ void dn_conv_kernel(ConvArgs a) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= a.n) return;
-  const int64_t b = i / a.qkv_dim;
-  int ch = (int)(i - b * a.qkv_dim), seg = 0;
-  while (seg < 2 && ch >= a.dim[seg]) ch -= a.dim[seg++];
+  const bool live = i < a.n;
+  const int64_t b = live ? i / a.qkv_dim : 0;
+  int ch = live ? (int)(i - b * a.qkv_dim) : 0, seg = 0;
+  if (ch >= a.dim[0]) {
+    ch -= a.dim[0];
+    seg = 1;
+    if (ch >= a.dim[1]) {
+      ch -= a.dim[1];
+      seg = 2;
+    }
+  }
+  // Selects, not indexing: a runtime index into the parameter arrays would
+  // copy them to local memory.
+  const int dim = seg == 0 ? a.dim[0] : seg == 1 ? a.dim[1] : a.dim[2];
+  float *const sbuf = seg == 0 ? a.buf[0] : seg == 1 ? a.buf[1] : a.buf[2];
+  const float *const sw = seg == 0 ? a.w[0] : seg == 1 ? a.w[1] : a.w[2];
+  const float *const sbias = seg == 0 ? a.bias[0] : seg == 1 ? a.bias[1] : a.bias[2];
   const int hist = a.ck - 1;
-  float *buf = a.buf[seg] + (b * a.dim[seg] + ch) * hist;
-  const float *w = a.w[seg] + (int64_t)ch * a.ck;
-  const float x = a.qkv[b * a.qkv_ld + (i - b * a.qkv_dim)];
-  float acc = 0.0f;
-  for (int t = 0; t < hist; ++t) acc = __fadd_rn(acc, __fmul_rn(buf[t], w[t]));
-  acc = __fadd_rn(acc, __fmul_rn(x, w[hist]));
-  if (a.bias[seg]) acc = __fadd_rn(acc, a.bias[seg][ch]);
+  float *buf = sbuf + (b * dim + ch) * hist;
+  const float *w = sw + (int64_t)ch * a.ck;
+  float acc = 0.0f, wl = 0.0f, hb[8];  // conv_kernel <= 8: hist <= 7
+  if (live) {
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      if (t < hist) {
+        hb[t] = __ldcg(buf + t);
+        acc = __fadd_rn(acc, __fmul_rn(hb[t], w[t]));
+      }
+    }
+    wl = w[hist];
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (!live) return;
+  const float x = __ldcg(a.qkv + b * a.qkv_ld + (i - b * a.qkv_dim));
+  acc = __fadd_rn(acc, __fmul_rn(x, wl));
+  if (sbias) acc = __fadd_rn(acc, sbias[ch]);
   a.post[i] = dn_silu(acc);
-  for (int t = 0; t + 1 < hist; ++t) buf[t] = buf[t + 1];
+#pragma unroll
+  for (int t = 0; t < 7; ++t)
+    if (t + 1 < hist) buf[t] = hb[t + 1];
   if (hist > 0) buf[hist - 1] = x;
 }
 
@@ -167,26 +198,33 @@ __global__ void __launch_bounds__(512) dn_recur_kernel(RecurArgs a) {
   const int vd = a.vd, vl = vd / NS, kd = a.kd, RG = a.rg;
   const int cl = threadIdx.x % vl, g = threadIdx.x / vl, c = part * vl + cl;
   const int kh = h / a.vg;
-  const float *row = a.post + (int64_t)b * a.qkv_dim;
-  for (int r = threadIdx.x; r < kd; r += blockDim.x) {
-    sq[r] = row[kh * kd + r];
-    sk[r] = row[a.q_dim + kh * kd + r];
-  }
-  if (threadIdx.x == 0) {
-    const float braw = a.braw[(int64_t)b * a.ba_ld + h];
-    const float araw = a.araw[(int64_t)b * a.ba_ld + h];
-    scal[0] = dn_sigmoid(braw);  // beta (:484-487)
-    const float a_val = dn_softplus(a.a_log[h]);
-    const float dt_val = dn_softplus(__fadd_rn(araw, a.dt_bias[h]));
-    scal[1] = expf(-__fmul_rn(a_val, dt_val));  // decay (:489-494)
-  }
-  __syncthreads();
+  // Launched with programmatic dependent launch after the conv kernel: the
+  // state (last written by this layer's previous step, complete before the
+  // conv kernel could start) is loaded before griddepcontrol.wait, the
+  // outputs of the conv kernel and of the input projection after it.
   // Row r = g + i RG of column c sits at S + r vd + c: one pointer, one stride.
   float *const Sg = a.s + ((int64_t)b * a.nvh + h) * kd * vd + (int64_t)g * vd + c;
   const int stride = STRIDE ? STRIDE : RG * vd;
   float s[RPT];
 #pragma unroll
-  for (int i = 0; i < RPT; ++i) s[i] = g + i * RG < kd ? Sg[i * stride] : 0.0f;
+  for (int i = 0; i < RPT; ++i) s[i] = g + i * RG < kd ? __ldcg(Sg + i * stride) : 0.0f;
+  const float a_log = a.a_log[h], dt_bias = a.dt_bias[h];
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const float *row = a.post + (int64_t)b * a.qkv_dim;
+  for (int r = threadIdx.x; r < kd; r += blockDim.x) {
+    sq[r] = __ldcg(row + kh * kd + r);
+    sk[r] = __ldcg(row + a.q_dim + kh * kd + r);
+  }
+  if (threadIdx.x == 0) {
+    const float braw = __ldcg(a.braw + (int64_t)b * a.ba_ld + h);
+    const float araw = __ldcg(a.araw + (int64_t)b * a.ba_ld + h);
+    scal[0] = dn_sigmoid(braw);  // beta (:484-487)
+    const float a_val = dn_softplus(a_log);
+    const float dt_val = dn_softplus(__fadd_rn(araw, dt_bias));
+    scal[1] = expf(-__fmul_rn(a_val, dt_val));  // decay (:489-494)
+  }
+  __syncthreads();
   // S^T k (:512), partial over this thread's rows, then over the groups.
   float p = 0.0f;
 #pragma unroll
@@ -199,7 +237,7 @@ __global__ void __launch_bounds__(512) dn_recur_kernel(RecurArgs a) {
   if (g == 0) {
     float stk = 0.0f;
     for (int q = 0; q < RG; ++q) stk = __fadd_rn(stk, red[q * vl + cl]);
-    const float v = row[a.q_dim + a.k_dim + h * vd + c];
+    const float v = __ldcg(row + a.q_dim + a.k_dim + h * vd + c);
     vec[cl] = __fadd_rn(v, -stk);  // v - S^T k (:515-516)
   }
   __syncthreads();
@@ -243,7 +281,7 @@ __global__ void __launch_bounds__(512) dn_recur_kernel(RecurArgs a) {
   }
   const float scale = 1.0f / sqrtf(__fadd_rn(total / (float)vd, a.eps));
   if (g == 0) {
-    const float zc = a.z[(int64_t)b * a.z_ld + h * vd + c];
+    const float zc = __ldcg(a.z + (int64_t)b * a.z_ld + h * vd + c);
     const float out = __fmul_rn(dn_silu(zc), __fmul_rn(o, scale));
     const int64_t idx = (int64_t)b * a.z_dim + h * vd + c;
     if (a.og_dt == NVFP4_DTYPE_F32)
@@ -283,13 +321,15 @@ cudaError_t launch_recur_cfg(const RecurArgs &a, int B, cudaStream_t st) {
   cfg.gridDim = dim3(a.nvh * a.nsplit, B, 1);
   cfg.blockDim = dim3((a.vd / a.nsplit) * a.rg, 1, 1);
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = a.nsplit;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = a.nsplit;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = a.nsplit > 1 ? 1 : 0;
+  cfg.numAttrs = a.nsplit > 1 ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, dn_recur_kernel<RPT, STRIDE>, a);
 }
 
@@ -392,8 +432,19 @@ extern "C" int nvfp4_deltanet_forward(const nvfp4_deltanet_desc *desc,
   ca.qkv_dim = d.qkv_dim;
   ca.ck = d.ck;
   ca.n = B * d.qkv_dim;
-  dn_conv_kernel<<<(unsigned)((ca.n + 255) / 256), 256, 0, st>>>(ca);
-  if ((rc = check_launch(cudaGetLastError(), "DeltaNet conv launch"))) return rc;
+  {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((ca.n + 255) / 256), 1, 1);
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if ((rc = check_launch(cudaLaunchKernelEx(&cfg, dn_conv_kernel, ca), "DeltaNet conv launch")))
+      return rc;
+  }
 
   // Steps 4-5 (:481-541): the recurrence per (value head, sequence).
   RecurArgs ra;
