@@ -45,10 +45,12 @@ __global__ void __launch_bounds__(32 * kRouterWarps)
   float *red = xs + (size_t)hslice * kRouterTok;
   const int e0 = blockIdx.x * 32, t0 = blockIdx.y * kRouterTok, h0 = blockIdx.z * hslice;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  pdl_wait();  // x may come from the previous kernel
+  pdl_trigger();
   for (int i = threadIdx.x; i < hslice * kRouterTok; i += blockDim.x) {
     const int h = i / kRouterTok, tt = i % kRouterTok;
     const int t = t0 + tt;
-    xs[i] = t < T ? __uint_as_float((uint32_t)x[(int64_t)t * H + h0 + h] << 16) : 0.0f;
+    xs[i] = t < T ? __uint_as_float((uint32_t)__ldcg(x + (int64_t)t * H + h0 + h) << 16) : 0.0f;
   }
   __syncthreads();
   const int e = min(e0 + lane, E - 1);
@@ -147,8 +149,8 @@ __global__ void __launch_bounds__(128) router_logits_tc_kernel(const uint16_t *_
   auto fetch = [&](int h0) {
 #pragma unroll
     for (int u = 0; u < 2; ++u)
-      xr[u] = xv[u] ? __ldg(reinterpret_cast<const uint4 *>(x + (int64_t)(t0 + xt[u]) * H + h0 +
-                                                            xk[u]))
+      xr[u] = xv[u] ? __ldcg(reinterpret_cast<const uint4 *>(x + (int64_t)(t0 + xt[u]) * H + h0 +
+                                                             xk[u]))
                     : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
     for (int u = 0; u < 4; ++u)
@@ -162,6 +164,8 @@ __global__ void __launch_bounds__(128) router_logits_tc_kernel(const uint16_t *_
   for (int j = 0; j < 8; ++j)
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[j][i] = 0.0f;
+  pdl_wait();  // x may come from the previous kernel
+  pdl_trigger();
   fetch(hbeg);
   for (int h0 = hbeg; h0 < hend; h0 += kRtcK) {
 #pragma unroll
@@ -238,6 +242,8 @@ __global__ void router_topk_kernel(const float *__restrict__ part, int nslices,
                                    int renormalize, int32_t *__restrict__ topk_ids,
                                    float *__restrict__ topk_w) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  pdl_wait();
+  pdl_trigger();
   if (warp >= T) return;
   float p[8];
   float mx = -FLT_MAX;
@@ -246,7 +252,7 @@ __global__ void router_topk_kernel(const float *__restrict__ part, int nslices,
     const int e = lane + 32 * i;
     float v = 0.0f;
     if (e < E) {
-      for (int z = 0; z < nslices; ++z) v += part[((int64_t)z * T + warp) * E + e];
+      for (int z = 0; z < nslices; ++z) v += __ldcg(part + ((int64_t)z * T + warp) * E + e);
       if (logits_out) logits_out[(int64_t)warp * E + e] = v;
     }
     p[i] = e < E ? v : -FLT_MAX;
@@ -340,7 +346,9 @@ cudaError_t launch_router(const uint16_t *x, const float *router, float *part, i
   const bool aligned16 = (((uintptr_t)x | (uintptr_t)router) & 15) == 0;
   if (router_tc_ok(T, H, E) && aligned16 && H % (nslices * kRtcK) == 0) {
     dim3 grid((E + kRtcExp - 1) / kRtcExp, (T + kRtcTok - 1) / kRtcTok, nslices);
-    router_logits_tc_kernel<<<grid, 128, 0, st>>>(x, router, part, T, H, E, H / nslices);
+    cudaError_t e = launch_pdl(router_logits_tc_kernel, grid, dim3(128), 0, st, x, router, part, T,
+                               H, E, H / nslices);
+    if (e != cudaSuccess) return e;
   } else {
     while (nslices > 1 && H % (nslices * kRouterWarps) != 0) nslices >>= 1;
     const int hslice = H / nslices;
@@ -353,11 +361,12 @@ cudaError_t launch_router(const uint16_t *x, const float *router, float *part, i
       configured = smem;
     }
     dim3 grid((E + 31) / 32, (T + kRouterTok - 1) / kRouterTok, nslices);
-    router_logits_kernel<<<grid, 32 * kRouterWarps, smem, st>>>(x, router, part, T, H, E, hslice);
+    cudaError_t e = launch_pdl(router_logits_kernel, grid, dim3(32 * kRouterWarps), smem, st, x,
+                               router, part, T, H, E, hslice);
+    if (e != cudaSuccess) return e;
   }
-  router_topk_kernel<<<(T * 32 + 255) / 256, 256, 0, st>>>(part, nslices, logits_out, T, E, k,
-                                                           renormalize, ids, w);
-  return cudaGetLastError();
+  return launch_pdl(router_topk_kernel, dim3((T * 32 + 255) / 256), dim3(256), 0, st, part,
+                    nslices, logits_out, T, E, k, renormalize, ids, w);
 }
 
 // ---------------------------------------------------------------------------
@@ -370,10 +379,12 @@ __global__ void __launch_bounds__(1024) moe_permute_kernel(const int32_t *__rest
                                                           int R, int E, int tpi, MoePlan plan) {
   __shared__ int cnt[1024], off[1025], cur[1024], items[1025];
   const int tid = threadIdx.x;
+  pdl_wait();  // the routing ids come from the previous kernels
+  pdl_trigger();
   for (int e = tid; e < E; e += blockDim.x) cnt[e] = 0;
   __syncthreads();
   for (int r = tid; r < R; r += blockDim.x) {
-    const int e = row_expert[r];
+    const int e = __ldcg(row_expert + r);
     if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
   }
   __syncthreads();
@@ -405,10 +416,10 @@ __global__ void __launch_bounds__(1024) moe_permute_kernel(const int32_t *__rest
   }
   __syncthreads();
   for (int r = tid; r < R; r += blockDim.x) {
-    const int e = row_expert[r];
+    const int e = __ldcg(row_expert + r);
     if (e >= 0 && e < E) {
       const int p = atomicAdd(&cur[e], 1);
-      plan.src_row[p] = x_row_index ? x_row_index[r] : r;
+      plan.src_row[p] = x_row_index ? __ldcg(x_row_index + r) : r;
       plan.dst_row[p] = r;
     }
   }
@@ -422,20 +433,21 @@ __global__ void __launch_bounds__(1024) moe_permute_kernel(const int32_t *__rest
 
 cudaError_t launch_moe_permute(const int32_t *row_expert, const int32_t *x_row_index, int R,
                                int E, int tpi, const MoePlan &plan, cudaStream_t st) {
-  moe_permute_kernel<<<1, 1024, 0, st>>>(row_expert, x_row_index, R, E, tpi, plan);
-  return cudaGetLastError();
+  return launch_pdl(moe_permute_kernel, dim3(1), dim3(1024), 0, st, row_expert, x_row_index, R, E,
+                    tpi, plan);
 }
 
 // Slot -> token index for the single-GPU forward: row r = t * k + j reads x[t].
 __global__ void slot_token_kernel(int32_t *__restrict__ idx, int R, int k) {
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  pdl_wait();  // keeps the chain of programmatic launches ordered
+  pdl_trigger();
   if (r < R) idx[r] = r / k;
 }
 
 cudaError_t launch_slot_token(int32_t *idx, int R, int k, cudaStream_t st) {
   if (R == 0) return cudaSuccess;
-  slot_token_kernel<<<(R + 255) / 256, 256, 0, st>>>(idx, R, k);
-  return cudaGetLastError();
+  return launch_pdl(slot_token_kernel, dim3((R + 255) / 256), dim3(256), 0, st, idx, R, k);
 }
 
 // ---------------------------------------------------------------------------
@@ -609,18 +621,20 @@ cudaError_t launch_ep_pad(const int32_t *counts, const int32_t *send_token,
 // sums in j order, residual added last, one bf16 rounding at the end.  Slot
 // outputs are fp32 (or bf16).  8 features per thread.
 // ---------------------------------------------------------------------------
+// L2-coherent loads: the data comes from the kernels before (programmatic
+// dependent launch).
 template <typename SlotT>
 __device__ __forceinline__ void load8(const SlotT *p, float (&v)[8]);
 template <>
 __device__ __forceinline__ void load8<float>(const float *p, float (&v)[8]) {
-  const float4 a = *reinterpret_cast<const float4 *>(p);
-  const float4 b = *reinterpret_cast<const float4 *>(p + 4);
+  const float4 a = __ldcg(reinterpret_cast<const float4 *>(p));
+  const float4 b = __ldcg(reinterpret_cast<const float4 *>(p + 4));
   v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
   v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
 template <>
 __device__ __forceinline__ void load8<uint16_t>(const uint16_t *p, float (&v)[8]) {
-  const uint4 r = *reinterpret_cast<const uint4 *>(p);
+  const uint4 r = __ldcg(reinterpret_cast<const uint4 *>(p));
   const uint32_t rr[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
@@ -637,14 +651,16 @@ __global__ void moe_combine_kernel(const SlotT *__restrict__ ys, const float *__
                                    int T, int k, int H) {
   const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;  // vector index
   const int hv = H / 8;
+  pdl_wait();
+  pdl_trigger();
   if (i >= (int64_t)T * hv) return;
   const int t = (int)(i / hv), h8 = (int)(i % hv);
   float s[8];
 #pragma unroll
   for (int q = 0; q < 8; ++q) s[q] = 0.0f;
   for (int j = 0; j < k; ++j) {
-    const float wj = w[(int64_t)t * k + j];
-    const int64_t row = slot_pos ? slot_pos[(int64_t)t * k + j] : (int64_t)t * k + j;
+    const float wj = __ldcg(w + (int64_t)t * k + j);
+    const int64_t row = slot_pos ? __ldcg(slot_pos + (int64_t)t * k + j) : (int64_t)t * k + j;
     if (row < 0) continue;  // slot that was not dispatched contributes nothing
     float v[8];
     load8<SlotT>(ys + row * H + 8 * h8, v);
@@ -685,14 +701,17 @@ cudaError_t launch_moe_combine(const void *ys, int ys_dtype, const float *w,
   const float *yf = static_cast<const float *>(ys);
   const uint16_t *yb = static_cast<const uint16_t *>(ys);
   if (ys_dtype == kF32 && y_dtype == kF32)
-    moe_combine_kernel<float, float><<<blocks, 256, 0, st>>>(yf, w, residual, slot_pos, extra, static_cast<float *>(y), T, k, H);
+    return launch_pdl(moe_combine_kernel<float, float>, dim3(blocks), dim3(256), 0, st, yf, w,
+                      residual, slot_pos, extra, static_cast<float *>(y), T, k, H);
   else if (ys_dtype == kF32)
-    moe_combine_kernel<float, uint16_t><<<blocks, 256, 0, st>>>(yf, w, residual, slot_pos, extra, static_cast<uint16_t *>(y), T, k, H);
+    return launch_pdl(moe_combine_kernel<float, uint16_t>, dim3(blocks), dim3(256), 0, st, yf, w,
+                      residual, slot_pos, extra, static_cast<uint16_t *>(y), T, k, H);
   else if (y_dtype == kF32)
-    moe_combine_kernel<uint16_t, float><<<blocks, 256, 0, st>>>(yb, w, residual, slot_pos, extra, static_cast<float *>(y), T, k, H);
+    return launch_pdl(moe_combine_kernel<uint16_t, float>, dim3(blocks), dim3(256), 0, st, yb, w,
+                      residual, slot_pos, extra, static_cast<float *>(y), T, k, H);
   else
-    moe_combine_kernel<uint16_t, uint16_t><<<blocks, 256, 0, st>>>(yb, w, residual, slot_pos, extra, static_cast<uint16_t *>(y), T, k, H);
-  return cudaGetLastError();
+    return launch_pdl(moe_combine_kernel<uint16_t, uint16_t>, dim3(blocks), dim3(256), 0, st, yb,
+                      w, residual, slot_pos, extra, static_cast<uint16_t *>(y), T, k, H);
 }
 
 }  // namespace nvfp4
