@@ -252,7 +252,15 @@ __global__ void router_topk_kernel(const float *__restrict__ part, int nslices,
     const int e = lane + 32 * i;
     float v = 0.0f;
     if (e < E) {
-      for (int z = 0; z < nslices; ++z) v += __ldcg(part + ((int64_t)z * T + warp) * E + e);
+      // All slices' loads first (up to 16 in flight), then the sum in z order.
+      float pz[16];
+#pragma unroll
+      for (int z = 0; z < 16; ++z)
+        pz[z] = z < nslices ? __ldcg(part + ((int64_t)z * T + warp) * E + e) : 0.0f;
+#pragma unroll
+      for (int z = 0; z < 16; ++z)
+        if (z < nslices) v += pz[z];
+      for (int z = 16; z < nslices; ++z) v += __ldcg(part + ((int64_t)z * T + warp) * E + e);
       if (logits_out) logits_out[(int64_t)warp * E + e] = v;
     }
     p[i] = e < E ? v : -FLT_MAX;
@@ -382,24 +390,60 @@ __global__ void __launch_bounds__(1024) moe_permute_kernel(const int32_t *__rest
   pdl_wait();  // the routing ids come from the previous kernels
   pdl_trigger();
   for (int e = tid; e < E; e += blockDim.x) cnt[e] = 0;
+  // The first 4 x 1024 routing ids stay in registers for the scatter below.
+  int my_e[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = tid + i * 1024;
+    my_e[i] = r < R ? __ldcg(row_expert + r) : -1;
+  }
   __syncthreads();
-  for (int r = tid; r < R; r += blockDim.x) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    if (my_e[i] >= 0 && my_e[i] < E) atomicAdd(&cnt[my_e[i]], 1);
+  for (int r = tid + 4 * 1024; r < R; r += blockDim.x) {
     const int e = __ldcg(row_expert + r);
     if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
   }
   __syncthreads();
-  if (tid == 0) {
-    int acc = 0, it = 0;
-    for (int e = 0; e < E; ++e) {
-      off[e] = acc;
-      items[e] = it;
-      acc += cnt[e];
-      it += (cnt[e] + tpi - 1) / tpi;
+  // Exclusive scans of the counts and of the items per expert (E <= 256):
+  // one warp, 8 experts per lane.
+  if (tid < 32) {
+    int c[8], n[8], sc = 0, sn = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int e = tid * 8 + j;
+      c[j] = e < E ? cnt[e] : 0;
+      n[j] = (c[j] + tpi - 1) / tpi;
+      sc += c[j];
+      sn += n[j];
     }
-    off[E] = acc;
-    items[E] = it;
-    *plan.n_work = it;
-    *plan.n_rows = acc;
+    int ic = sc, in = sn;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int uc = __shfl_up_sync(0xffffffffu, ic, o), un = __shfl_up_sync(0xffffffffu, in, o);
+      if (tid >= o) {
+        ic += uc;
+        in += un;
+      }
+    }
+    int ac = ic - sc, an = in - sn;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int e = tid * 8 + j;
+      if (e < E) {
+        off[e] = ac;
+        items[e] = an;
+      }
+      ac += c[j];
+      an += n[j];
+    }
+    if (tid == 31) {
+      off[E] = ic;
+      items[E] = in;
+      *plan.n_work = in;
+      *plan.n_rows = ic;
+    }
   }
   __syncthreads();
   for (int e = tid; e <= E; e += blockDim.x) plan.offsets[e] = off[e];
@@ -416,7 +460,8 @@ __global__ void __launch_bounds__(1024) moe_permute_kernel(const int32_t *__rest
   }
   __syncthreads();
   for (int r = tid; r < R; r += blockDim.x) {
-    const int e = __ldcg(row_expert + r);
+    const int i = (r - tid) / 1024;
+    const int e = i < 4 ? my_e[i] : __ldcg(row_expert + r);
     if (e >= 0 && e < E) {
       const int p = atomicAdd(&cur[e], 1);
       plan.src_row[p] = x_row_index ? __ldcg(x_row_index + r) : r;
@@ -433,6 +478,7 @@ __global__ void __launch_bounds__(1024) moe_permute_kernel(const int32_t *__rest
 
 cudaError_t launch_moe_permute(const int32_t *row_expert, const int32_t *x_row_index, int R,
                                int E, int tpi, const MoePlan &plan, cudaStream_t st) {
+  if (E <= 0 || E > 256) return cudaErrorInvalidValue;  // the one-warp scan covers 256 experts
   return launch_pdl(moe_permute_kernel, dim3(1), dim3(1024), 0, st, row_expert, x_row_index, R, E,
                     tpi, plan);
 }
@@ -658,14 +704,28 @@ __global__ void moe_combine_kernel(const SlotT *__restrict__ ys, const float *__
   float s[8];
 #pragma unroll
   for (int q = 0; q < 8; ++q) s[q] = 0.0f;
-  for (int j = 0; j < k; ++j) {
-    const float wj = __ldcg(w + (int64_t)t * k + j);
-    const int64_t row = slot_pos ? __ldcg(slot_pos + (int64_t)t * k + j) : (int64_t)t * k + j;
-    if (row < 0) continue;  // slot that was not dispatched contributes nothing
-    float v[8];
-    load8<SlotT>(ys + row * H + 8 * h8, v);
+  // Slots in groups of 8: the group's loads first, then the sums in slot order.
+  for (int j0 = 0; j0 < k; j0 += 8) {
+    float wv[8], v[8][8];
+    int64_t rows[8];
 #pragma unroll
-    for (int q = 0; q < 8; ++q) s[q] = fmaf(wj, v[q], s[q]);
+    for (int jj = 0; jj < 8; ++jj) {
+      const int j = j0 + jj;
+      rows[jj] = -1;
+      if (j < k) {
+        wv[jj] = __ldcg(w + (int64_t)t * k + j);
+        rows[jj] = slot_pos ? __ldcg(slot_pos + (int64_t)t * k + j) : (int64_t)t * k + j;
+      }
+    }
+#pragma unroll
+    for (int jj = 0; jj < 8; ++jj)
+      if (rows[jj] >= 0) load8<SlotT>(ys + rows[jj] * H + 8 * h8, v[jj]);
+#pragma unroll
+    for (int jj = 0; jj < 8; ++jj) {
+      if (rows[jj] < 0) continue;  // slot that was not dispatched contributes nothing
+#pragma unroll
+      for (int q = 0; q < 8; ++q) s[q] = fmaf(wv[jj], v[jj][q], s[q]);
+    }
   }
   if (extra) {  // fp32 rows added after the routed sum (the shared expert)
     float e[8];

@@ -1,5 +1,6 @@
 // moe_abi.cu -- extern "C" MoE entry points (include/nvfp4.h): validation,
 // workspace layout and the launch sequence of one MoE layer.
+#include <algorithm>
 #include "../../include/nvfp4.h"
 #include "abi_util.h"
 #include "kernels.h"
@@ -53,7 +54,11 @@ int choose_tpi(const nvfp4_moe_desc &d, int64_t R) {
   return gemv_shape_ok(d, R) ? 8 : path_tpi(d, R, ExpertPath::kSkinny);
 }
 
-int64_t work_capacity(int64_t R, int E, int tpi) { return (R + tpi - 1) / tpi + E; }
+// Upper bound of the permutation's work items: every expert with slots adds
+// at most one partial item, and at most min(E, R) experts have slots.
+int64_t work_capacity(int64_t R, int E, int tpi) {
+  return (R + tpi - 1) / tpi + std::min<int64_t>(E, R);
+}
 
 struct ExpertsLayout {
   size_t offsets, n_work, n_rows, work, src_row, dst_row, inter, inter_lo, x_perm, total;
