@@ -458,7 +458,7 @@ class MoELayerBench:
     unit = "tokens/s"
 
     @staticmethod
-    def describe(tokens, layers=None, world=1):
+    def describe(tokens, layers=None, world=1, exchange=None):
         return (f"one MoE FFN layer, 128 experts, top-8 (softmax, renormalised), hidden "
                 f"2048, expert intermediate 768, NVFP4 gate_up [1536, 2048] and down "
                 f"[2048, 768] per expert; T = {tokens} bf16 tokens ~N(0,1)")
@@ -546,7 +546,7 @@ class DeltaNetBench:
     unit = "tokens/s"
 
     @staticmethod
-    def describe(tokens, layers=None, world=1):
+    def describe(tokens, layers=None, world=1, exchange=None):
         return (f"one gated DeltaNet decode step of the reference's default layer (d_model "
                 f"2048, 16 key / 32 value heads of 128 x 128, conv kernel 4) with NVFP4 "
                 f"projections qkv [8192, 2048], z [4096, 2048], beta / alpha [32, 2048], out "
@@ -664,14 +664,17 @@ class EPStackBench:
     scaling = "strong"  # the global token batch is fixed; experts and tokens split over GPUs
 
     @staticmethod
-    def describe(tokens, layers=48, world=1):
+    def describe(tokens, layers=48, world=1, exchange="nccl"):
+        how = ("NCCL all-to-all dispatch/combine" if exchange == "nccl" else
+               "device-initiated dispatch/combine through peer memory (NVLink stores and loads "
+               "issued by the kernels, cross-GPU flags)")
         return (f"{layers}-layer stack of pre-norm MoE blocks h += MoE(RMSNorm(h)) (128 "
                 f"experts, top-8, hidden 2048, intermediate 768, NVFP4 experts; the "
                 f"residual add is fused in the combine); expert-parallel over {world} GPU(s) "
-                f"({MOE_E // world} experts each) with NCCL all-to-all dispatch/combine; "
+                f"({MOE_E // world} experts each) with {how}; "
                 f"{tokens} bf16 tokens ~N(0,1) per step ({tokens // world} per GPU)")
 
-    def __init__(self, device, seed=0, tokens=64, layers=48):
+    def __init__(self, device, seed=0, tokens=64, layers=48, exchange="nccl"):
         import torch
         import torch.distributed as dist
         from nvfp4.ep import EPMoELayer
@@ -685,7 +688,7 @@ class EPStackBench:
         self.T = tokens
         self.T_local = tokens // world
         epr = MOE_E // world
-        self.workload = self.describe(tokens, layers, world)
+        self.workload = self.describe(tokens, layers, world, exchange)
         self.layers = []
         for l in range(layers):
             g = torch.Generator(device=device)
@@ -694,14 +697,22 @@ class EPStackBench:
             wd = synthetic_local_experts(epr, seed=seed + 7919 * l + 104729 * rank, device=device)
             wd["router"] = router
             local = MoEWeights.from_dict(wd, device)
-            self.layers.append(EPMoELayer(local, router, top_k=MOE_K, num_experts=MOE_E))
+            self.layers.append(EPMoELayer(local, router, top_k=MOE_K, num_experts=MOE_E,
+                                          exchange=exchange, max_tokens=self.T_local,
+                                          timeout_ms=10000))
         self.x = torch.randn((self.T_local, MOE_H), device=device).to(torch.bfloat16)
         # Fixed-capacity exchange (no host-side counts) for small batches: the
         # whole step, NCCL calls included, is then replayed from a CUDA graph.
-        self.graphable = self.layers[0].uses_static(self.T_local)
-        self.exchange = "fixed capacity, CUDA graph" if self.graphable else "variable counts"
+        if exchange == "p2p":
+            # router (2), dispatch, wait, permutation, 2 expert GEMVs, done signal, combine
+            self.graphable = True
+            self.exchange = "peer memory, CUDA graph"
+            self.launches_per_step = layers * 9
+        else:
+            self.graphable = self.layers[0].uses_static(self.T_local)
+            self.exchange = "fixed capacity, CUDA graph" if self.graphable else "variable counts"
+            self.launches_per_step = layers * 10
         self.sets = 1
-        self.launches_per_step = layers * 10
         self.dominant_bytes = None
         self.config = {"workload": self.workload, "layers": layers, "global_tokens": tokens,
                        "experts_per_gpu": epr, "parallelism": f"ep{world}",
@@ -833,7 +844,7 @@ def run_reference(args, world, rank):
     el = time.perf_counter() - t0
     value = units * args.steps / el
     if hasattr(wl_cls, "describe"):
-        wdesc = wl_cls.describe(args.tokens, args.layers, world)
+        wdesc = wl_cls.describe(args.tokens, args.layers, world, args.exchange)
     else:
         wdesc = wl_cls.workload
     line = {
@@ -864,6 +875,8 @@ def main():
                     help="MoE: tokens per step (default 4096); EP stack: global tokens (default "
                          "64); DeltaNet: sequences per step (default 4)")
     ap.add_argument("--layers", type=int, default=48, help="EP stack: number of MoE layers")
+    ap.add_argument("--exchange", default="nccl", choices=["nccl", "p2p"],
+                    help="EP stack: NCCL all-to-all or device-initiated peer-memory exchange")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.tokens is None:
@@ -883,6 +896,7 @@ def main():
     kw = {"tokens": args.tokens} if args.workload in ("moe", "ep", "deltanet") else {}
     if args.workload == "ep":
         kw["layers"] = args.layers
+        kw["exchange"] = args.exchange
     wl = WORKLOADS[args.workload](device, seed=17 * rank, **kw)
     stream = torch.cuda.Stream(device)
 

@@ -2,6 +2,7 @@
 // workspace layout and the launch sequence of one MoE layer.
 #include <algorithm>
 #include "../../include/nvfp4.h"
+#include "../../include/nvfp4_ep.h"
 #include "abi_util.h"
 #include "kernels.h"
 #include "moe.h"
@@ -578,4 +579,104 @@ extern "C" int nvfp4_stack_rows(const void *const *srcs, const int64_t *rows, in
     o += bytes;
   }
   return NVFP4_OK;
+}
+namespace nvfp4 {
+namespace {
+
+// Workspace of the expert-parallel step through peer memory: the routing of
+// this rank's T tokens and the expert workspace for the world*T*k received rows.
+struct EpP2pLayout {
+  size_t ids, w, part, experts, total;
+};
+
+nvfp4_moe_desc ep_local_desc(const nvfp4_moe_desc &d, int world) {
+  nvfp4_moe_desc l = d;
+  l.num_experts = d.num_experts / world;
+  l.top_k = 1;  // the expert pass takes one expert id per row
+  return l;
+}
+
+EpP2pLayout ep_p2p_layout(const nvfp4_moe_desc &d, int world, int64_t T) {
+  EpP2pLayout L;
+  const int64_t R = T * d.top_k;
+  size_t o = 0;
+  L.ids = o;
+  o = up(o + sizeof(int32_t) * R);
+  L.w = o;
+  o = up(o + sizeof(float) * R);
+  L.part = o;
+  o = up(o + sizeof(float) * T * d.num_experts * router_slices((int)T, d.hidden, d.num_experts));
+  L.experts = o;
+  o = up(o + experts_layout(ep_local_desc(d, world), (int64_t)world * R).total);
+  L.total = o;
+  return L;
+}
+
+int check_ep_desc(const nvfp4_moe_desc *d, const nvfp4_ep_peers *p) {
+  int rc = check_desc(d);
+  if (rc) return rc;
+  if (!p || p->world < 1 || p->world > NVFP4_EP_MAX_WORLD)
+    return fail(NVFP4_ERR_INVALID_ARG, "null peer table or bad world size");
+  if (d->num_experts % p->world)
+    return fail(NVFP4_ERR_INVALID_ARG, "num_experts %d not divisible by world %d", d->num_experts,
+                p->world);
+  if (p->hidden != d->hidden)
+    return fail(NVFP4_ERR_INVALID_ARG, "peer windows sized for hidden %d, layer has %d",
+                p->hidden, d->hidden);
+  return NVFP4_OK;
+}
+
+}  // namespace
+}  // namespace nvfp4
+
+extern "C" size_t nvfp4_ep_p2p_workspace_size(const nvfp4_moe_desc *d, const nvfp4_ep_peers *p,
+                                              int64_t T) {
+  if (check_ep_desc(d, p) || T < 0) return 0;
+  return ep_p2p_layout(*d, p->world, T).total;
+}
+
+extern "C" int nvfp4_ep_p2p_forward(const nvfp4_moe_desc *d, const nvfp4_moe_weights *local,
+                                    const nvfp4_ep_peers *p, const void *x, const void *residual,
+                                    void *y, int y_dtype, int64_t T, void *ws, size_t ws_bytes,
+                                    void *stream) {
+  int rc = check_ep_desc(d, p);
+  if (rc) return rc;
+  if ((rc = check_weights(local))) return rc;
+  if (!local->router) return fail(NVFP4_ERR_INVALID_ARG, "null router pointer");
+  if (T < 0 || T * d->top_k > p->max_rows)
+    return fail(NVFP4_ERR_INVALID_ARG, "bad token count for the windows' capacity");
+  if ((T > 0 && (!x || !y)) || !ws)
+    return fail(NVFP4_ERR_INVALID_ARG, "null activation, output or workspace");
+  if (!aligned(x, 16) || !aligned(y, 16) || (residual && !aligned(residual, 16)) ||
+      !aligned(ws, kAlign))
+    return fail(NVFP4_ERR_INVALID_ARG, "x/y/residual must be 16-byte and workspace 256-byte aligned");
+  const EpP2pLayout L = ep_p2p_layout(*d, p->world, T);
+  if (ws_bytes < L.total)
+    return fail(NVFP4_ERR_WORKSPACE, "workspace of %zu bytes, %zu needed", ws_bytes, L.total);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t *base = static_cast<uint8_t *>(ws);
+  int32_t *ids = reinterpret_cast<int32_t *>(base + L.ids);
+  float *tw = reinterpret_cast<float *>(base + L.w);
+  const int epr = d->num_experts / p->world, k = d->top_k;
+  // Every rank takes every step, also with no tokens: the peers wait on its flags.
+  if (T > 0) {
+    rc = check_launch(launch_router(static_cast<const uint16_t *>(x), local->router,
+                                    reinterpret_cast<float *>(base + L.part),
+                                    router_slices((int)T, d->hidden, d->num_experts), nullptr,
+                                    (int)T, d->hidden, d->num_experts, k, d->renormalize, ids, tw,
+                                    st),
+                      "router launch");
+    if (rc) return rc;
+  }
+  if ((rc = nvfp4_ep_p2p_dispatch(p, ids, x, T, k, epr, stream))) return rc;
+  if ((rc = nvfp4_ep_p2p_wait_dispatch(p, stream))) return rc;
+  void *recv_x = nullptr;
+  int32_t *recv_e = nullptr;
+  float *out = nullptr;
+  if ((rc = nvfp4_ep_p2p_rows(p, T, k, &recv_x, &recv_e, &out))) return rc;
+  rc = run_experts(ep_local_desc(*d, p->world), *local, static_cast<const uint16_t *>(recv_x),
+                   nullptr, recv_e, (int64_t)p->world * T * k, out, kF32, base + L.experts, st);
+  if (rc) return rc;
+  if ((rc = nvfp4_ep_p2p_signal_done(p, stream))) return rc;
+  return nvfp4_ep_p2p_combine(p, ids, tw, T, k, epr, residual, y, y_dtype, stream);
 }

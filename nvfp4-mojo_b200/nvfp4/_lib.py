@@ -129,6 +129,20 @@ class DeltaNetStatePtrs(ctypes.Structure):
     _fields_ = [("s", ctypes.c_void_p), ("conv_q", ctypes.c_void_p),
                 ("conv_k", ctypes.c_void_p), ("conv_v", ctypes.c_void_p)]
 
+EP_MAX_WORLD = 8
+EP_HANDLE_BYTES = 64
+EP_ERR_DISPATCH_TIMEOUT = 0x1
+EP_ERR_DONE_TIMEOUT = 0x2
+
+
+class EpPeers(ctypes.Structure):
+    """struct nvfp4_ep_peers (include/nvfp4_ep.h)."""
+
+    _fields_ = [("rank", ctypes.c_int32), ("world", ctypes.c_int32),
+                ("max_rows", ctypes.c_int64), ("hidden", ctypes.c_int32),
+                ("timeout_ms", ctypes.c_int32), ("windows", ctypes.c_void_p * EP_MAX_WORLD)]
+
+
 _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
 _int = ctypes.c_int
@@ -168,6 +182,27 @@ SIGNATURES = {
     "nvfp4_gather_rows": (_int, [_vp, _vp, _i64, _i64, _vp, _vp]),
     "nvfp4_ep_dispatch_padded": (_int, [_vp, _vp, _vp, _vp, _i64, ctypes.c_int32, ctypes.c_int32,
                                         _i64, _vp, _i64, _vp, _vp, _vp, _vp]),
+    # include/nvfp4_ep.h
+    "nvfp4_ep_window_size": (ctypes.c_size_t, [ctypes.c_int32, _i64, ctypes.c_int32]),
+    "nvfp4_ep_window_create": (_int, [ctypes.c_size_t, ctypes.POINTER(_vp), _vp]),
+    "nvfp4_ep_window_open": (_int, [_vp, ctypes.POINTER(_vp)]),
+    "nvfp4_ep_window_close": (_int, [_vp]),
+    "nvfp4_ep_window_destroy": (_int, [_vp]),
+    "nvfp4_ep_p2p_rows": (_int, [ctypes.POINTER(EpPeers), _i64, ctypes.c_int32,
+                                 ctypes.POINTER(_vp), ctypes.POINTER(_vp), ctypes.POINTER(_vp)]),
+    "nvfp4_ep_p2p_dispatch": (_int, [ctypes.POINTER(EpPeers), _vp, _vp, _i64, ctypes.c_int32,
+                                     ctypes.c_int32, _vp]),
+    "nvfp4_ep_p2p_wait_dispatch": (_int, [ctypes.POINTER(EpPeers), _vp]),
+    "nvfp4_ep_p2p_signal_done": (_int, [ctypes.POINTER(EpPeers), _vp]),
+    "nvfp4_ep_p2p_combine": (_int, [ctypes.POINTER(EpPeers), _vp, _vp, _i64, ctypes.c_int32,
+                                    ctypes.c_int32, _vp, _vp, _int, _vp]),
+    "nvfp4_ep_p2p_error": (_int, [ctypes.POINTER(EpPeers), ctypes.POINTER(_u32), ctypes.c_int32,
+                                  _vp]),
+    "nvfp4_ep_p2p_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(MoEDesc),
+                                                      ctypes.POINTER(EpPeers), _i64]),
+    "nvfp4_ep_p2p_forward": (_int, [ctypes.POINTER(MoEDesc), ctypes.POINTER(MoEWeightPtrs),
+                                    ctypes.POINTER(EpPeers), _vp, _vp, _vp, _int, _i64, _vp,
+                                    ctypes.c_size_t, _vp]),
     # include/nvfp4_deltanet.h
     "nvfp4_deltanet_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(DeltaNetDesc), _i64]),
     "nvfp4_deltanet_forward": (_int, [ctypes.POINTER(DeltaNetDesc),

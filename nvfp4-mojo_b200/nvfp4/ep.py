@@ -14,13 +14,20 @@ fp32 router.  Per layer, on every rank:
   7. combine them in slot order with the routing weights (+ residual).
 
 Steps 1, 2, 4 (gather), 5 and 7 are libnvfp4 CUDA kernels; steps 3, 4 and 6
-are NCCL collectives.  For small batches the exchange uses fixed capacities
+are NCCL collectives.  With exchange="p2p" the kernels move the rows
+themselves: the dispatch kernel stores each routed row straight into the
+owning rank's window (peer memory over NVLink / NVSwitch) and the combine
+kernel loads the expert outputs back from the peers' windows, ordered by
+cross-GPU flags with bounded waits (include/nvfp4_ep.h) -- no NCCL call and
+no host synchronisation in the step.  For small batches the exchange uses fixed capacities
 instead (EPMoELayer.forward_static): no step 3, no host synchronisation.  The kernel calls go through a backend object so the
 exchange logic can be exercised with CPU ranks (gloo) in tests.
 """
 from __future__ import annotations
 
 from typing import Optional
+
+import ctypes
 
 import torch
 import torch.distributed as dist
@@ -99,6 +106,149 @@ class CudaBackend:
         return moe_combine(y_send, tw, residual=residual, slot_pos=slot_pos)
 
 
+def exchange_handles(handle: bytes, group=None) -> list:
+    """All-gathers one fixed-size byte string per rank (the windows' IPC
+    handles): element p of the result is rank p's."""
+    world = dist.get_world_size(group)
+    dev = torch.device("cuda", torch.cuda.current_device()) \
+        if dist.get_backend(group) == "nccl" else torch.device("cpu")
+    mine = torch.tensor(list(handle), dtype=torch.uint8, device=dev)
+    every = torch.empty(world * len(handle), dtype=torch.uint8, device=dev)
+    dist.all_gather_into_tensor(every, mine, group=group)
+    raw = every.cpu().numpy().tobytes()
+    return [raw[p * len(handle):(p + 1) * len(handle)] for p in range(world)]
+
+
+class PeerWindows:
+    """This rank's exchange window and the other ranks' windows as mapped in
+    this process (nvfp4_ep_window_create / _open).  `rendezvous` builds them
+    across the processes of a group (IPC handles all-gathered once);
+    `emulated` builds the windows of `world` ranks in one process on one
+    device, for running the ranks' steps one after another in one stream."""
+
+    def __init__(self, rank, world, max_rows, hidden, windows, owned, opened, timeout_ms=0):
+        self.rank, self.world = rank, world
+        self.max_rows, self.hidden = max_rows, hidden
+        self.windows = list(windows)
+        self._owned = list(owned)    # windows this object frees
+        self._opened = list(opened)  # peer mappings this object closes
+        self.timeout_ms = timeout_ms
+
+    @staticmethod
+    def _create(world, max_rows, hidden):
+        L = _lib.load()
+        size = L.nvfp4_ep_window_size(world, max_rows, hidden)
+        if size == 0:
+            raise ValueError(f"bad window shape: world {world}, max_rows {max_rows}, "
+                             f"hidden {hidden}")
+        win = ctypes.c_void_p()
+        handle = (ctypes.c_uint8 * _lib.EP_HANDLE_BYTES)()
+        _lib.check(L.nvfp4_ep_window_create(size, ctypes.byref(win), handle))
+        return win.value, bytes(handle)
+
+    @classmethod
+    def rendezvous(cls, max_rows: int, hidden: int, group=None, timeout_ms: int = 0):
+        world = dist.get_world_size(group) if dist.is_initialized() else 1
+        rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if world > _lib.EP_MAX_WORLD:
+            raise ValueError(f"peer exchange supports up to {_lib.EP_MAX_WORLD} ranks")
+        own, handle = cls._create(world, max_rows, hidden)
+        windows, opened = [None] * world, []
+        windows[rank] = own
+        if world > 1:
+            every = exchange_handles(handle, group)
+            L = _lib.load()
+            for p in range(world):
+                if p == rank:
+                    continue
+                h = (ctypes.c_uint8 * _lib.EP_HANDLE_BYTES).from_buffer_copy(every[p])
+                w = ctypes.c_void_p()
+                _lib.check(L.nvfp4_ep_window_open(h, ctypes.byref(w)))
+                windows[p] = w.value
+                opened.append(w.value)
+            dist.barrier(group)  # every window zeroed and mapped before any step
+        return cls(rank, world, max_rows, hidden, windows, [own], opened, timeout_ms)
+
+    @classmethod
+    def emulated(cls, world: int, max_rows: int, hidden: int, timeout_ms: int = 0):
+        wins = [cls._create(world, max_rows, hidden)[0] for _ in range(world)]
+        return [cls(r, world, max_rows, hidden, wins, wins if r == 0 else [], [], timeout_ms)
+                for r in range(world)]
+
+    def peers(self) -> _lib.EpPeers:
+        p = _lib.EpPeers()
+        p.rank, p.world, p.max_rows = self.rank, self.world, self.max_rows
+        p.hidden, p.timeout_ms = self.hidden, self.timeout_ms
+        for i, w in enumerate(self.windows):
+            p.windows[i] = w
+        return p
+
+    def rows(self, T: int, k: int):
+        """Device pointers of this rank's received rows, expert ids and
+        expert output rows for a step of T tokens."""
+        x, e, o = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_void_p()
+        _lib.check(_lib.load().nvfp4_ep_p2p_rows(ctypes.byref(self.peers()), T, k,
+                                                 ctypes.byref(x), ctypes.byref(e),
+                                                 ctypes.byref(o)))
+        return x.value, e.value, o.value
+
+    def error(self, clear: bool = True, stream=None) -> int:
+        v = ctypes.c_uint32()
+        _lib.check(_lib.load().nvfp4_ep_p2p_error(ctypes.byref(self.peers()), ctypes.byref(v),
+                                                  int(clear), _stream(stream)))
+        return v.value
+
+    def close(self):
+        L = _lib.load()
+        for w in self._opened:
+            L.nvfp4_ep_window_close(w)
+        for w in self._owned:
+            L.nvfp4_ep_window_destroy(w)
+        self._opened, self._owned = [], []
+
+
+def p2p_dispatch(pw: PeerWindows, topk_ids, x, experts_per_rank: int, stream=None):
+    T, k = topk_ids.shape
+    _lib.check(_lib.load().nvfp4_ep_p2p_dispatch(ctypes.byref(pw.peers()), _ptr(topk_ids),
+                                                 _ptr(x), T, k, experts_per_rank,
+                                                 _stream(stream)))
+
+
+def p2p_wait_dispatch(pw: PeerWindows, stream=None):
+    _lib.check(_lib.load().nvfp4_ep_p2p_wait_dispatch(ctypes.byref(pw.peers()), _stream(stream)))
+
+
+def p2p_experts(pw: PeerWindows, local: MoEWeights, T: int, k: int, workspace=None,
+                stream=None):
+    """The local experts on the world*T*k received rows, into the window."""
+    rx, re, out = pw.rows(T, k)
+    R = pw.world * T * k
+    desc = make_desc(local, 1)
+    L = _lib.load()
+    need = L.nvfp4_moe_experts_workspace_size(ctypes.byref(desc), R)
+    ws = workspace if workspace is not None and workspace.numel() >= need else \
+        torch.empty(max(need, 256), dtype=torch.uint8, device=local.gate_up.device)
+    _lib.check(L.nvfp4_moe_experts(ctypes.byref(desc), ctypes.byref(local.ptrs()), rx, None, re,
+                                   R, out, _lib.DTYPE_F32, _ptr(ws), ws.numel(),
+                                   _stream(stream)))
+
+
+def p2p_signal_done(pw: PeerWindows, stream=None):
+    _lib.check(_lib.load().nvfp4_ep_p2p_signal_done(ctypes.byref(pw.peers()), _stream(stream)))
+
+
+def p2p_combine(pw: PeerWindows, topk_ids, topk_w, experts_per_rank: int, residual=None,
+                out=None, stream=None):
+    T, k = topk_ids.shape
+    y = out if out is not None else torch.empty((T, pw.hidden), dtype=torch.bfloat16,
+                                                device=topk_ids.device)
+    ydt = {torch.float32: _lib.DTYPE_F32, torch.bfloat16: _lib.DTYPE_BF16}[y.dtype]
+    _lib.check(_lib.load().nvfp4_ep_p2p_combine(ctypes.byref(pw.peers()), _ptr(topk_ids),
+                                                _ptr(topk_w), T, k, experts_per_rank,
+                                                _ptr(residual), _ptr(y), ydt, _stream(stream)))
+    return y
+
+
 class EPMoELayer:
     """Expert-parallel MoE layer; `backend` defaults to the CUDA kernels.
 
@@ -114,7 +264,8 @@ class EPMoELayer:
     def __init__(self, local: Optional[MoEWeights], router: torch.Tensor, top_k: int = 8,
                  num_experts: Optional[int] = None, group=None, backend=None,
                  renormalize: bool = True, static: Optional[bool] = None,
-                 static_rows: int = 8192):
+                 static_rows: int = 8192, exchange: str = "nccl",
+                 max_tokens: Optional[int] = None, timeout_ms: int = 0):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.E = num_experts if num_experts is not None else router.shape[1]
@@ -125,6 +276,19 @@ class EPMoELayer:
         self.backend = backend or CudaBackend(local, router, top_k, renormalize)
         self.static = static
         self.static_rows = static_rows
+        if exchange not in ("nccl", "p2p"):
+            raise ValueError("exchange must be 'nccl' or 'p2p'")
+        self.exchange = exchange
+        self.windows = None
+        self.renormalize = renormalize
+        self._ws = {}
+        if exchange == "p2p":
+            if max_tokens is None:
+                raise ValueError("the peer exchange needs max_tokens (rows per rank are "
+                                 "max_tokens * top_k)")
+            self.max_tokens = max_tokens
+            self.windows = PeerWindows.rendezvous(max_tokens * top_k, router.shape[0], group,
+                                                  timeout_ms)
 
     def uses_static(self, T: int) -> bool:
         if self.static is not None:
@@ -155,7 +319,39 @@ class EPMoELayer:
         self._a2a(y_send, y_recv, None, None)
         return be.combine(y_send, tw, slot_pad, residual)
 
+    def forward_p2p(self, x: torch.Tensor, residual: Optional[torch.Tensor] = None,
+                    out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """One step through peer memory (nvfp4_ep_p2p_forward): every rank
+        calls it with the same token count."""
+        T = x.shape[0]
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens exceed the windows' {self.max_tokens}")
+        be = self.backend
+        w = be.router_w
+        desc = _lib.MoEDesc(self.E, self.top_k, w.hidden, w.intermediate, int(self.renormalize))
+        peers = self.windows.peers()
+        L = _lib.load()
+        ws = self._ws.get(T)
+        if ws is None:
+            need = L.nvfp4_ep_p2p_workspace_size(ctypes.byref(desc), ctypes.byref(peers), T)
+            if need == 0:
+                raise ValueError("bad expert-parallel layer shape")
+            ws = self._ws[T] = torch.empty(need, dtype=torch.uint8, device=x.device)
+        y = out if out is not None else torch.empty_like(x)
+        ydt = {torch.float32: _lib.DTYPE_F32, torch.bfloat16: _lib.DTYPE_BF16}[y.dtype]
+        _lib.check(L.nvfp4_ep_p2p_forward(ctypes.byref(desc), ctypes.byref(w.ptrs()),
+                                          ctypes.byref(peers), _ptr(x), _ptr(residual), _ptr(y),
+                                          ydt, T, _ptr(ws), ws.numel(), _stream(None)))
+        return y
+
+    def close(self):
+        if self.windows is not None:
+            self.windows.close()
+            self.windows = None
+
     def forward(self, x: torch.Tensor, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if self.exchange == "p2p":
+            return self.forward_p2p(x, residual)
         if self.uses_static(x.shape[0]):
             return self.forward_static(x, residual)
         be = self.backend

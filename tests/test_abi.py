@@ -84,6 +84,60 @@ def test_shared_expert_and_stack_validation_without_gpu():
     assert L.nvfp4_stack_rows(srcs, rows, 1, 0, 16, None) == _lib.NVFP4_ERR_INVALID_ARG
 
 
+def test_peer_exchange_validation_without_gpu():
+    """include/nvfp4_ep.h host side: window sizes and layout, and the checks
+    that refuse a bad peer table before any CUDA work."""
+    from nvfp4 import _lib
+
+    L = _lib.load()
+    H, k = 2048, 8
+    up = lambda v: (v + 255) // 256 * 256
+    for world, rows in ((1, 8), (2, 64), (8, 512)):
+        n = world * rows
+        want = up(up(256 + 4 * n) + 2 * n * H) + 4 * n * H
+        assert L.nvfp4_ep_window_size(world, rows, H) == want
+    assert L.nvfp4_ep_window_size(9, 8, H) == 0
+    assert L.nvfp4_ep_window_size(2, 8, 1000) == 0
+    assert L.nvfp4_ep_window_size(2, 0, H) == 0
+
+    def peers(rank=1, world=2, rows=64, wins=(1 << 20, 1 << 30)):
+        p = _lib.EpPeers()
+        p.rank, p.world, p.max_rows, p.hidden, p.timeout_ms = rank, world, rows, H, 0
+        for i, w in enumerate(wins):
+            p.windows[i] = w
+        return p
+
+    x, e, o = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_void_p()
+    p = peers()
+    assert L.nvfp4_ep_p2p_rows(ctypes.byref(p), 8, k, ctypes.byref(x), ctypes.byref(e),
+                               ctypes.byref(o)) == 0
+    base = 1 << 30  # rank 1's own window
+    assert e.value == base + 256
+    assert x.value == base + up(256 + 4 * 128)
+    assert o.value == x.value + up(2 * 128 * H)
+    # 9 tokens x 8 slots exceed the 64 rows per rank.
+    assert L.nvfp4_ep_p2p_dispatch(ctypes.byref(p), 16, 16, 9, k, 16, None) == \
+        _lib.NVFP4_ERR_INVALID_ARG
+    assert b"exceed" in L.nvfp4_last_error_string()
+    for bad in (peers(rank=2), peers(world=9), peers(wins=(1 << 20, 0)),
+                peers(wins=(1 << 20, (1 << 30) + 16))):
+        assert L.nvfp4_ep_p2p_dispatch(ctypes.byref(bad), 16, 16, 1, k, 16, None) == \
+            _lib.NVFP4_ERR_INVALID_ARG
+        assert L.nvfp4_ep_p2p_wait_dispatch(ctypes.byref(bad), None) == _lib.NVFP4_ERR_INVALID_ARG
+    assert L.nvfp4_ep_p2p_combine(ctypes.byref(p), 16, 16, 1, k, 16, None, 16, 7, None) == \
+        _lib.NVFP4_ERR_INVALID_ARG  # output dtype
+    desc = _lib.MoEDesc(128, k, H, 768, 1)
+    assert L.nvfp4_ep_p2p_workspace_size(ctypes.byref(desc), ctypes.byref(p), 8) > 0
+    assert L.nvfp4_ep_p2p_workspace_size(ctypes.byref(_lib.MoEDesc(127, k, H, 768, 1)),
+                                         ctypes.byref(p), 8) == 0  # E % world
+    assert L.nvfp4_ep_p2p_workspace_size(ctypes.byref(_lib.MoEDesc(128, k, 1024, 768, 1)),
+                                         ctypes.byref(p), 8) == 0  # hidden mismatch
+    w = _lib.MoEWeightPtrs(16, 16, 16, None, None, 16, 16, None, None)
+    rc = L.nvfp4_ep_p2p_forward(ctypes.byref(desc), ctypes.byref(w), ctypes.byref(p), 16, None,
+                                16, 1, 8, 256, 1024, None)
+    assert rc == _lib.NVFP4_ERR_WORKSPACE
+
+
 def test_python_api_refuses_host_tensors():
     import torch
     import nvfp4

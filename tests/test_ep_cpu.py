@@ -136,3 +136,86 @@ def test_ep_exchange_matches_single_process_oracle(O, static):
     ref, _, _ = O.moe(x_all, wd, top_k=K_TOP)
     got = np.concatenate([np.array(ret[r], np.float32) for r in range(world)])
     np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-6)
+
+
+def _handles_worker(rank, world, port, ret):
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parents[1]
+    sys.path.insert(0, str(root / "nvfp4-mojo_b200"))
+    import torch.distributed as dist
+    from nvfp4.ep import exchange_handles
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        mine = bytes((rank * 37 + i) % 256 for i in range(64))
+        ret[rank] = [list(h) for h in exchange_handles(mine)]
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_window_handle_exchange():
+    """exchange_handles: every rank gets every rank's 64-byte IPC handle, in
+    rank order (gloo ranks stand in for the GPUs' processes)."""
+    world = 3
+    mgr = mp.Manager()
+    ret = mgr.dict()
+    mp.spawn(_handles_worker, args=(world, _port(), ret), nprocs=world, join=True)
+    want = [[(p * 37 + i) % 256 for i in range(64)] for p in range(world)]
+    for r in range(world):
+        assert ret[r] == want
+
+
+def peer_step_model(O, wd, xs, world, k):
+    """The peer-exchange step (include/nvfp4_ep.h) with numpy arrays for the
+    windows: each rank's dispatch stores row x[t] and the local expert id at
+    row rank*T*k + s of the owner's window (id -1 in the others), each owner
+    runs its experts on its world*T*k rows, each rank combines its slots from
+    the owners' output rows in j order."""
+    T = xs[0].shape[0]
+    R, epr = T * k, E // world
+    recv_x = [np.zeros((world * R, H), np.float32) for _ in range(world)]
+    recv_e = [np.full(world * R, -1, np.int64) for _ in range(world)]
+    routes = []
+    for r in range(world):
+        _, ids, tw = O.moe(xs[r], wd, top_k=k)
+        routes.append((ids, tw))
+        for s, e in enumerate(ids.reshape(-1)):
+            d = int(e) // epr
+            recv_x[d][r * R + s] = xs[r][s // k]
+            recv_e[d][r * R + s] = int(e) % epr
+    out = [np.zeros((world * R, H), np.float32) for _ in range(world)]
+    for d in range(world):
+        for row in range(world * R):
+            le = recv_e[d][row]
+            if le < 0:
+                continue
+            e = d * epr + le
+            h = O.matvec(wd["gu_w"][e], wd["gu_sf"][e], recv_x[d][row], ws2_rows=wd["gu_ws2"][e])
+            a = np.array([O.silu(float(v)) for v in h[:I]], np.float32) * h[I:]
+            out[d][row] = O.matvec(wd["dn_w"][e], wd["dn_sf"][e], a, ws2_rows=wd["dn_ws2"][e])
+    ys = []
+    for r in range(world):
+        ids, tw = routes[r]
+        y = np.zeros((T, H), np.float32)
+        for t in range(T):
+            for j in range(k):
+                d = int(ids[t, j]) // epr
+                y[t] += tw[t, j] * out[d][r * R + t * k + j]
+        ys.append(y)
+    return ys
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_peer_exchange_layout_matches_oracle(O, world):
+    from nvfp4 import synthetic
+
+    wd = synthetic.moe_weights(E, H, I, seed=5)
+    x_all = synthetic.bf16_round(synthetic.activations(3 * world, H, seed=6))
+    xs = [x_all[3 * r:3 * (r + 1)] for r in range(world)]
+    ys = peer_step_model(O, wd, xs, world, K_TOP)
+    ref, _, _ = O.moe(x_all, wd, top_k=K_TOP)
+    np.testing.assert_allclose(np.concatenate(ys), ref, rtol=1e-5, atol=1e-6)
