@@ -690,6 +690,13 @@ class EPStackBench:
         epr = MOE_E // world
         self.workload = self.describe(tokens, layers, world, exchange)
         self.layers = []
+        # One set of peer windows for the whole stack: the layers run one
+        # after another, so layer l+1 reuses layer l's receive rows (L2-resident).
+        windows = None
+        if exchange == "p2p":
+            from nvfp4.ep import PeerWindows
+            windows = PeerWindows.rendezvous(self.T_local * MOE_K, MOE_H, timeout_ms=10000)
+        self.windows = windows
         for l in range(layers):
             g = torch.Generator(device=device)
             g.manual_seed(1000 + l)  # router identical on every rank
@@ -699,7 +706,7 @@ class EPStackBench:
             local = MoEWeights.from_dict(wd, device)
             self.layers.append(EPMoELayer(local, router, top_k=MOE_K, num_experts=MOE_E,
                                           exchange=exchange, max_tokens=self.T_local,
-                                          timeout_ms=10000))
+                                          windows=windows))
         self.x = torch.randn((self.T_local, MOE_H), device=device).to(torch.bfloat16)
         # Fixed-capacity exchange (no host-side counts) for small batches: the
         # whole step, NCCL calls included, is then replayed from a CUDA graph.

@@ -265,7 +265,8 @@ class EPMoELayer:
                  num_experts: Optional[int] = None, group=None, backend=None,
                  renormalize: bool = True, static: Optional[bool] = None,
                  static_rows: int = 8192, exchange: str = "nccl",
-                 max_tokens: Optional[int] = None, timeout_ms: int = 0):
+                 max_tokens: Optional[int] = None, timeout_ms: int = 0,
+                 windows: Optional["PeerWindows"] = None):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.E = num_experts if num_experts is not None else router.shape[1]
@@ -280,6 +281,7 @@ class EPMoELayer:
             raise ValueError("exchange must be 'nccl' or 'p2p'")
         self.exchange = exchange
         self.windows = None
+        self._own_windows = False
         self.renormalize = renormalize
         self._ws = {}
         if exchange == "p2p":
@@ -287,8 +289,18 @@ class EPMoELayer:
                 raise ValueError("the peer exchange needs max_tokens (rows per rank are "
                                  "max_tokens * top_k)")
             self.max_tokens = max_tokens
-            self.windows = PeerWindows.rendezvous(max_tokens * top_k, router.shape[0], group,
-                                                  timeout_ms)
+            if windows is not None:
+                # Layers that run one after another in one stream may share
+                # windows: each step's flags carry the step counter, and the
+                # received rows of one layer are dead once its combine ran.
+                if (windows.world != self.world or windows.hidden != router.shape[0] or
+                        windows.max_rows < max_tokens * top_k):
+                    raise ValueError("shared windows do not fit this layer")
+                self.windows = windows
+            else:
+                self.windows = PeerWindows.rendezvous(max_tokens * top_k, router.shape[0],
+                                                      group, timeout_ms)
+                self._own_windows = True
 
     def uses_static(self, T: int) -> bool:
         if self.static is not None:
@@ -345,9 +357,9 @@ class EPMoELayer:
         return y
 
     def close(self):
-        if self.windows is not None:
+        if self.windows is not None and self._own_windows:
             self.windows.close()
-            self.windows = None
+        self.windows = None
 
     def forward(self, x: torch.Tensor, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
         if self.exchange == "p2p":

@@ -118,6 +118,34 @@ def test_single_rank_layer_forward(cuda):
         ep_layer.close()
 
 
+def test_layers_share_windows(cuda):
+    """Two layers of a stack on one set of windows (the step counter runs on
+    across layers): equal to the two single-GPU layers applied in turn."""
+    from nvfp4.ep import EPMoELayer, PeerWindows
+    from nvfp4.moe import MoELayer, MoEWeights
+
+    ws = [MoEWeights.from_dict(moe_dict(seed)) for seed in (11, 12)]
+    pw = PeerWindows.rendezvous(T * K, H)
+    layers = [EPMoELayer(w, w.router, top_k=K, num_experts=E, exchange="p2p", max_tokens=T,
+                         windows=pw) for w in ws]
+    try:
+        with pytest.raises(ValueError):
+            EPMoELayer(ws[0], ws[0].router, top_k=K, num_experts=E, exchange="p2p",
+                       max_tokens=2 * T, windows=pw)
+        for step in range(2):
+            h = tokens(50 + step)
+            ref = h
+            for lyr, w in zip(layers, ws):
+                h = lyr(h, residual=h)
+                ref = MoELayer(w, top_k=K)(ref, residual=ref)
+                assert torch.equal(h.view(torch.int16), ref.view(torch.int16)), step
+        assert pw.error() == 0
+    finally:
+        for lyr in layers:
+            lyr.close()  # shared windows stay open
+        pw.close()
+
+
 def test_dispatch_wait_times_out(cuda):
     """Rank 1 never dispatches: rank 0's wait gives up after its bound,
     records rank 1 as missing, and the context stays usable."""
