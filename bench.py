@@ -857,7 +857,8 @@ def run_reference(args, world, rank):
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": wl_cls.unit,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1e3 * el / args.steps, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": 1e3 * el / args.steps, "higher_is_better": True,
+        "scaling": getattr(wl_cls, "scaling", "weak"),
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": wdesc, "sample": desc},
         "cpu_baseline": {"value": value, "unit": wl_cls.unit, "cores": cores, "kind": "port",
