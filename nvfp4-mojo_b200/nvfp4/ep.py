@@ -155,18 +155,24 @@ class PeerWindows:
         own, handle = cls._create(world, max_rows, hidden)
         windows, opened = [None] * world, []
         windows[rank] = own
-        if world > 1:
-            every = exchange_handles(handle, group)
-            L = _lib.load()
-            for p in range(world):
-                if p == rank:
-                    continue
-                h = (ctypes.c_uint8 * _lib.EP_HANDLE_BYTES).from_buffer_copy(every[p])
-                w = ctypes.c_void_p()
-                _lib.check(L.nvfp4_ep_window_open(h, ctypes.byref(w)))
-                windows[p] = w.value
-                opened.append(w.value)
-            dist.barrier(group)  # every window zeroed and mapped before any step
+        L = _lib.load()
+        try:
+            if world > 1:
+                every = exchange_handles(handle, group)
+                for p in range(world):
+                    if p == rank:
+                        continue
+                    h = (ctypes.c_uint8 * _lib.EP_HANDLE_BYTES).from_buffer_copy(every[p])
+                    w = ctypes.c_void_p()
+                    _lib.check(L.nvfp4_ep_window_open(h, ctypes.byref(w)))
+                    windows[p] = w.value
+                    opened.append(w.value)
+                dist.barrier(group)  # every window zeroed and mapped before any step
+        except BaseException:
+            for w in opened:
+                L.nvfp4_ep_window_close(w)
+            L.nvfp4_ep_window_destroy(own)
+            raise
         return cls(rank, world, max_rows, hidden, windows, [own], opened, timeout_ms)
 
     @classmethod

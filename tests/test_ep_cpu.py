@@ -219,3 +219,23 @@ def test_peer_exchange_layout_matches_oracle(O, world):
     ys = peer_step_model(O, wd, xs, world, K_TOP)
     ref, _, _ = O.moe(x_all, wd, top_k=K_TOP)
     np.testing.assert_allclose(np.concatenate(ys), ref, rtol=1e-5, atol=1e-6)
+
+
+def test_peer_windows_table_and_layer_arguments():
+    """Host side of the peer exchange without a GPU: the ctypes peer table
+    carries rank, world, capacity, hidden size, timeout and every window, and
+    EPMoELayer refuses bad exchange arguments before touching the device."""
+    from nvfp4 import _lib
+    from nvfp4.ep import EPMoELayer, PeerWindows
+
+    pw = PeerWindows(2, 4, 64, 2048, [0x1000, 0x2000, 0x3000, 0x4000], [], [], timeout_ms=250)
+    p = pw.peers()
+    assert (p.rank, p.world, p.max_rows, p.hidden, p.timeout_ms) == (2, 4, 64, 2048, 250)
+    assert [p.windows[i] for i in range(4)] == [0x1000, 0x2000, 0x3000, 0x4000]
+    assert all(p.windows[i] is None for i in range(4, _lib.EP_MAX_WORLD))
+    pw.close()  # owns nothing: no call into the library
+    router = torch.zeros((H, E))
+    with pytest.raises(ValueError):
+        EPMoELayer(None, router, top_k=K_TOP, num_experts=E, backend=object(), exchange="nvshmem")
+    with pytest.raises(ValueError):
+        EPMoELayer(None, router, top_k=K_TOP, num_experts=E, backend=object(), exchange="p2p")
