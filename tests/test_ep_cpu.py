@@ -239,3 +239,59 @@ def test_peer_windows_table_and_layer_arguments():
         EPMoELayer(None, router, top_k=K_TOP, num_experts=E, backend=object(), exchange="nvshmem")
     with pytest.raises(ValueError):
         EPMoELayer(None, router, top_k=K_TOP, num_experts=E, backend=object(), exchange="p2p")
+
+
+def _dropped_rank_worker(rank, world, port, ret):
+    import datetime
+    import sys
+    import time
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parents[1]
+    sys.path.insert(0, str(root / "nvfp4-mojo_b200"))
+    sys.path.insert(0, str(root))
+    import torch.distributed as dist
+    from nvfp4 import synthetic
+    from nvfp4.ep import EPMoELayer
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=5))
+    wd = synthetic.moe_weights(E, H, I, seed=5)
+    layer = EPMoELayer(None, torch.from_numpy(wd["router"]), top_k=K_TOP, num_experts=E,
+                       backend=CpuBackend(wd, rank, world), static=False)
+    if rank == 1:
+        ret[1] = "left"
+        os._exit(0)  # this rank leaves between steps, without a word to the others
+    x = torch.from_numpy(synthetic.bf16_round(synthetic.activations(6, H, seed=6)))
+    t0 = time.monotonic()
+    try:
+        layer(x)
+        ret[0] = "no error"
+    except Exception as e:  # the exchange with the missing rank must fail, not hang
+        ret[0] = type(e).__name__
+    ret["t"] = time.monotonic() - t0
+    os._exit(0)
+
+
+def test_dropped_rank_fails_the_exchange_in_bounded_time():
+    """A rank that leaves between steps: the surviving rank's next exchange
+    (the counts all-to-all) ends with an error within the process group's
+    5 s timeout instead of waiting forever."""
+    ctx = mp.get_context("spawn")
+    mgr = ctx.Manager()
+    ret = mgr.dict()
+    port = _port()
+    procs = [ctx.Process(target=_dropped_rank_worker, args=(r, 2, port, ret)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    assert not alive, "a rank hung"
+    assert ret.get(1) == "left"
+    assert ret.get(0) not in (None, "no error"), ret.get(0)
+    assert ret["t"] < 60
