@@ -357,6 +357,7 @@ extern "C" int nvfp4_deltanet_forward(const nvfp4_deltanet_desc *desc,
                                       int hidden_dt, void *output, int out_dt, int64_t B,
                                       const nvfp4_deltanet_state *state, int proj_dt, void *ws,
                                       size_t ws_bytes, void *stream) {
+  NVFP4_ABI_RANGE();
   int rc = check_dn_desc(desc);
   if (rc) return rc;
   if (!w || !state) return fail(NVFP4_ERR_INVALID_ARG, "null weights or state");

@@ -312,6 +312,7 @@ extern "C" size_t nvfp4_moe_experts_workspace_size(const nvfp4_moe_desc *d, int6
 
 extern "C" int nvfp4_moe_route(const nvfp4_moe_desc *d, const float *router, const void *x,
                                int64_t T, int32_t *ids, float *w, float *logits, void *stream) {
+  NVFP4_ABI_RANGE();
   int rc = check_desc(d);
   if (rc) return rc;
   if (T < 0 || T > (1 << 24)) return fail(NVFP4_ERR_INVALID_ARG, "bad token count");
@@ -343,6 +344,7 @@ extern "C" int nvfp4_moe_experts(const nvfp4_moe_desc *d, const nvfp4_moe_weight
                                  const void *x, const int32_t *x_row_index,
                                  const int32_t *row_expert, int64_t R, void *y_rows, int y_dtype,
                                  void *ws, size_t ws_bytes, void *stream) {
+  NVFP4_ABI_RANGE();
   int rc = check_desc(d);
   if (rc) return rc;
   if ((rc = check_weights(w))) return rc;
@@ -364,6 +366,7 @@ extern "C" int nvfp4_moe_experts(const nvfp4_moe_desc *d, const nvfp4_moe_weight
 extern "C" int nvfp4_moe_combine(const void *y_slots, int slot_dtype, const float *topk_w,
                                  const int32_t *slot_pos, const void *residual, void *y,
                                  int y_dtype, int64_t T, int32_t k, int32_t H, void *stream) {
+  NVFP4_ABI_RANGE();
   if (T < 0 || k <= 0 || H <= 0 || H % 8) return fail(NVFP4_ERR_INVALID_ARG, "bad combine shape");
   if ((slot_dtype != NVFP4_DTYPE_F32 && slot_dtype != NVFP4_DTYPE_BF16) ||
       (y_dtype != NVFP4_DTYPE_F32 && y_dtype != NVFP4_DTYPE_BF16))
@@ -539,6 +542,7 @@ extern "C" int nvfp4_moe_forward(const nvfp4_moe_desc *d, const nvfp4_moe_weight
                                  const void *x, const void *residual, void *y, int y_dtype,
                                  int64_t T, int32_t *topk_ids, float *topk_w, void *ws,
                                  size_t ws_bytes, void *stream) {
+  NVFP4_ABI_RANGE();
   return moe_forward_impl(d, w, nullptr, 0, x, residual, y, y_dtype, T, topk_ids, topk_w, ws,
                           ws_bytes, stream);
 }
@@ -557,6 +561,7 @@ extern "C" int nvfp4_moe_forward_shared(const nvfp4_moe_desc *d, const nvfp4_moe
                                         const void *residual, void *y, int y_dtype, int64_t T,
                                         int32_t *topk_ids, float *topk_w, void *ws,
                                         size_t ws_bytes, void *stream) {
+  NVFP4_ABI_RANGE();
   if (!shared) return fail(NVFP4_ERR_INVALID_ARG, "null shared-expert weights");
   return moe_forward_impl(d, w, shared, shared_intermediate, x, residual, y, y_dtype, T,
                           topk_ids, topk_w, ws, ws_bytes, stream);
@@ -639,6 +644,7 @@ extern "C" int nvfp4_ep_p2p_forward(const nvfp4_moe_desc *d, const nvfp4_moe_wei
                                     const nvfp4_ep_peers *p, const void *x, const void *residual,
                                     void *y, int y_dtype, int64_t T, void *ws, size_t ws_bytes,
                                     void *stream) {
+  NVFP4_ABI_RANGE();
   int rc = check_ep_desc(d, p);
   if (rc) return rc;
   if ((rc = check_weights(local))) return rc;

@@ -66,6 +66,7 @@ extern "C" int nvfp4_moe_forward_noalloc(const nvfp4_moe_desc *desc,
                                          const nvfp4_moe_weights *weights, const void *x,
                                          const void *residual, void *y, int y_dtype, int64_t T,
                                          int32_t *topk_ids, float *topk_w, void *stream) {
+  NVFP4_ABI_RANGE();
   if (!desc) return fail(NVFP4_ERR_INVALID_ARG, "null MoE descriptor");
   if (T < 0) return fail(NVFP4_ERR_INVALID_ARG, "bad token count");
   const size_t need = nvfp4_moe_workspace_size(desc, T);

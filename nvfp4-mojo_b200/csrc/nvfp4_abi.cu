@@ -108,6 +108,7 @@ static int check_weights(const uint8_t *w, const uint8_t *sf, int64_t N, int64_t
 extern "C" int nvfp4_quantize_act(const void *x, int x_dt, int64_t M, int64_t K, int64_t x_ld,
                                   float input_scale, uint8_t *codes, uint8_t *scales,
                                   void *stream) {
+  NVFP4_ABI_RANGE();
   if (!valid_dtype(x_dt)) return fail(NVFP4_ERR_INVALID_ARG, "bad dtype");
   if (M < 0 || K <= 0 || K % NVFP4_GROUP_SIZE || x_ld < K)
     return fail(NVFP4_ERR_INVALID_ARG, "bad shape M=%lld K=%lld ld=%lld", (long long)M,
@@ -128,6 +129,7 @@ extern "C" int nvfp4_quantize_act(const void *x, int x_dt, int64_t M, int64_t K,
 extern "C" int nvfp4_linear_w4a4(const nvfp4_linear_desc *lin, const uint8_t *w,
                                  const uint8_t *sf, const uint8_t *xq, const uint8_t *xsf,
                                  void *y, int y_dt, int64_t M, void *stream) {
+  NVFP4_ABI_RANGE();
   if (!lin) return fail(NVFP4_ERR_INVALID_ARG, "null linear descriptor");
   int rc = check_weights(w, sf, lin->out_features, lin->in_features);
   if (rc) return rc;
@@ -177,6 +179,7 @@ static int run_w4a4_with_scratch(const nvfp4_linear_desc *lin, const uint8_t *w,
 extern "C" int nvfp4_linear_forward(const nvfp4_linear_desc *lin, const uint8_t *w,
                                     const uint8_t *sf, const void *x, int x_dt, void *y,
                                     int y_dt, int64_t M, uint32_t flags, void *stream) {
+  NVFP4_ABI_RANGE();
   if (!lin) return fail(NVFP4_ERR_INVALID_ARG, "null linear descriptor");
   int rc = check_weights(w, sf, lin->out_features, lin->in_features);
   if (rc) return rc;
@@ -200,6 +203,7 @@ extern "C" int nvfp4_linear_forward(const nvfp4_linear_desc *lin, const uint8_t 
 extern "C" int nvfp4_gemm_kernel(int64_t M_out, int64_t N_tok, int64_t K, const uint8_t *w,
                                  const uint8_t *sf, const void *act, int act_dt, void *out,
                                  int out_dt, float alpha, void *stream) {
+  NVFP4_ABI_RANGE();
   int rc = check_weights(w, sf, M_out, K);
   if (rc) return rc;
   if (!valid_dtype(act_dt) || !valid_dtype(out_dt)) return fail(NVFP4_ERR_INVALID_ARG, "bad dtype");
@@ -220,6 +224,7 @@ extern "C" int nvfp4_gemm_kernel(int64_t M_out, int64_t N_tok, int64_t K, const 
 
 extern "C" int nvfp4_matvec(const nvfp4_linear_desc *lin, const uint8_t *w, const uint8_t *sf,
                             const float *x, float *y, void *stream) {
+  NVFP4_ABI_RANGE();
   if (!lin) return fail(NVFP4_ERR_INVALID_ARG, "null linear descriptor");
   int rc = check_weights(w, sf, lin->out_features, lin->in_features);
   if (rc) return rc;
@@ -242,6 +247,7 @@ extern "C" int nvfp4_dequant_tile(const uint8_t *w, const uint8_t *sf, float *ou
                                   int64_t weight_stride, int64_t scale_stride, int64_t start_row,
                                   int64_t start_col, int64_t tile_m, int64_t tile_k,
                                   void *stream) {
+  NVFP4_ABI_RANGE();
   if (!w || !sf || !out) return fail(NVFP4_ERR_INVALID_ARG, "null pointer");
   if (tile_m < 0 || tile_k < 0 || start_row < 0 || start_col < 0)
     return fail(NVFP4_ERR_INVALID_ARG, "negative tile geometry");
@@ -266,6 +272,7 @@ extern "C" int nvfp4_device_status(void) {
 
 extern "C" int nvfp4_dequant(const uint8_t *w, const uint8_t *sf, int64_t rows, int64_t K,
                              void *out, int out_dt, void *stream) {
+  NVFP4_ABI_RANGE();
   int rc = check_weights(w, sf, rows, K);
   if (rc) return rc;
   if (!out) return fail(NVFP4_ERR_INVALID_ARG, "null output pointer");

@@ -562,6 +562,7 @@ extern "C" int64_t nvfp4_st_read_host(const nvfp4_st_file *f, int64_t i, void *d
 }
 
 extern "C" int nvfp4_st_read_device(nvfp4_st_file *f, int64_t i, void *dst, void *stream) {
+  NVFP4_ABI_RANGE();
   if (!tensor_ok(f, i)) return fail(NVFP4_ERR_INVALID_ARG, "bad file handle or tensor index");
   const nvfp4_st_tensor_info &t = f->infos[i];
   if (t.data_size == 0) return NVFP4_OK;
@@ -701,6 +702,7 @@ extern "C" int nvfp4_st_get_linear_info(const nvfp4_st_model *m, const char *pre
 
 extern "C" int nvfp4_st_load_linear(nvfp4_st_model *m, const char *prefix, uint8_t *w,
                                     uint8_t *sf, float *ws2, uint32_t flags, void *stream) {
+  NVFP4_ABI_RANGE();
   if (!w || !sf) return fail(NVFP4_ERR_INVALID_ARG, "null weight or blockscale destination");
   LinearLoc L;
   const int rc = locate_linear(m, prefix, &L);
@@ -714,6 +716,7 @@ extern "C" int nvfp4_st_load_experts(nvfp4_st_model *m, const char *layer, int32
                                      uint8_t *gate_up_scale, float *gate_up_scale_2,
                                      uint8_t *down, uint8_t *down_scale, float *down_scale_2,
                                      void *stream) {
+  NVFP4_ABI_RANGE();
   if (!m || !layer) return fail(NVFP4_ERR_INVALID_ARG, "null model or layer prefix");
   if (count <= 0 || first < 0 || (shared && (count != 1 || first != 0)))
     return fail(NVFP4_ERR_INVALID_ARG, "bad expert range");
