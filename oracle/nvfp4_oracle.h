@@ -19,8 +19,8 @@
  *   - The MoE layer and the W4A4 activation quantizer have no counterpart in
  *     the reference at all: their semantics are defined here (parity unpinned).
  *
- * Naming follows BASELINE naming: M = tokens, N = out_features, K = in_features,
- * except where a function mirrors a reference function whose names differ.
+ * Naming: M = tokens, N = out_features, K = in_features, except where a
+ * function mirrors a reference function whose names differ.
  */
 #ifndef NVFP4_ORACLE_H
 #define NVFP4_ORACLE_H
