@@ -236,6 +236,38 @@ def linear_w4a4(packed, scales, x, input_scale, ws2=1.0, ws2_rows=None, rows=Non
                   ws2_rows=ws2_rows, rows=rows, cols=cols, n_threads=n_threads)
 
 
+def fp4_digits(x, digits=4):
+    """FP4-digit decomposition of activations (the decode GEMV draft's
+    input side; no reference counterpart): per token t and digit d,
+    s[t, d] = amax(residual_t) / (6 * 448), digit = quantize_act(residual_t,
+    s[t, d]) (per-16 E4M3 scales, E2M1 codes, RNE), residual_t -=
+    dequant(digit) * s[t, d].  Returns codes [M * D, K/2], scales
+    [M * D, K/16] and s [M * D] with row t * D + d."""
+    x = _f32(x)
+    M, K = x.shape
+    codes = np.zeros((M * digits, K // 2), np.uint8)
+    scs = np.zeros((M * digits, K // 16), np.uint8)
+    sd = np.zeros(M * digits, np.float32)
+    for t in range(M):
+        r = x[t:t + 1].copy()
+        for d in range(digits):
+            s_ = np.float32(np.abs(r).max()) / np.float32(6.0 * 448.0)
+            row = t * digits + d
+            sd[row] = s_
+            if s_ == 0.0:
+                continue
+            q, sc = quantize_act(r, float(s_))
+            codes[row], scs[row] = q[0], sc[0]
+            r = (r - dequant(q, sc) * s_).astype(np.float32)
+    return codes, scs, sd
+
+
+def fp4_digits_value(codes, scales, sd, digits=4):
+    """The activations the digits represent: [M, K] fp32."""
+    v = dequant(codes, scales) * sd[:, None]
+    return v.reshape(-1, digits, v.shape[1]).sum(axis=1, dtype=np.float32)
+
+
 def router(x, router_w):
     x, r = _f32(x), _f32(router_w)
     T, H = x.shape
