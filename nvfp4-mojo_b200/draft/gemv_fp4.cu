@@ -177,15 +177,18 @@ __global__ void __launch_bounds__(256) fp4_digits_kernel(const uint16_t *__restr
       const int g = tid + 256 * i;
       if (g >= G) continue;
       const uint32_t sf = s > 0.0f ? e4m3_rn(ga[i] / (6.0f * s)) : 0u;
-      const float sdeq = e4m3_to_f32(sf) * s;
+      const float sff = e4m3_to_f32(sf);
+      const float sdeq = sff * s;
       uint32_t packed[2] = {0u, 0u};
       if (sdeq != 0.0f) {
+        // Residual as the oracle forms it: (LUT * scale, exact) * s, then
+        // the subtraction, each rounded once (no contraction into an FMA).
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const uint32_t c = e2m1x2_rn(v[i][2 * j] / sdeq, v[i][2 * j + 1] / sdeq);
           packed[j >> 2] |= c << (8 * (j & 3));
-          v[i][2 * j] -= e2m1_to_f32(c & 15u) * sdeq;
-          v[i][2 * j + 1] -= e2m1_to_f32(c >> 4) * sdeq;
+          v[i][2 * j] = __fsub_rn(v[i][2 * j], __fmul_rn(e2m1_to_f32(c & 15u) * sff, s));
+          v[i][2 * j + 1] = __fsub_rn(v[i][2 * j + 1], __fmul_rn(e2m1_to_f32(c >> 4) * sff, s));
         }
       }
       *reinterpret_cast<uint2 *>(q + (int64_t)row * (K / 2) + g * 8) =
