@@ -102,6 +102,12 @@ __device__ __forceinline__ void tmem_st_x16(uint32_t taddr, const uint32_t (&v)[
       : "memory");
 }
 
+// Adds `bytes` to the phase's expected transaction count without arriving.
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
 __device__ __forceinline__ void tmem_st_wait_all() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
@@ -262,14 +268,35 @@ __global__ void __launch_bounds__(kGvThreads, 1)
   const uint32_t tmem = *tmem_slot;
   const uint32_t tmem_sf = tmem + 2 * kGvBN;
   volatile int *abort = &abort_flag;
-  // The digits (B, their scales, sd) come from the previous kernel.
-  // Next step: stream the first stages' weights before this wait.
-  pdl_wait();
-  pdl_trigger();
+  // Programmatic dependent launch: the digits (B, their scales, sd) come
+  // from the previous kernel, the weights do not.  The producer issues the
+  // first stages' weight loads before griddepcontrol.wait (their phases
+  // cannot complete before the digit loads' arrive.expect_tx); every other
+  // thread waits first.  The weight buffers must therefore not be written by
+  // the kernel launched just before this one.
+  const bool pre_issue = warp == 0 && lane == 0;
+  if (!pre_issue) {
+    pdl_wait();
+    pdl_trigger();
+  }
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
+      constexpr int kTxA = L::kA + L::kSA;
+      // Weights of the first stages, before the wait.
+      const int pre = hi - lo < kGvStages ? (int)(hi - lo) : kGvStages;
+      for (int g = 0; g < pre; ++g) {
+        const int64_t u = lo + g;
+        const int tile = (int)(u / a.KB), kb = (int)(u % a.KB);
+        const uint32_t st = sbase + g * L::kStage;
+        mbar_expect_tx(bar_full + 8 * g, kTxA);
+        tma_load_2d(st, &tmA, kb * (kGvBK / 2), tile * kGvBM, bar_full + 8 * g);
+        tma_load_2d(st + L::kA + L::kB, &tmSA, kb * (kGvBK / 16), tile * kGvBM,
+                    bar_full + 8 * g);
+      }
+      pdl_wait();
+      pdl_trigger();
       int g = 0, issued = 0;
       for (int64_t u = lo; u < hi; ++u, ++g) {
         const int tile = (int)(u / a.KB), kb = (int)(u % a.KB);
@@ -278,14 +305,19 @@ __global__ void __launch_bounds__(kGvThreads, 1)
                                  kDevTimeoutEmpty, abort))
           break;
         const uint32_t st = sbase + s * L::kStage;
-        mbar_arrive_expect_tx(bar_full + 8 * s, L::kTx);
-        tma_load_2d(st, &tmA, kb * (kGvBK / 2), tile * kGvBM, bar_full + 8 * s);
+        if (g < pre) {
+          mbar_arrive_expect_tx(bar_full + 8 * s, L::kTx - kTxA);
+        } else {
+          mbar_arrive_expect_tx(bar_full + 8 * s, L::kTx);
+          tma_load_2d(st, &tmA, kb * (kGvBK / 2), tile * kGvBM, bar_full + 8 * s);
+          tma_load_2d(st + L::kA + L::kB, &tmSA, kb * (kGvBK / 16), tile * kGvBM,
+                      bar_full + 8 * s);
+        }
         tma_load_2d(st + L::kA, &tmB, kb * (kGvBK / 2), 0, bar_full + 8 * s);
-        tma_load_2d(st + L::kA + L::kB, &tmSA, kb * (kGvBK / 16), tile * kGvBM,
-                    bar_full + 8 * s);
         tma_load_2d(st + L::kA + L::kB + L::kSA, &tmSB, kb * (kGvBK / 16), 0, bar_full + 8 * s);
         issued = g + 1;
       }
+      // (The loop cannot stop before `pre`: its first waits come at g >= S.)
       for (int qq = issued - kGvStages > 0 ? issued - kGvStages : 0; qq < issued; ++qq) {
         volatile int no_abort = 0;
         mbar_wait(bar_full + 8 * (qq % kGvStages), (qq / kGvStages) & 1, &g_fp4gv_status,
