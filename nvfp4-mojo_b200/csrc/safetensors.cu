@@ -126,6 +126,7 @@ struct Json {
         case 'u': {
           uint32_t cp;
           if (!hex4(cp)) return false;
+          if (cp >= 0xDC00 && cp < 0xE000) return fail_at("lone low surrogate");
           if (cp >= 0xD800 && cp < 0xDC00) {  // surrogate pair
             uint32_t lo;
             if (end - p < 6 || p[0] != '\\' || p[1] != 'u') return fail_at("lone surrogate");
@@ -209,11 +210,49 @@ struct Json {
   }
 };
 
+// Well-formed UTF-8 (RFC 3629: no overlong forms, no surrogates, at most
+// U+10FFFF), which the safetensors format requires of its header.
+bool valid_utf8(const char *s, size_t n) {
+  const unsigned char *p = reinterpret_cast<const unsigned char *>(s), *e = p + n;
+  while (p < e) {
+    const unsigned c = *p;
+    int len;
+    unsigned cp;
+    if (c < 0x80) {
+      ++p;
+      continue;
+    } else if ((c & 0xE0) == 0xC0) {
+      len = 2;
+      cp = c & 0x1F;
+    } else if ((c & 0xF0) == 0xE0) {
+      len = 3;
+      cp = c & 0x0F;
+    } else if ((c & 0xF8) == 0xF0) {
+      len = 4;
+      cp = c & 0x07;
+    } else {
+      return false;
+    }
+    if (e - p < len) return false;
+    for (int i = 1; i < len; ++i) {
+      if ((p[i] & 0xC0) != 0x80) return false;
+      cp = (cp << 6) | (p[i] & 0x3F);
+    }
+    if ((len == 2 && cp < 0x80) || (len == 3 && cp < 0x800) || (len == 4 && cp < 0x10000) ||
+        cp > 0x10FFFF || (cp >= 0xD800 && cp < 0xE000))
+      return false;
+    p += len;
+  }
+  return true;
+}
+
 // _parse_safetensors_header (nvfp4/weight_loader.mojo:292-363): a flat object
 // of name -> {dtype, shape, data_offsets}, `__metadata__` skipped, header
 // order kept.  Missing fields default as in the reference (dtype "", shape
 // [], data offsets 0/0).
 int parse_header(const char *json, size_t n, int64_t data_bytes, nvfp4_st_file *f) {
+  if (!valid_utf8(json, n))
+    return fail(NVFP4_ERR_INVALID_ARG, "safetensors header is not valid UTF-8");
   Json j{json, json + n, {}};
   if (!j.expect('{')) return fail(NVFP4_ERR_INVALID_ARG, "safetensors header: %s", j.err.c_str());
   if (j.peek('}')) return NVFP4_OK;
@@ -221,6 +260,8 @@ int parse_header(const char *json, size_t n, int64_t data_bytes, nvfp4_st_file *
     std::string name;
     if (!j.string(name) || !j.expect(':'))
       return fail(NVFP4_ERR_INVALID_ARG, "safetensors header: %s", j.err.c_str());
+    if (name.find('\0') != std::string::npos)
+      return fail(NVFP4_ERR_INVALID_ARG, "safetensors header: NUL character in a tensor name");
     if (name == "__metadata__") {
       if (!j.skip()) return fail(NVFP4_ERR_INVALID_ARG, "safetensors header: %s", j.err.c_str());
     } else {
@@ -237,6 +278,8 @@ int parse_header(const char *json, size_t n, int64_t data_bytes, nvfp4_st_file *
           if (key == "dtype") {
             std::string dt;
             ok = j.string(dt);
+            if (ok && dt.find('\0') != std::string::npos)
+              return fail(NVFP4_ERR_INVALID_ARG, "tensor %s: NUL character in dtype", name.c_str());
             if (ok && dt.size() >= sizeof(info.dtype))
               return fail(NVFP4_ERR_INVALID_ARG, "tensor %s: dtype too long", name.c_str());
             if (ok) memcpy(info.dtype, dt.c_str(), dt.size() + 1);
