@@ -107,3 +107,64 @@ def test_config_sizes():
     assert nvh * vd == 4096                     # z_dim
     assert nvh * kd * vd == 524288              # total_state_floats
     assert nvh * kd * vd * 4 == 2097152         # state bytes per layer
+
+
+def dn_shape_ok(d_model, nkh, nvh, kd, vd, ck, eps):
+    """The shapes nvfp4_deltanet_forward serves (include/nvfp4_deltanet.h)."""
+    return (d_model > 0 and d_model % 16 == 0 and nkh > 0 and nvh > 0 and nvh % nkh == 0
+            and 0 < kd <= 256 and 4 <= vd <= 256 and vd & (vd - 1) == 0 and 1 <= ck <= 8
+            and (nvh * vd) % 16 == 0 and eps >= 0.0)
+
+
+def test_descriptor_rules_without_gpu():
+    """nvfp4_deltanet_workspace_size is 0 exactly for the shapes the header
+    rules out (host-side check, no GPU), over generated descriptors."""
+    import ctypes
+
+    from hypothesis import given, settings
+    from hypothesis import strategies as st
+    from nvfp4 import _lib
+
+    L = _lib.load()
+
+    @settings(max_examples=400, deadline=None)
+    @given(st.integers(-16, 4096), st.integers(-1, 9), st.integers(-1, 40), st.integers(-1, 300),
+           st.sampled_from([-4, 0, 2, 3, 4, 8, 12, 16, 32, 64, 96, 128, 256, 512]),
+           st.integers(-1, 10), st.sampled_from([1e-6, 0.0, -1e-6]), st.integers(0, 3))
+    def check(d_model, nkh, nvh, kd, vd, ck, eps, B):
+        desc = _lib.DeltaNetDesc(d_model, nkh, nvh, kd, vd, ck, eps)
+        size = L.nvfp4_deltanet_workspace_size(ctypes.byref(desc), B)
+        assert (size > 0) == dn_shape_ok(d_model, nkh, nvh, kd, vd, ck, eps), desc
+
+    check()
+
+
+def test_forward_argument_checks_without_gpu():
+    """nvfp4_deltanet_forward refuses bad arguments before any CUDA work."""
+    import ctypes
+
+    from nvfp4 import _lib
+
+    L = _lib.load()
+    desc = _lib.DeltaNetDesc(2048, 16, 32, 128, 128, 4, 1e-6)
+    w = _lib.DeltaNetWeightPtrs()
+    st = _lib.DeltaNetStatePtrs()
+
+    def call(B=1, hdt=1, odt=1, pdt=1, ws=256, ws_bytes=1 << 40, weights=w, state=st):
+        return L.nvfp4_deltanet_forward(ctypes.byref(desc), ctypes.byref(weights), 256, hdt, 256,
+                                        odt, B, ctypes.byref(state), pdt, ws, ws_bytes, None)
+
+    assert call() == _lib.NVFP4_ERR_INVALID_ARG  # null weight pointers
+    for name in ("a_log", "dt_bias", "conv_q", "conv_k", "conv_v"):
+        setattr(w, name, 256)
+    for name in ("s", "conv_q", "conv_k", "conv_v"):
+        setattr(st, name, 256)
+    w.conv_bias_q = 256  # one bias of three
+    assert call() == _lib.NVFP4_ERR_INVALID_ARG
+    assert b"biases" in L.nvfp4_last_error_string()
+    w.conv_bias_q = None
+    assert call(hdt=7) == _lib.NVFP4_ERR_INVALID_ARG
+    assert call(ws=16) == _lib.NVFP4_ERR_INVALID_ARG  # workspace not 256-byte aligned
+    assert call(B=-1) == _lib.NVFP4_ERR_INVALID_ARG
+    assert call(B=0) == _lib.NVFP4_OK  # nothing to do
+    assert call(ws_bytes=1024) == _lib.NVFP4_ERR_WORKSPACE
