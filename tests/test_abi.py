@@ -149,3 +149,28 @@ def test_python_api_refuses_host_tensors():
     y = torch.zeros((2, 32), dtype=torch.bfloat16)
     with pytest.raises(ValueError, match="CUDA"):
         nvfp4.nvfp4_linear_forward(lin, w, sf, x, y, 2)
+
+
+def test_moe_descriptor_rules_without_gpu():
+    """nvfp4_moe_workspace_size is 0 exactly for the layers nvfp4.h rules
+    out, over generated descriptors (host-side check)."""
+    from hypothesis import given, settings
+    from hypothesis import strategies as st
+    from nvfp4 import _lib
+
+    L = _lib.load()
+
+    def ok(E, k, H, I):
+        return (1 <= E <= 256 and 1 <= k <= min(32, E) and H > 0 and H % 128 == 0
+                and H <= 6144 and I > 0 and I % 128 == 0)
+
+    @settings(max_examples=300, deadline=None)
+    @given(st.integers(-1, 300), st.integers(-1, 40),
+           st.sampled_from([-128, 0, 64, 128, 256, 2048, 6144, 6272, 8192]),
+           st.sampled_from([-128, 0, 96, 128, 768, 1024]), st.integers(0, 64))
+    def check(E, k, H, I, T):
+        desc = _lib.MoEDesc(E, k, H, I, 1)
+        size = L.nvfp4_moe_workspace_size(ctypes.byref(desc), T)
+        assert (size > 0) == ok(E, k, H, I), (E, k, H, I, T)
+
+    check()
