@@ -1,6 +1,9 @@
 // gemv_fp4.cu -- DRAFT, not part of libnvfp4.so: it compiles for sm_100a
 // beside the sources in ../csrc (copy it there to build it) but has not yet
-// run on a GPU, so nothing calls it.  Decode GEMV y[M, N] =
+// run on a GPU, so nothing calls it.  To wire it in: an opt-in flag of
+// nvfp4_linear_forward for M <= 8, K % 256 == 0, K <= 8192, its scratch
+// (digits, scales, partial sums: gemv_fp4_scratch_bytes) taken from
+// stream-ordered memory as the W4A4 path does.  Decode GEMV y[M, N] =
 // alpha[n] * x[M, K] . W[N, K]^T (M <= 8) on the block-scaled FP4 tensor
 // cores, with no per-weight decode.
 //
