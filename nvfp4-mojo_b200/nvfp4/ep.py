@@ -126,8 +126,10 @@ class PeerWindows:
     `emulated` builds the windows of `world` ranks in one process on one
     device, for running the ranks' steps one after another in one stream."""
 
-    def __init__(self, rank, world, max_rows, hidden, windows, owned, opened, timeout_ms=0):
+    def __init__(self, rank, world, max_rows, hidden, windows, owned, opened, timeout_ms=0,
+                 group=None, collective=False):
         self.rank, self.world = rank, world
+        self.group, self._collective = group, collective
         self.max_rows, self.hidden = max_rows, hidden
         self.windows = list(windows)
         self._owned = list(owned)    # windows this object frees
@@ -173,7 +175,8 @@ class PeerWindows:
                 L.nvfp4_ep_window_close(w)
             L.nvfp4_ep_window_destroy(own)
             raise
-        return cls(rank, world, max_rows, hidden, windows, [own], opened, timeout_ms)
+        return cls(rank, world, max_rows, hidden, windows, [own], opened, timeout_ms, group,
+                   collective=world > 1)
 
     @classmethod
     def emulated(cls, world: int, max_rows: int, hidden: int, timeout_ms: int = 0):
@@ -205,12 +208,19 @@ class PeerWindows:
         return v.value
 
     def close(self):
+        """Unmaps the peers' windows and frees this rank's.  For windows made
+        by `rendezvous` this is collective: every rank unmaps first, then a
+        barrier, then each frees its own, so no window is freed while another
+        process still maps it."""
         L = _lib.load()
         for w in self._opened:
             L.nvfp4_ep_window_close(w)
+        self._opened = []
+        if self._collective and self._owned and dist.is_initialized():
+            dist.barrier(self.group)
         for w in self._owned:
             L.nvfp4_ep_window_destroy(w)
-        self._opened, self._owned = [], []
+        self._owned = []
 
 
 def p2p_dispatch(pw: PeerWindows, topk_ids, x, experts_per_rank: int, stream=None):
