@@ -62,7 +62,7 @@ extern "C" {
 /* Error word bits (nvfp4_ep_p2p_error). */
 #define NVFP4_EP_ERR_DISPATCH_TIMEOUT 0x1u /* a dispatch flag did not arrive */
 #define NVFP4_EP_ERR_DONE_TIMEOUT 0x2u     /* a done flag did not arrive */
-/* bits 8..15: 1 + the first rank whose flag was missing */
+/* bit 8 + p set: rank p's flag was missing (bits 8..15, one per rank) */
 
 typedef struct nvfp4_ep_peers {
   int32_t rank;
