@@ -101,12 +101,32 @@ def test_forward_small_golden(O):
 
 def test_config_sizes():
     """test_config / test_state_init / test_o1_memory
-    (tests/test_deltanet.mojo:219-445): the default layer's dimensions."""
-    nkh, nvh, kd, vd = 16, 32, 128, 128
-    assert 2 * nkh * kd + nvh * vd == 8192      # total_qkv_dim
-    assert nvh * vd == 4096                     # z_dim
-    assert nvh * kd * vd == 524288              # total_state_floats
-    assert nvh * kd * vd * 4 == 2097152         # state bytes per layer
+    (tests/test_deltanet.mojo:219-445): the default layer's dimensions,
+    through the Python mirror's DeltaNetConfig and DeltaNetState."""
+    from nvfp4.deltanet import DeltaNetConfig, DeltaNetState
+
+    c = DeltaNetConfig()
+    assert (c.d_model, c.num_key_heads, c.num_value_heads, c.key_dim, c.value_dim,
+            c.conv_kernel) == (2048, 16, 32, 128, 128, 4)
+    assert c.total_qkv_dim() == 8192
+    assert c.z_dim() == 4096 and c.v_dim() == 4096
+    assert c.q_dim() == c.k_dim() == 2048
+    assert c.v_groups() == 2
+    assert c.state_size_per_head() == 16384
+    assert c.total_state_floats() == 524288
+    assert c.total_state_floats() * 4 == 2097152  # state bytes per layer
+    st = DeltaNetState(c, batch=2, device="cpu")
+    assert tuple(st.s_matrix.shape) == (2, 32, 128, 128) and not st.s_matrix.any()
+    assert tuple(st.conv_buf_q.shape) == (2, 2048, 3)
+    assert tuple(st.conv_buf_v.shape) == (2, 4096, 3)
+
+
+def test_host_softplus_matches_oracle(O):
+    """nvfp4.deltanet.softplus (host-side mirror) against the oracle's."""
+    from nvfp4.deltanet import softplus
+
+    for x in (-30.0, -20.5, -1.0, 0.0, 0.5, 1.0, 19.9, 20.5, 30.0):
+        expect_close(softplus(x), O.softplus(x), 1e-6)
 
 
 def dn_shape_ok(d_model, nkh, nvh, kd, vd, ck, eps):
