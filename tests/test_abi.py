@@ -174,3 +174,28 @@ def test_moe_descriptor_rules_without_gpu():
         assert (size > 0) == ok(E, k, H, I), (E, k, H, I, T)
 
     check()
+
+
+def test_headers_compile_as_c():
+    """Every header of the drop-in boundary is plain C (C99 and C11, no C++ or
+    torch types), so any FFI (Mojo external_call, cgo, ctypes, JNI) can bind
+    it; each also compiles on its own."""
+    import shutil
+    import subprocess
+    import tempfile
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    headers = sorted((ROOT / "include").glob("*.h"))
+    assert headers
+    with tempfile.TemporaryDirectory() as d:
+        for std in ("c99", "c11"):
+            for hs in [[h] for h in headers] + [headers]:
+                src = Path(d) / "t.c"
+                src.write_text("".join(f'#include "{h.name}"\n' for h in hs) +
+                               "int main(void) { return 0; }\n")
+                out = subprocess.run([cc, f"-std={std}", "-Wall", "-Wextra", "-Werror",
+                                      "-pedantic", "-fsyntax-only", "-I", str(ROOT / "include"),
+                                      str(src)], capture_output=True, text=True)
+                assert out.returncode == 0, (std, [h.name for h in hs], out.stderr)
