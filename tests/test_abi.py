@@ -199,3 +199,35 @@ def test_headers_compile_as_c():
                                       "-pedantic", "-fsyntax-only", "-I", str(ROOT / "include"),
                                       str(src)], capture_output=True, text=True)
                 assert out.returncode == 0, (std, [h.name for h in hs], out.stderr)
+
+
+def test_plain_c_program_links_and_calls_the_library():
+    """A C program (no Python, no torch) links libnvfp4.so and gets the
+    library's answers and error strings through the C ABI alone."""
+    import shutil
+    import subprocess
+    import tempfile
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    libdir = ROOT / "nvfp4-mojo_b200" / "nvfp4"
+    with tempfile.TemporaryDirectory() as d:
+        src, exe = Path(d) / "abi.c", Path(d) / "abi"
+        src.write_text(
+            '#include <stdio.h>\n#include "nvfp4.h"\n#include "nvfp4_ep.h"\n'
+            "int main(void) {\n"
+            "  nvfp4_linear_desc d = {2048, 1536, 1.0f, 1.0f, 0};\n"
+            '  printf("%d %zu\\n", nvfp4_abi_version(), nvfp4_ep_window_size(2, 64, 2048));\n'
+            "  int rc = nvfp4_linear_forward(&d, 0, 0, 0, 1, 0, 1, 4, 0, 0);\n"
+            '  printf("%d %s\\n", rc, nvfp4_last_error_string());\n'
+            "  return 0;\n}\n")
+        out = subprocess.run([cc, "-std=c11", "-I", str(ROOT / "include"), str(src), "-L",
+                              str(libdir), "-lnvfp4", f"-Wl,-rpath,{libdir}", "-o", str(exe)],
+                             capture_output=True, text=True)
+        assert out.returncode == 0, out.stderr
+        run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+        assert run.returncode == 0, run.stderr
+        lines = run.stdout.splitlines()
+        assert lines[0] == "1 1573632"
+        assert lines[1].startswith("-1 ") and "null" in lines[1]
