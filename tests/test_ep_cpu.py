@@ -128,7 +128,7 @@ def test_ep_exchange_matches_single_process_oracle(O, static):
     from nvfp4 import synthetic
 
     world = 2
-    mgr = mp.Manager()
+    mgr = mp.get_context("spawn").Manager()
     ret = mgr.dict()
     mp.spawn(_worker, args=(world, _port(), static, ret), nprocs=world, join=True)
     wd = synthetic.moe_weights(E, H, I, seed=5)
@@ -161,7 +161,7 @@ def test_peer_window_handle_exchange():
     """exchange_handles: every rank gets every rank's 64-byte IPC handle, in
     rank order (gloo ranks stand in for the GPUs' processes)."""
     world = 3
-    mgr = mp.Manager()
+    mgr = mp.get_context("spawn").Manager()
     ret = mgr.dict()
     mp.spawn(_handles_worker, args=(world, _port(), ret), nprocs=world, join=True)
     want = [[(p * 37 + i) % 256 for i in range(64)] for p in range(world)]
