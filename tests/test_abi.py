@@ -231,3 +231,38 @@ def test_plain_c_program_links_and_calls_the_library():
         lines = run.stdout.splitlines()
         assert lines[0] == "1 1573632"
         assert lines[1].startswith("-1 ") and "null" in lines[1]
+
+
+def test_compute_calls_fail_loudly_without_a_gpu():
+    """On a host without a usable GPU every compute entry point returns
+    NVFP4_ERR_CUDA with the failing step named (no CPU fallback, no crash).
+    Fake device addresses are passed, so this runs only where no GPU is
+    visible: on a GPU host the same calls would launch kernels on them."""
+    import torch
+
+    from nvfp4 import _lib
+
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is visible: the fake device pointers must not reach a kernel")
+    L = _lib.load()
+    A = 1 << 20  # 256-byte aligned, never dereferenced on the host
+    lin = _lib.LinearDesc(2048, 1536, 1.0, 1.0, None)
+    moe = _lib.MoEDesc(16, 4, 256, 256, 1)
+    w = _lib.MoEWeightPtrs(A, A, A, None, None, A, A, None, None)
+    peers = _lib.EpPeers()
+    peers.rank, peers.world, peers.max_rows, peers.hidden = 0, 1, 64, 256
+    peers.windows[0] = A
+    calls = {
+        "linear_forward": lambda: L.nvfp4_linear_forward(ctypes.byref(lin), A, A, A, 1, A, 1, 4,
+                                                         0, None),
+        "dequant": lambda: L.nvfp4_dequant(A, A, 16, 256, A, 0, None),
+        "quantize_act": lambda: L.nvfp4_quantize_act(A, 1, 4, 256, 256, 1.0, A, A, None),
+        "moe_forward": lambda: L.nvfp4_moe_forward(ctypes.byref(moe), ctypes.byref(w), A, None, A,
+                                                   1, 4, None, None, A, 1 << 30, None),
+        "ep_p2p_dispatch": lambda: L.nvfp4_ep_p2p_dispatch(ctypes.byref(peers), A, A, 4, 4, 16,
+                                                           None),
+    }
+    for name, call in calls.items():
+        rc = call()
+        assert rc == _lib.NVFP4_ERR_CUDA, (name, rc, L.nvfp4_last_error_string())
+        assert L.nvfp4_last_error_string(), name
