@@ -2,17 +2,22 @@
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
 
-Workloads (synthetic inputs in the benchmark configurations' shapes):
-  gemv     decode GEMV sweep, M in {1,2,4,8} x (K,N) in {(2048,1536), (768,2048),
-           (4096,14336)}; one step = the 12 calls; GB/s over weight+scale bytes.
+Default workload `ep` (one step = one pass of a 48-layer stack of the
+128-expert, top-8 NVFP4 MoE layer, h = h + MoE(h), over a 64-token decode
+batch, expert-parallel over the N ranks: 128/N experts and 64/N tokens per
+GPU, device-initiated dispatch/combine through peer memory).  Beside it, at
+N = 1, the same line carries the decode GEMV sweep and the W4A16 prefill sweep
+(`secondary`), each with the roofline of its dominant launch, and the layer's
+`parity` against the CPU oracle.  Other workloads: gemv, prefill,
+prefill_w4a4, dequant, moe (one layer), deltanet.
 
 `value` is device-timed (CUDA events, max over ranks) with weights resident
 and the step replayed from a CUDA graph; `e2e` times the public Python API
-(nvfp4_linear_forward over ctypes) with the step's activations copied from
-pinned host memory and its outputs copied back.  `--impl reference` times the
-reference's CPU path (the oracle port of nvfp4_matvec, all host threads) on a
-bounded sample of the same workload.  N > 1: one process per GPU (torchrun);
-the GEMV does not shard, so each rank runs an independent replica.
+(ctypes into libnvfp4.so) with the step's activations copied from pinned host
+memory and its outputs copied back.  `--impl reference` times the
+reference's CPU path (the oracle port, all host threads) on a bounded sample
+of the same workload.  N > 1: one process per GPU (torchrun); workloads that
+do not shard (gemv, prefill) run independent replicas.
 """
 from __future__ import annotations
 
@@ -658,23 +663,27 @@ class DeltaNetBench:
 # Workload: 48-layer stack of the MoE layer, expert-parallel over the ranks.
 # ---------------------------------------------------------------------------
 class EPStackBench:
+    """Config 4: a 48-layer stack of the config-3 MoE layer, h = h + MoE(h)
+    (the residual add is fused in the combine kernel), expert-parallel over
+    the ranks.  A step is one pass of the stack over the global token batch."""
+
     name = "ep"
     unit = "tokens/s"
-    graphable = False  # set per batch: True with the fixed-capacity exchange
+    graphable = False  # set per batch: True with the fixed-capacity or peer exchange
     scaling = "strong"  # the global token batch is fixed; experts and tokens split over GPUs
 
     @staticmethod
-    def describe(tokens, layers=48, world=1, exchange="nccl"):
+    def describe(tokens, layers=48, world=1, exchange="p2p"):
         how = ("NCCL all-to-all dispatch/combine" if exchange == "nccl" else
                "device-initiated dispatch/combine through peer memory (NVLink stores and loads "
                "issued by the kernels, cross-GPU flags)")
-        return (f"{layers}-layer stack of pre-norm MoE blocks h += MoE(RMSNorm(h)) (128 "
-                f"experts, top-8, hidden 2048, intermediate 768, NVFP4 experts; the "
-                f"residual add is fused in the combine); expert-parallel over {world} GPU(s) "
-                f"({MOE_E // world} experts each) with {how}; "
-                f"{tokens} bf16 tokens ~N(0,1) per step ({tokens // world} per GPU)")
+        return (f"{layers}-layer stack of MoE FFN layers h = h + MoE(h) (128 experts, top-8, "
+                f"hidden 2048, intermediate 768, NVFP4 experts; the residual add is fused in "
+                f"the combine); expert-parallel over {world} GPU(s) ({MOE_E // world} experts "
+                f"each) with {how}; {tokens} bf16 tokens ~N(0,1) per step "
+                f"({tokens // world} per GPU)")
 
-    def __init__(self, device, seed=0, tokens=64, layers=48, exchange="nccl"):
+    def __init__(self, device, seed=0, tokens=64, layers=48, exchange="p2p"):
         import torch
         import torch.distributed as dist
         from nvfp4.ep import EPMoELayer
@@ -685,11 +694,14 @@ class EPStackBench:
         rank = dist.get_rank() if dist.is_initialized() else 0
         if tokens % world:
             raise ValueError("global token count must divide by the number of GPUs")
+        self.world, self.rank = world, rank
         self.T = tokens
         self.T_local = tokens // world
-        epr = MOE_E // world
+        self.n_layers = layers
+        self.epr = epr = MOE_E // world
+        self.exchange_mode = exchange
         self.workload = self.describe(tokens, layers, world, exchange)
-        self.layers = []
+        self.layers, self.local_w = [], []
         # One set of peer windows for the whole stack: the layers run one
         # after another, so layer l+1 reuses layer l's receive rows (L2-resident).
         windows = None
@@ -704,23 +716,30 @@ class EPStackBench:
             wd = synthetic_local_experts(epr, seed=seed + 7919 * l + 104729 * rank, device=device)
             wd["router"] = router
             local = MoEWeights.from_dict(wd, device)
+            self.local_w.append(local)
             self.layers.append(EPMoELayer(local, router, top_k=MOE_K, num_experts=MOE_E,
                                           exchange=exchange, max_tokens=self.T_local,
                                           windows=windows))
-        self.x = torch.randn((self.T_local, MOE_H), device=device).to(torch.bfloat16)
-        # Fixed-capacity exchange (no host-side counts) for small batches: the
-        # whole step, NCCL calls included, is then replayed from a CUDA graph.
+        g = torch.Generator(device=device)
+        g.manual_seed(77 + rank)
+        self.x = torch.randn((self.T_local, MOE_H), generator=g, device=device).to(torch.bfloat16)
         if exchange == "p2p":
             # router (2), dispatch, wait, permutation, 2 expert GEMVs, done signal, combine
             self.graphable = True
             self.exchange = "peer memory, CUDA graph"
             self.launches_per_step = layers * 9
         else:
+            # Fixed-capacity exchange (no host-side counts) for small batches:
+            # the whole step, NCCL calls included, is replayed from a CUDA graph.
             self.graphable = self.layers[0].uses_static(self.T_local)
             self.exchange = "fixed capacity, CUDA graph" if self.graphable else "variable counts"
             self.launches_per_step = layers * 10
         self.sets = 1
         self.dominant_bytes = None
+        # Expert weight bytes one GPU streams per layer: its experts that at
+        # least one of the T tokens routes to (expectation under uniform routing).
+        self.touched_per_gpu = epr * (1.0 - (1.0 - MOE_K / MOE_E) ** tokens)
+        self.layer_bytes = self.touched_per_gpu * moe_expert_bytes()
         self.config = {"workload": self.workload, "layers": layers, "global_tokens": tokens,
                        "experts_per_gpu": epr, "parallelism": f"ep{world}",
                        "exchange": self.exchange,
@@ -728,16 +747,95 @@ class EPStackBench:
                              f"expert weights per GPU per step"}
 
     def run_step(self, i):
-        torch = self.torch
         h = self.x
         for L in self.layers:
-            hf = h.float()
-            hn = (hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + 1e-6)).to(torch.bfloat16)
-            h = L(hn, residual=h)
+            h = L(h, residual=h)
         self.out = h
 
     def units(self, steps):
         return self.T_local * steps  # per rank; the job total is this times the world size
+
+    def roofline(self, ms_per_step, peaks):
+        """Layer-level roofline: the expert weight bytes one GPU must stream
+        per layer over the average layer time of the timed region."""
+        layer_s = ms_per_step / 1e3 / self.n_layers
+        achieved = self.layer_bytes / layer_s / 1e9
+        return {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"], "traffic": load_traffic(self.name),
+                "kernel": (f"one expert-parallel MoE layer ({self.launches_per_step // self.n_layers}"
+                           f" launches), per GPU"),
+                "algorithmic_bytes_per_launch": self.layer_bytes,
+                "algorithmic_bytes_note": (
+                    f"{self.touched_per_gpu:.2f} of this GPU's {self.epr} experts touched by "
+                    f"{self.T} tokens x top-{MOE_K} (expectation, uniform routing) x "
+                    f"{moe_expert_bytes()} bytes per expert"),
+                "avg_launch_us": layer_s * 1e6,
+                "timing": "average layer time of the timed region (CUDA events)",
+                "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs, copy burst)"}
+
+    def parity(self):
+        """Layer 0 of the stack on this step's tokens, every rank's tokens,
+        against the CPU oracle's MoE layer (the checker; outside every timed
+        region).  Rank 0 gathers the tokens, the outputs and layer 0's experts
+        from all ranks and evaluates the oracle on all tokens; router
+        near-ties (a gap < 1e-5 among the k+1 largest probabilities) replay
+        the GPU's expert choice."""
+        import numpy as np
+        import torch
+        import torch.distributed as dist
+
+        world, rank = self.world, self.rank
+        L0 = self.layers[0]
+        if self.exchange_mode == "p2p":
+            y = L0.forward_p2p(self.x, out=torch.empty((self.T_local, MOE_H),
+                                                       dtype=torch.float32, device=self.x.device))
+            out_dtype = "f32"
+        else:
+            y = L0(self.x)
+            out_dtype = "bf16"
+        torch.cuda.synchronize()
+
+        def gather(t):
+            t = t.contiguous()
+            if world == 1:
+                return t
+            out = torch.empty((world * t.shape[0],) + tuple(t.shape[1:]), dtype=t.dtype,
+                              device=t.device)
+            dist.all_gather_into_tensor(out, t)
+            return out
+
+        u8 = lambda t: t.view(torch.uint8) if t.dtype != torch.uint8 else t
+        w = self.local_w[0]
+        xs, ys = gather(self.x), gather(y)
+        full = {"gu_w": gather(w.gate_up), "gu_sf": gather(u8(w.gate_up_scale)),
+                "gu_ws2": gather(w.gate_up_scale_2), "dn_w": gather(w.down),
+                "dn_sf": gather(u8(w.down_scale)), "dn_ws2": gather(w.down_scale_2)}
+        ids_gpu = L0.backend.route(xs)[0] if rank == 0 else None
+        torch.cuda.synchronize()
+        if rank != 0:
+            return None
+        from oracle import oracle as O
+
+        wd = {k: v.cpu().numpy() for k, v in full.items()}
+        wd["router"] = w.router.float().cpu().numpy()
+        x = xs.float().cpu().numpy()
+        got = ys.float().cpu().numpy()
+        ids_gpu = ids_gpu.cpu().numpy()
+        cores = O.host_cores()
+        _, probs = O.router(x, wd["router"])
+        srt = -np.sort(-probs, axis=1)[:, : MOE_K + 1]
+        ties = (srt[:, :-1] - srt[:, 1:]).min(axis=1) < 1e-5
+        ref, ref_ids, _ = O.moe(x, wd, top_k=MOE_K, n_threads=cores)
+        flips = [i for i in range(len(x)) if not np.array_equal(ref_ids[i], ids_gpu[i])]
+        unexplained = [i for i in flips if not ties[i]]
+        if flips:
+            ref, _, _ = O.moe(x, wd, top_k=MOE_K, force_ids=ids_gpu, n_threads=cores)
+        ref64 = ref.astype(np.float64)
+        err = float(np.abs(got - ref64).max() / np.sqrt(np.mean(ref64 * ref64)))
+        return {"max_err_over_rms": err, "tol": 2e-2, "ok": bool(err <= 2e-2 and not unexplained),
+                "layer": 0, "tokens": int(len(x)), "out_dtype": out_dtype,
+                "near_tie_tokens_replayed": len(flips), "routing_mismatches": len(unexplained),
+                "oracle": "CPU oracle MoE layer (C), all tokens of every rank"}
 
     def e2e_setup(self):
         torch = self.torch
@@ -761,7 +859,7 @@ class EPStackBench:
         def run():
             O.moe(x, wd, top_k=MOE_K, n_threads=threads)
 
-        n_layers = len(self.layers) if hasattr(self, "layers") else 48
+        n_layers = getattr(self, "n_layers", 48)
         desc = (f"{n_tok} tokens through one layer, reported per layer-token and divided by "
                 f"the layer count {n_layers} (oracle cost is linear in tokens and layers)")
         return run, float(n_tok) / n_layers, desc
@@ -830,6 +928,30 @@ def time_cpu(run, units, reps_target_s=10.0, max_reps=50):
     return units * n / el, n, el
 
 
+def cpu_baselines(wl_cls, wl, target_s=10.0):
+    """The oracle port of the reference's CPU loop on this host, timed twice:
+    single-thread (the reference's own form, nvfp4/deltanet.mojo:569-584, one
+    core) and with OpenMP over output rows on every host core.  The timing
+    build is compiled for this host (-O3 -march=native, still without FMA
+    contraction) when a compiler is present."""
+    from oracle import oracle as O
+
+    build = O.use_native_build()
+    cores = O.host_cores()
+    out = {}
+    for label, threads in (("single_thread", 1), ("openmp", cores)):
+        res = wl_cls.cpu_sample(wl, threads)
+        run, units, desc = res[:3]
+        used = res[3] if len(res) > 3 else threads
+        v, n, el = time_cpu(run, units, reps_target_s=target_s)
+        out[label] = {"value": v, "cores": used, "sample": f"{desc}; {n} passes in {el:.1f} s"}
+        if used == 1 and label == "single_thread" and len(res) > 3:
+            break  # the sample is single-threaded by construction
+    best = out.get("openmp", out["single_thread"])
+    return {"value": best["value"], "unit": wl_cls.unit, "cores": best["cores"], "kind": "port",
+            "sample": best["sample"], "build": build, **out}
+
+
 def run_reference(args, world, rank):
     """CPU reference arm: the oracle port of the reference's CPU path."""
     if rank != 0:
@@ -837,9 +959,12 @@ def run_reference(args, world, rank):
     from oracle import oracle as O
 
     wl_cls = WORKLOADS[args.workload]
+    build = O.use_native_build()
     cores = O.host_cores()
     # Build only what the CPU sample needs (no GPU use).
     wl = wl_cls.__new__(wl_cls)
+    if args.workload == "ep":
+        wl.n_layers = args.layers
     res = wl_cls.cpu_sample(wl, cores)
     run, units, desc = res[:3]
     cores = res[3] if len(res) > 3 else cores
@@ -862,7 +987,7 @@ def run_reference(args, world, rank):
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": wdesc, "sample": desc},
         "cpu_baseline": {"value": value, "unit": wl_cls.unit, "cores": cores, "kind": "port",
-                         "sample": desc},
+                         "sample": desc, "build": build},
         "e2e": {"value": value, "unit": wl_cls.unit, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -870,21 +995,135 @@ def run_reference(args, world, rank):
     return 0
 
 
+def time_dominant(wl, stream, steps, warmup):
+    """Average duration of one dominant launch: a CUDA graph holding only the
+    dominant launches of each weight set, replayed back to back on the
+    launching stream and timed with CUDA events (no host gaps)."""
+    import torch
+
+    dg = []
+    n_dom = 1
+    for s in range(getattr(wl, "sets", 1)):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            n_dom = wl.run_dominant(s)
+        dg.append(g)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for i in range(warmup):
+            dg[i % len(dg)].replay()
+        d0 = torch.cuda.Event(enable_timing=True)
+        d1 = torch.cuda.Event(enable_timing=True)
+        d0.record(stream)
+        for i in range(steps):
+            dg[i % len(dg)].replay()
+        d1.record(stream)
+    torch.cuda.synchronize()
+    ms = d0.elapsed_time(d1) / (steps * n_dom)
+    del dg
+    return ms
+
+
+def dominant_roofline(wl, dom_ms, peaks):
+    traffic = load_traffic(wl.name)
+    if getattr(wl, "bound", "hbm") == "tensor":
+        achieved = wl.dominant_bytes / (dom_ms / 1e3) / 1e12
+        scale = getattr(wl, "peak_scale", 1.0)
+        peak = peaks["bf16_tflops"] * scale
+        src = (f"{peaks['source']} (MEASURED_PEAKS.json bf16_tflops, cuBLAS bf16 burst)"
+               if scale == 1.0 else
+               f"{scale:g} x {peaks['source']} bf16_tflops (MEASURED_PEAKS.json, cuBLAS bf16 "
+               f"burst): dense FP4 is {scale:g} x dense BF16 on B200; no FP4 peak is measured")
+        return {"bound": "tensor", "achieved": achieved, "peak": peak,
+                "unit": "TFLOP/s", "frac": achieved / peak,
+                "traffic": traffic, "kernel": wl.dominant_name,
+                "algorithmic_flop_per_launch": wl.dominant_bytes,
+                "avg_launch_us": dom_ms * 1e3, "peak_source": src}
+    achieved = wl.dominant_bytes / (dom_ms / 1e3) / 1e9
+    return {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
+            "kernel": wl.dominant_name, "algorithmic_bytes_per_launch": wl.dominant_bytes,
+            "avg_launch_us": dom_ms * 1e3,
+            "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs, copy burst)"}
+
+
+def capture_step_graphs(wl, stream):
+    import torch
+
+    graphs = []
+    for s in range(getattr(wl, "sets", 1)):
+        graphs.append(torch.cuda.CUDAGraph())
+        with torch.cuda.graph(graphs[-1], stream=stream):
+            wl.run_step(s)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):  # a first replay outside the timed region
+        for g in graphs:
+            g.replay()
+    torch.cuda.synchronize()
+    return graphs
+
+
+def time_steps(wl, graphs, stream, steps, start=0):
+    import torch
+
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for i in range(start, start + steps):
+            if graphs:
+                graphs[i % len(graphs)].replay()
+            else:
+                wl.run_step(i)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1)
+
+
+def secondary_line(cls, device, peaks, steps, warmup):
+    """A single-GPU workload measured beside the headline one (same process,
+    same GPU): its sweep throughput and its dominant launch's roofline."""
+    import torch
+
+    wl = cls(device)
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        for i in range(warmup):
+            wl.run_step(i)
+    torch.cuda.synchronize()
+    graphs = capture_step_graphs(wl, stream)
+    t_ms = time_steps(wl, graphs, stream, steps)
+    dom_ms = time_dominant(wl, stream, steps, warmup)
+    out = {"workload": wl.workload, "value": wl.units(steps) / (t_ms / 1e3), "unit": wl.unit,
+           "ms_per_step": t_ms / steps, "steps": steps,
+           "roofline": dominant_roofline(wl, dom_ms, peaks), "l2": wl.config.get("l2")}
+    del graphs, wl
+    gc.collect()
+    torch.cuda.empty_cache()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="gemv", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="ep", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--no-parity", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="skip the decode GEMV and prefill lines measured beside the EP stack")
     ap.add_argument("--tokens", type=int, default=None,
                     help="MoE: tokens per step (default 4096); EP stack: global tokens (default "
                          "64); DeltaNet: sequences per step (default 4)")
     ap.add_argument("--layers", type=int, default=48, help="EP stack: number of MoE layers")
-    ap.add_argument("--exchange", default="nccl", choices=["nccl", "p2p"],
-                    help="EP stack: NCCL all-to-all or device-initiated peer-memory exchange")
+    ap.add_argument("--exchange", default="p2p", choices=["nccl", "p2p"],
+                    help="EP stack: device-initiated peer-memory exchange or NCCL all-to-all")
+    ap.add_argument("--clock-window", type=float, default=0.6,
+                    help="seconds of untimed step replays before the timed steps, inside the "
+                         "clock-sampling window (so the sampler sees the GPU under this load)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.tokens is None:
@@ -916,62 +1155,28 @@ def main():
 
     graphs = None
     if not args.no_graph and getattr(wl, "graphable", True):
-        graphs = []
-        for s in range(getattr(wl, "sets", 1)):
-            graphs.append(torch.cuda.CUDAGraph())
-            with torch.cuda.graph(graphs[-1], stream=stream):
-                wl.run_step(s)
-        torch.cuda.synchronize()
-        # A first replay outside the timed region.
-        with torch.cuda.stream(stream):
-            for gi in range(len(graphs)):
-                graphs[gi].replay()
-        torch.cuda.synchronize()
+        graphs = capture_step_graphs(wl, stream)
 
-    # Dominant-kernel launch duration: a CUDA graph holding only the dominant
-    # launches of each weight set, replayed back to back on the launching
-    # stream and timed with CUDA events (no host gaps between launches).
     dom_ms = None
     if hasattr(wl, "run_dominant"):
-        dg = []
-        for s in range(getattr(wl, "sets", 1)):
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=stream):
-                n_dom = wl.run_dominant(s)
-            dg.append(g)
-        torch.cuda.synchronize()
-        with torch.cuda.stream(stream):
-            for i in range(args.warmup):
-                dg[i % len(dg)].replay()
-            d0 = torch.cuda.Event(enable_timing=True)
-            d1 = torch.cuda.Event(enable_timing=True)
-            d0.record(stream)
-            for i in range(args.steps):
-                dg[i % len(dg)].replay()
-            d1.record(stream)
-        torch.cuda.synchronize()
-        dom_ms = d0.elapsed_time(d1) / (args.steps * n_dom)
-        del dg, g
+        dom_ms = time_dominant(wl, stream, args.steps, args.warmup)
 
+    # Untimed replays fill the clock-sampling window before the timed steps;
+    # every rank runs the same count (the peer exchange steps in lockstep).
+    barrier(world)
+    one = time_steps(wl, graphs, stream, 2) / 2
+    n_pre = int(max_over_ranks(float(math.ceil(args.clock_window * 1e3 / max(one, 1e-3))), world))
     barrier(world)
     torch.cuda.synchronize()
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.3)
-    ev0 = torch.cuda.Event(enable_timing=True)
-    ev1 = torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        ev0.record(stream)
-        for i in range(args.steps):
-            if graphs:
-                graphs[i % len(graphs)].replay()
-            else:
-                wl.run_step(i)
-        ev1.record(stream)
-    torch.cuda.synchronize()
-    # Keep the GPU loaded a little longer so the sampler sees the clocks.
-    t_ms = ev0.elapsed_time(ev1)
+    if n_pre:
+        time_steps(wl, graphs, stream, n_pre)
+    t_ms = time_steps(wl, graphs, stream, args.steps)
     clk = clocks.stop()
+    clk["window"] = (f"{n_pre} untimed steps ({n_pre * one / 1e3:.2f} s) then the "
+                     f"{args.steps} timed steps ({t_ms / 1e3:.3f} s)")
     barrier(world)
     t_ms = max_over_ranks(t_ms, world)
     ms_per_step = t_ms / args.steps
@@ -997,40 +1202,24 @@ def main():
 
     roof = None
     if dom_ms and wl.dominant_bytes:
-        traffic = load_traffic(wl.name)
-        if getattr(wl, "bound", "hbm") == "tensor":
-            achieved = wl.dominant_bytes / (dom_ms / 1e3) / 1e12
-            scale = getattr(wl, "peak_scale", 1.0)
-            peak = peaks["bf16_tflops"] * scale
-            src = (f"{peaks['source']} (MEASURED_PEAKS.json bf16_tflops, cuBLAS bf16 burst)"
-                   if scale == 1.0 else
-                   f"{scale:g} x {peaks['source']} bf16_tflops (MEASURED_PEAKS.json, cuBLAS bf16 "
-                   f"burst): dense FP4 is {scale:g} x dense BF16 on B200; no FP4 peak is measured")
-            roof = {"bound": "tensor", "achieved": achieved, "peak": peak,
-                    "unit": "TFLOP/s", "frac": achieved / peak,
-                    "traffic": traffic, "kernel": wl.dominant_name,
-                    "algorithmic_flop_per_launch": wl.dominant_bytes,
-                    "avg_launch_us": dom_ms * 1e3, "peak_source": src}
-        else:
-            achieved = wl.dominant_bytes / (dom_ms / 1e3) / 1e9
-            roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                    "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
-                    "kernel": wl.dominant_name, "algorithmic_bytes_per_launch": wl.dominant_bytes,
-                    "avg_launch_us": dom_ms * 1e3,
-                    "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs, copy burst)"}
+        roof = dominant_roofline(wl, dom_ms, peaks)
+    elif hasattr(wl, "roofline"):
+        roof = wl.roofline(ms_per_step, peaks)
+
+    parity = None
+    if hasattr(wl, "parity") and not args.no_parity:
+        parity = wl.parity()
+
+    secondary = None
+    if args.workload == "ep" and world == 1 and not args.no_secondary:
+        secondary = {}
+        graphs = None
+        for key, cls in (("gemv", GemvSweep), ("prefill", PrefillSweep)):
+            secondary[key] = secondary_line(cls, device, peaks, max(args.steps, 20), args.warmup)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        from oracle import oracle as O
-
-        cores = O.host_cores()
-        res = wl.cpu_sample(cores)
-        run, units, desc = res[:3]
-        cores = res[3] if len(res) > 3 else cores
-        v, n, el = time_cpu(run, units)
-        extra = ", OpenMP over output rows" if cores > 1 else ""
-        cpu = {"value": v, "unit": wl.unit, "cores": cores, "kind": "port",
-               "sample": f"{desc}; {n} passes in {el:.1f} s{extra}"}
+        cpu = cpu_baselines(type(wl), wl)
 
     if rank == 0:
         line = {
@@ -1045,6 +1234,10 @@ def main():
                     "d2h_bytes_per_step": wl.d2h},
             "clocks": clk, "gpu_launches": wl.launches_per_step * args.steps,
         }
+        if parity is not None:
+            line["parity"] = parity
+        if secondary:
+            line["secondary"] = secondary
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
@@ -1053,6 +1246,8 @@ def main():
         # group is destroyed, or the exit waits for them forever.
         torch.cuda.synchronize()
         graphs = None
+        if getattr(wl, "windows", None) is not None:
+            wl.windows.close()  # collective: every rank unmaps, then each frees its own
         wl = None
         gc.collect()
         torch.cuda.synchronize()

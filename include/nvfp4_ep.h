@@ -17,8 +17,12 @@
  * cudaMalloc'd and zeroed) and maps the other ranks' windows through CUDA
  * IPC handles exchanged by the host (any transport: torch.distributed, a
  * file).  A window holds control words (one dispatch and one done flag per
- * source rank, an epoch, an error word), the received rows and expert ids
- * ([world][max_rows]) and the expert outputs ([world][max_rows] fp32).
+ * source rank, an epoch, an error word, the row count of each source rank's
+ * last dispatch), then room for world * max_rows received rows and expert ids
+ * and as many fp32 expert-output rows.  In a step of T tokens the rows of
+ * source rank p sit at p*T*k .. (p+1)*T*k - 1, so every rank must step with
+ * the same T: the wait (step 3) checks it and sets NVFP4_EP_ERR_SHAPE when a
+ * peer's row count differs (that step's results are then meaningless).
  *
  * One layer step on rank r (all ranks run the same steps with the same T):
  *   1. route its T tokens (softmax top-k over all E experts);
@@ -33,6 +37,9 @@
  *   6. combine: wait for every done flag, then
  *      y[t] = sum_j w[t,j] * out_{e_j / (E/world)}[r*T*k + t*k + j] (+ residual)
  *      with fp32 sums in j order, loading the rows from the peers' windows.
+ *      Each block of the combine waits on its own: when the error word has
+ *      NVFP4_EP_ERR_DONE_TIMEOUT, y is undefined (blocks that gave up leave
+ *      their part untouched, blocks that saw a late flag write theirs).
  * Flags carry a step counter kept in each window, so nothing is reset
  * between steps and a step can be captured in a CUDA graph.
  *
@@ -62,7 +69,9 @@ extern "C" {
 /* Error word bits (nvfp4_ep_p2p_error). */
 #define NVFP4_EP_ERR_DISPATCH_TIMEOUT 0x1u /* a dispatch flag did not arrive */
 #define NVFP4_EP_ERR_DONE_TIMEOUT 0x2u     /* a done flag did not arrive */
-/* bit 8 + p set: rank p's flag was missing (bits 8..15, one per rank) */
+#define NVFP4_EP_ERR_SHAPE 0x4u            /* a peer dispatched a different T * k */
+/* bit 8 + p set: rank p's flag was missing, or its row count differed
+ * (bits 8..15, one per rank) */
 
 typedef struct nvfp4_ep_peers {
   int32_t rank;

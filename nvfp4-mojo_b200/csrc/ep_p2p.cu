@@ -35,6 +35,7 @@ struct EpCtrl {
   uint32_t epoch;                     // steps this rank has entered (advanced by the wait)
   uint32_t error;                     // NVFP4_EP_ERR_* | missing-rank mask << 8
   uint32_t blocks_done;               // dispatch: blocks finished (last block resets it)
+  uint32_t rows_from[kMaxWorld];      // [source rank]: T*k of its last dispatch here
 };
 
 struct WinLayout {
@@ -147,19 +148,28 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(PeerTable P, const int
   __syncthreads();
   if (s_last) {
     if (threadIdx.x == 0) own->blocks_done = 0;  // the next step's launch starts after this one
+    // The row count goes out with the flag (the release orders it first), so
+    // that every owner can check that all ranks step with the same T.
+    if (threadIdx.x < P.world) ctrl_of(s_win[threadIdx.x])->rows_from[P.rank] = (uint32_t)R;
     __threadfence_system();
     if (threadIdx.x < P.world) st_release_sys(&ctrl_of(s_win[threadIdx.x])->flag_dispatch[P.rank], step);
   }
 }
 
-// Step 3: one warp; lane p waits for rank p's dispatch flag, then the step
-// counter advances (also after a timeout, which the error word records).
+// Step 3: one warp; lane p waits for rank p's dispatch flag and checks that
+// rank p stored as many rows as this rank did (the fixed row layout needs the
+// same T on every rank), then the step counter advances (also after a timeout
+// or a shape mismatch, which the error word records).
 __global__ void ep_wait_dispatch_kernel(PeerTable P) {
   EpCtrl *own = ctrl_of(win_at(P, P.rank));
   const int lane = threadIdx.x;
   const uint32_t step = __ldcg(&own->epoch) + 1;
-  if (lane < P.world && !wait_flag(&own->flag_dispatch[lane], step, P.timeout_ns))
-    atomicOr(&own->error, NVFP4_EP_ERR_DISPATCH_TIMEOUT | (1u << (8 + lane)));
+  if (lane < P.world) {
+    if (!wait_flag(&own->flag_dispatch[lane], step, P.timeout_ns))
+      atomicOr(&own->error, NVFP4_EP_ERR_DISPATCH_TIMEOUT | (1u << (8 + lane)));
+    else if (ld_acquire_sys(&own->rows_from[lane]) != ld_acquire_sys(&own->rows_from[P.rank]))
+      atomicOr(&own->error, NVFP4_EP_ERR_SHAPE | (1u << (8 + lane)));
+  }
   __syncwarp();
   if (lane == 0) own->epoch = step;
 }
@@ -287,9 +297,9 @@ int check_step(const nvfp4_ep_peers *p, int64_t T, int32_t k, int32_t epr) {
   if (rc) return rc;
   if (T < 0 || k < 1 || k > 32 || epr < 1 || (int64_t)epr * p->world > 65536)
     return fail(NVFP4_ERR_INVALID_ARG, "bad token count, top_k or experts per rank");
-  if (T * k > p->max_rows)
-    return fail(NVFP4_ERR_INVALID_ARG, "%lld slots exceed the windows' %lld rows per rank",
-                (long long)(T * k), (long long)p->max_rows);
+  if (T > p->max_rows / k)
+    return fail(NVFP4_ERR_INVALID_ARG, "%lld tokens x top-%d exceed the windows' %lld rows per rank",
+                (long long)T, (int)k, (long long)p->max_rows);
   return NVFP4_OK;
 }
 

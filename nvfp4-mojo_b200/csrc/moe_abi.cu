@@ -300,13 +300,17 @@ int run_experts(const nvfp4_moe_desc &d, const nvfp4_moe_weights &w, const uint1
 
 using namespace nvfp4;
 
+// Token counts are bounded by T * top_k <= 2^24 slots, tested as a division so
+// that no product of a caller's count can wrap.
+bool tokens_ok(const nvfp4_moe_desc &d, int64_t T) { return T >= 0 && T <= (1 << 24) / d.top_k; }
+
 extern "C" size_t nvfp4_moe_workspace_size(const nvfp4_moe_desc *d, int64_t T) {
-  if (check_desc(d) || T < 0) return 0;
+  if (check_desc(d) || !tokens_ok(*d, T)) return 0;
   return forward_layout(*d, T).total;
 }
 
 extern "C" size_t nvfp4_moe_experts_workspace_size(const nvfp4_moe_desc *d, int64_t R) {
-  if (check_desc(d) || R < 0) return 0;
+  if (check_desc(d) || R < 0 || R > (1 << 24)) return 0;
   return experts_layout(*d, R).total;
 }
 
@@ -387,7 +391,7 @@ extern "C" int nvfp4_ep_dispatch_plan(const int32_t *topk_ids, int64_t T, int32_
                                       int32_t *send_counts, int32_t *send_token,
                                       int32_t *send_expert, int32_t *slot_pos, void *stream) {
   if (T < 0 || k <= 0 || k > 32 || experts_per_rank <= 0 || world <= 0 || world > 64 ||
-      T * k > (1 << 24))
+      T > (1 << 24) / k)
     return fail(NVFP4_ERR_INVALID_ARG, "bad dispatch-plan shape");
   if (!topk_ids || !send_counts || !send_token || !send_expert || !slot_pos)
     return fail(NVFP4_ERR_INVALID_ARG, "null dispatch-plan pointer");
@@ -415,8 +419,8 @@ extern "C" int nvfp4_ep_dispatch_padded(const int32_t *send_counts, const int32_
                                         const void *x, int64_t row_bytes, void *send_rows,
                                         int32_t *send_expert_padded, int32_t *slot_padded,
                                         void *stream) {
-  if (T < 0 || k <= 0 || k > 32 || world <= 0 || world > 64 || cap < 0 || T * k > (1 << 24) ||
-      (int64_t)world * cap > (1 << 24) || row_bytes <= 0 || row_bytes % 16)
+  if (T < 0 || k <= 0 || k > 32 || world <= 0 || world > 64 || cap < 0 || T > (1 << 24) / k ||
+      cap > (1 << 24) / world || row_bytes <= 0 || row_bytes % 16)
     return fail(NVFP4_ERR_INVALID_ARG, "bad padded-dispatch shape");
   if (cap < T * k)
     return fail(NVFP4_ERR_INVALID_ARG, "capacity %lld below the %lld slots of this rank",
@@ -482,7 +486,7 @@ int moe_forward_impl(const nvfp4_moe_desc *d, const nvfp4_moe_weights *w,
     if ((rc = check_desc(&ds))) return rc;
     if ((rc = check_weights(shared))) return rc;
   }
-  if (T < 0 || T * d->top_k > (1 << 24)) return fail(NVFP4_ERR_INVALID_ARG, "bad token count");
+  if (!tokens_ok(*d, T)) return fail(NVFP4_ERR_INVALID_ARG, "bad token count");
   if (T == 0) return NVFP4_OK;
   if (!x || !y || !ws) return fail(NVFP4_ERR_INVALID_ARG, "null activation, output or workspace");
   if (y_dtype != NVFP4_DTYPE_F32 && y_dtype != NVFP4_DTYPE_BF16)
@@ -549,7 +553,7 @@ extern "C" int nvfp4_moe_forward(const nvfp4_moe_desc *d, const nvfp4_moe_weight
 
 extern "C" size_t nvfp4_moe_shared_workspace_size(const nvfp4_moe_desc *d,
                                                   int32_t shared_intermediate, int64_t T) {
-  if (check_desc(d) || T < 0) return 0;
+  if (check_desc(d) || !tokens_ok(*d, T)) return 0;
   const nvfp4_moe_desc ds = shared_desc(*d, shared_intermediate);
   if (check_desc(&ds)) return 0;
   return forward_layout(*d, T).total + shared_layout(ds, T).total;
@@ -636,7 +640,7 @@ int check_ep_desc(const nvfp4_moe_desc *d, const nvfp4_ep_peers *p) {
 
 extern "C" size_t nvfp4_ep_p2p_workspace_size(const nvfp4_moe_desc *d, const nvfp4_ep_peers *p,
                                               int64_t T) {
-  if (check_ep_desc(d, p) || T < 0) return 0;
+  if (check_ep_desc(d, p) || T < 0 || T > p->max_rows / d->top_k) return 0;
   return ep_p2p_layout(*d, p->world, T).total;
 }
 
@@ -649,7 +653,7 @@ extern "C" int nvfp4_ep_p2p_forward(const nvfp4_moe_desc *d, const nvfp4_moe_wei
   if (rc) return rc;
   if ((rc = check_weights(local))) return rc;
   if (!local->router) return fail(NVFP4_ERR_INVALID_ARG, "null router pointer");
-  if (T < 0 || T * d->top_k > p->max_rows)
+  if (T < 0 || T > p->max_rows / d->top_k)
     return fail(NVFP4_ERR_INVALID_ARG, "bad token count for the windows' capacity");
   if ((T > 0 && (!x || !y)) || !ws)
     return fail(NVFP4_ERR_INVALID_ARG, "null activation, output or workspace");

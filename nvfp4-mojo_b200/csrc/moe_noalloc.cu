@@ -68,7 +68,8 @@ extern "C" int nvfp4_moe_forward_noalloc(const nvfp4_moe_desc *desc,
                                          int32_t *topk_ids, float *topk_w, void *stream) {
   NVFP4_ABI_RANGE();
   if (!desc) return fail(NVFP4_ERR_INVALID_ARG, "null MoE descriptor");
-  if (T < 0) return fail(NVFP4_ERR_INVALID_ARG, "bad token count");
+  if (desc->top_k <= 0 || T < 0 || T > (1 << 24) / desc->top_k)
+    return fail(NVFP4_ERR_INVALID_ARG, "bad token count or top_k");
   const size_t need = nvfp4_moe_workspace_size(desc, T);
   if (need == 0 && T > 0) return fail(NVFP4_ERR_INVALID_ARG, "invalid MoE descriptor");
   if (need > (size_t)NVFP4_NOALLOC_SCRATCH_BYTES)

@@ -133,6 +133,7 @@ EP_MAX_WORLD = 8
 EP_HANDLE_BYTES = 64
 EP_ERR_DISPATCH_TIMEOUT = 0x1
 EP_ERR_DONE_TIMEOUT = 0x2
+EP_ERR_SHAPE = 0x4
 
 
 class EpPeers(ctypes.Structure):

@@ -32,6 +32,27 @@ def build() -> Path:
     return _LIB_PATH
 
 
+def use_native_build() -> str:
+    """Switches this process to the timing build of the same C sources,
+    compiled for this host (-O3 -march=native, no FMA contraction), building
+    it on first use; falls back to the portable build when no compiler is
+    present.  Called by the CPU-baseline leg of bench.py only.  Returns a
+    description of the build in use."""
+    global _lib, _LIB_PATH
+    import tempfile
+
+    # A fresh path per process: a build made on another host is never reused.
+    native = Path(tempfile.mkdtemp(prefix="oracle-native-")) / "liboracle_native.so"
+    try:
+        subprocess.run(["make", "-s", "-C", str(_HERE), "native", f"NATIVE_LIB={native}"],
+                       check=True, capture_output=True, timeout=120)
+    except (OSError, subprocess.SubprocessError):
+        return "portable build (-O3, no -march=native): the native build failed on this host"
+    _LIB_PATH, _lib = native, None
+    lib()
+    return "gcc -O3 -march=native -ffp-contract=off -fopenmp, built on this host"
+
+
 def lib():
     global _lib
     if _lib is None:

@@ -84,6 +84,36 @@ def test_shared_expert_and_stack_validation_without_gpu():
     assert L.nvfp4_stack_rows(srcs, rows, 1, 0, 16, None) == _lib.NVFP4_ERR_INVALID_ARG
 
 
+def test_token_counts_that_would_wrap_are_refused():
+    """T * top_k is bounded by 2^24 slots without forming the product, so a
+    count near 2^61 cannot wrap into a small, accepted layer."""
+    from nvfp4 import _lib
+
+    L = _lib.load()
+    desc = _lib.MoEDesc(128, 8, 2048, 768, 1)
+    huge = (1 << 61) + 1
+    assert L.nvfp4_moe_workspace_size(ctypes.byref(desc), huge) == 0
+    assert L.nvfp4_moe_workspace_size(ctypes.byref(desc), (1 << 21) + 1) == 0
+    assert L.nvfp4_moe_workspace_size(ctypes.byref(desc), 1 << 21) > 0
+    assert L.nvfp4_moe_shared_workspace_size(ctypes.byref(desc), 1024, huge) == 0
+    assert L.nvfp4_moe_experts_workspace_size(ctypes.byref(desc), huge) == 0
+    w = _lib.MoEWeightPtrs(16, 16, 16, None, None, 16, 16, None, None)
+    rc = L.nvfp4_moe_forward_noalloc(ctypes.byref(desc), ctypes.byref(w), 16, None, 16, 1, huge,
+                                     None, None, None)
+    assert rc == _lib.NVFP4_ERR_INVALID_ARG and b"token count" in L.nvfp4_last_error_string()
+    rc = L.nvfp4_moe_forward(ctypes.byref(desc), ctypes.byref(w), 16, None, 16, 1, huge, None,
+                             None, 256, 1 << 40, None)
+    assert rc == _lib.NVFP4_ERR_INVALID_ARG and b"token count" in L.nvfp4_last_error_string()
+    for fn, args in (("nvfp4_ep_dispatch_plan", (16, huge, 8, 16, 8, 16, 16, 16, 16, None)),):
+        assert getattr(L, fn)(*args) == _lib.NVFP4_ERR_INVALID_ARG
+    p = _lib.EpPeers()
+    p.rank, p.world, p.max_rows, p.hidden, p.timeout_ms = 0, 1, 64, 2048, 0
+    p.windows[0] = 1 << 20
+    assert L.nvfp4_ep_p2p_dispatch(ctypes.byref(p), 16, 16, huge, 8, 16, None) == \
+        _lib.NVFP4_ERR_INVALID_ARG
+    assert L.nvfp4_ep_p2p_workspace_size(ctypes.byref(desc), ctypes.byref(p), huge) == 0
+
+
 def test_peer_exchange_validation_without_gpu():
     """include/nvfp4_ep.h host side: window sizes and layout, and the checks
     that refuse a bad peer table before any CUDA work."""

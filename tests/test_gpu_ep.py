@@ -1,9 +1,9 @@
-"""Expert-parallel MoE on 2 GPUs (NCCL all-to-all over NVLink) against the
+"""Expert-parallel MoE on 2 and 4 GPUs (NCCL all-to-all over NVLink) against the
 single-GPU layer: every row an expert computes is the same arithmetic in
 both, and the combine sums in the same slot order, so the outputs must be
 bitwise equal.  Both exchange modes; the fixed-capacity one also replayed
 from a CUDA graph that holds its NCCL calls.  Skipped on a host with fewer
-than 2 GPUs."""
+than the test's world size."""
 import os
 import socket
 
@@ -70,19 +70,19 @@ def _port():
     return p
 
 
+@pytest.mark.parametrize("world", [2, 4])
 @pytest.mark.parametrize("static", [False, True])
-def test_ep_two_gpus_equals_single_gpu(cuda, static):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+def test_ep_multi_gpu_equals_single_gpu(cuda, static, world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     from nvfp4 import synthetic
     from nvfp4.moe import MoELayer, MoEWeights
 
-    world = 2
     mgr = mp.get_context("spawn").Manager()
     ret = mgr.dict()
     mp.spawn(_worker, args=(world, _port(), static, ret), nprocs=world, join=True)
     if static:
-        assert ret["graph0"] and ret["graph1"]
+        assert all(ret[f"graph{r}"] for r in range(world))
     wd = synthetic.moe_weights(E, H, I, seed=11)
     x_all = synthetic.bf16_round(synthetic.activations(T_RANK * world, H, seed=12))
     layer = MoELayer(MoEWeights.from_dict(wd), top_k=K_TOP)

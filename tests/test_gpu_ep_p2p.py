@@ -11,7 +11,7 @@ output must equal the single-GPU layer's on the same tokens bit for bit
 the same slot order).  The timeout tests leave one flag unraised and check
 that the wait gives up, records the missing rank and leaves the context
 usable.  The 2-process test runs the real exchange over NVLink when the host
-has 2 GPUs."""
+has 2 or 4 GPUs (one process per GPU)."""
 import os
 import socket
 
@@ -258,12 +258,12 @@ def _port():
     return p
 
 
-def test_p2p_two_gpus_equals_single_gpu(cuda):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+@pytest.mark.parametrize("world", [2, 4])
+def test_p2p_multi_gpu_equals_single_gpu(cuda, world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     from nvfp4.moe import MoELayer, MoEWeights
 
-    world = 2
     mgr = mp.get_context("spawn").Manager()
     ret = mgr.dict()
     mp.spawn(_worker, args=(world, _port(), ret), nprocs=world, join=True)
