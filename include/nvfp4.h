@@ -62,6 +62,8 @@ typedef enum nvfp4_dtype {
 #define NVFP4_FLAG_FORCE_SKINNY 0x2u /* dispatch override (tests/bench): decode GEMV path */
 #define NVFP4_FLAG_FORCE_TC 0x4u     /* dispatch override (tests/bench): tcgen05 GEMM path */
 #define NVFP4_FLAG_FORCE_F32 0x8u    /* dispatch override: CUDA-core fp32 path */
+#define NVFP4_FLAG_LEGACY_GEMV 0x10u /* dispatch override (tests/bench): M <= 8 on the
+                                        mma.sync decode GEMV instead of the tcgen05 one */
 
 /*
  * Mirrors struct NvFp4Linear (nvfp4/config.mojo:64-103): in/out features,

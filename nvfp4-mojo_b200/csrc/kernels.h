@@ -92,6 +92,16 @@ cudaError_t launch_gemv(const WeightSpec &ws, const AlphaSpec &al, const uint16_
                         int64_t x_ld, void *y, int y_dtype, int64_t y_ld, int M,
                         cudaStream_t st);
 
+// Decode GEMV for M <= 8 tokens on tcgen05 with the decoded weights in TMEM
+// (A operand) and the activations in shared memory (B), K % 256 == 0,
+// 16-byte aligned weights, scales and x rows.
+bool gemv_ts_supported(int M, int N, int K, const void *w, const void *sf, const void *x,
+                       int64_t x_ld);
+cudaError_t launch_gemv_ts(const WeightSpec &ws, const AlphaSpec &al, const uint16_t *x,
+                           int64_t x_ld, void *y, int y_dtype, int64_t y_ld, int M,
+                           cudaStream_t st);
+int read_gemv_ts_device_status();
+
 // Grouped MoE expert GEMMs on the decode GEMV kernel (work items of at most
 // 8 token slots): gate_up -> silu(gate) * up as bf16 hi + lo [R, I] (rows in
 // slot order), down on those hi + lo rows -> y rows (dst_row scatter).

@@ -66,8 +66,14 @@ static int run_linear(const WeightSpec &ws, const AlphaSpec &al, const void *x, 
     return check_launch(launch_w4a16_tc(ws, al, reinterpret_cast<const uint16_t *>(x), xs_m, y,
                                         y_dt, ys_m, (int)M, st),
                         "tcgen05 GEMM launch");
-  // M <= 8: the decode GEMV (f16 tensor-core MMAs fed by hardware FP4 / FP8
-  // conversions, K split across a thread-block cluster).
+  // M <= 8: the decode GEMV on tcgen05 (decoded weights in tensor memory, K
+  // split across a thread-block cluster when the tiles do not fill the GPU).
+  if (!force_f32 && token_major && x_dt == kBF16 && !(flags & NVFP4_FLAG_LEGACY_GEMV) &&
+      gemv_ts_supported((int)M, ws.N, ws.K, ws.w, ws.sf, x, xs_m))
+    return check_launch(launch_gemv_ts(ws, al, reinterpret_cast<const uint16_t *>(x), xs_m, y,
+                                       y_dt, ys_m, (int)M, st),
+                        "decode GEMV launch");
+  // The same GEMV on register-fragment mma.sync tensor-core instructions.
   if (!force_f32 && token_major && x_dt == kBF16 &&
       gemv_supported((int)M, ws.K, ws.w, ws.sf, x, xs_m))
     return check_launch(launch_gemv(ws, al, reinterpret_cast<const uint16_t *>(x), xs_m, y, y_dt,
@@ -260,8 +266,9 @@ extern "C" int nvfp4_dequant_tile(const uint8_t *w, const uint8_t *sf, float *ou
 }
 
 extern "C" int nvfp4_device_status(void) {
-  const int words[4] = {read_gemm_device_status(), read_gemv_device_status(),
-                        read_moe_tc_device_status(), read_w4a4_device_status()};
+  const int words[5] = {read_gemm_device_status(), read_gemv_device_status(),
+                        read_moe_tc_device_status(), read_w4a4_device_status(),
+                        read_gemv_ts_device_status()};
   int v = 0;
   for (int w : words) {
     if (w < 0) return fail(NVFP4_ERR_CUDA, "could not read the device status word");

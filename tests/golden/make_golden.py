@@ -11,7 +11,7 @@ reference_kats.json -- the known-answer tests of the reference, read as text
 e4m3_table.json -- float8_e4m3fn -> float32 for all 256 codes from ml_dtypes
   (an implementation independent of the oracle), NaN written as "nan".
 
-Usage: python tests/golden/make_golden.py [path-to-reference-checkout]
+Usage: python tests/golden/make_golden.py <path-to-reference-checkout>
 """
 from __future__ import annotations
 
@@ -105,7 +105,9 @@ def e4m3_table() -> dict:
 
 
 def main() -> None:
-    ref = Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <path of the reference checkout>")
+    ref = Path(sys.argv[1])
     (HERE / "reference_kats.json").write_text(json.dumps(parse_reference(ref), indent=1) + "\n")
     (HERE / "e4m3_table.json").write_text(json.dumps(e4m3_table(), indent=0) + "\n")
     print("wrote", HERE / "reference_kats.json", HERE / "e4m3_table.json")

@@ -128,6 +128,10 @@ def test_decode_gemv_sweep(O, cuda, K, N, M):
     # Exact decode + fp32 accumulation: only summation order differs.
     assert rel_err(y32.cpu().numpy(), ref) <= 1e-5
     assert rel_err(ybf.float().cpu().numpy(), ref) <= TOL_BF16
+    # The mma.sync GEMV (kept selectable) agrees with the oracle too.
+    yl = torch.empty((M, N), dtype=torch.float32, device=cuda)
+    nvfp4.nvfp4_linear_forward(lin, W, SF, X, yl, M, flags=nvfp4._lib.FLAG_LEGACY_GEMV)
+    assert rel_err(yl.cpu().numpy(), ref) <= 1e-5
 
 
 @pytest.mark.parametrize("N,K,M", [(100, 512, 1), (100, 512, 3), (136, 768, 8), (64, 256, 5),
