@@ -1210,6 +1210,7 @@ def main():
     if hasattr(wl, "parity") and not args.no_parity:
         parity = wl.parity()
 
+    used_graph = bool(graphs)
     secondary = None
     if args.workload == "ep" and world == 1 and not args.no_secondary:
         secondary = {}
@@ -1228,7 +1229,7 @@ def main():
             "higher_is_better": True, "scaling": getattr(wl, "scaling", "weak"),
             "vs_baseline": None, "dtype": getattr(wl, "dtype", "bf16"),
             "data": "synthetic", "config": dict({"parallelism": (
-                "replicas" if world > 1 else "single GPU")}, **wl.config, graph=bool(graphs)),
+                "replicas" if world > 1 else "single GPU")}, **wl.config, graph=used_graph),
             "roofline": roof, "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": wl.unit, "h2d_bytes_per_step": wl.h2d,
                     "d2h_bytes_per_step": wl.d2h},

@@ -62,8 +62,11 @@ typedef enum nvfp4_dtype {
 #define NVFP4_FLAG_FORCE_SKINNY 0x2u /* dispatch override (tests/bench): decode GEMV path */
 #define NVFP4_FLAG_FORCE_TC 0x4u     /* dispatch override (tests/bench): tcgen05 GEMM path */
 #define NVFP4_FLAG_FORCE_F32 0x8u    /* dispatch override: CUDA-core fp32 path */
-#define NVFP4_FLAG_LEGACY_GEMV 0x10u /* dispatch override (tests/bench): M <= 8 on the
-                                        mma.sync decode GEMV instead of the tcgen05 one */
+#define NVFP4_FLAG_TS_GEMV 0x10u /* M <= 8 on the tcgen05 decode GEMV (decoded weights in
+                                    tensor memory) instead of the mma.sync one */
+#define NVFP4_FLAG_DIGIT_GEMV 0x20u /* M <= 8: activations as four NVFP4 digits, weights as
+                                       stored into block-scaled FP4 MMAs (~5e-4 x RMS of the
+                                       bf16-operand result; K <= 16384) */
 
 /*
  * Mirrors struct NvFp4Linear (nvfp4/config.mojo:64-103): in/out features,

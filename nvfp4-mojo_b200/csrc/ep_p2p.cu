@@ -9,7 +9,11 @@
 // with ld.acquire.sys (local memory, bounded by time) and every later read
 // of the published rows follows that acquire in the same stream.  All waits
 // are on this GPU's memory, all signals are remote stores, so no kernel ever
-// waits on another kernel of its own GPU.
+// waits on another kernel of its own GPU.  Every kernel here is launched with
+// programmatic dependent launch and executes griddepcontrol.wait before it
+// reads anything an earlier kernel of the stream wrote (ids, rows, the step
+// counter), so it is resident when its predecessor ends instead of being
+// launched then.
 #include <string.h>
 
 #include <algorithm>
@@ -124,6 +128,8 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(PeerTable P, const int
                                                           int epr) {
   __shared__ char *s_win[kMaxWorld];
   __shared__ int s_last;
+  pdl_wait();  // ids, x and the step counter come from earlier kernels
+  pdl_trigger();
   if (threadIdx.x < kMaxWorld) s_win[threadIdx.x] = win_at(P, threadIdx.x < P.world ? threadIdx.x : 0);
   __syncthreads();
   EpCtrl *own = ctrl_of(s_win[P.rank]);
@@ -161,6 +167,8 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(PeerTable P, const int
 // same T on every rank), then the step counter advances (also after a timeout
 // or a shape mismatch, which the error word records).
 __global__ void ep_wait_dispatch_kernel(PeerTable P) {
+  pdl_wait();
+  pdl_trigger();
   EpCtrl *own = ctrl_of(win_at(P, P.rank));
   const int lane = threadIdx.x;
   const uint32_t step = __ldcg(&own->epoch) + 1;
@@ -177,6 +185,8 @@ __global__ void ep_wait_dispatch_kernel(PeerTable P) {
 // Step 5: the expert rows of this step (written by the kernels before this
 // one) are complete; tell every rank.
 __global__ void ep_signal_done_kernel(PeerTable P) {
+  pdl_wait();  // the expert rows are complete once the kernels before have finished
+  pdl_trigger();
   EpCtrl *own = ctrl_of(win_at(P, P.rank));
   const uint32_t step = __ldcg(&own->epoch);
   __threadfence_system();
@@ -194,6 +204,8 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(PeerTable P, const int3
                                                          OutT *__restrict__ y, int T, int k, int epr) {
   __shared__ const float *s_out[kMaxWorld];
   __shared__ int s_ok;
+  pdl_wait();
+  pdl_trigger();
   EpCtrl *own = ctrl_of(win_at(P, P.rank));
   const uint32_t step = __ldcg(&own->epoch);
   if (threadIdx.x == 0) s_ok = 1;
@@ -377,23 +389,26 @@ extern "C" int nvfp4_ep_p2p_dispatch(const nvfp4_ep_peers *p, const int32_t *ids
   const int64_t R = T * k;
   // At least one block, so the flags go up even for an empty step.
   const unsigned blocks = (unsigned)std::max<int64_t>(1, std::min<int64_t>((R + 7) / 8, 148 * 8));
-  ep_dispatch_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      make_table(*p), ids, static_cast<const uint4 *>(x), (int)T, k, epr);
-  return check_launch(cudaGetLastError(), "dispatch launch");
+  return check_launch(launch_pdl(ep_dispatch_kernel, dim3(blocks), dim3(256), 0,
+                                  static_cast<cudaStream_t>(stream), make_table(*p), ids,
+                                  static_cast<const uint4 *>(x), (int)T, k, epr),
+                      "dispatch launch");
 }
 
 extern "C" int nvfp4_ep_p2p_wait_dispatch(const nvfp4_ep_peers *p, void *stream) {
   int rc = check_peers(p);
   if (rc) return rc;
-  ep_wait_dispatch_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(make_table(*p));
-  return check_launch(cudaGetLastError(), "dispatch wait launch");
+  return check_launch(launch_pdl(ep_wait_dispatch_kernel, dim3(1), dim3(32), 0,
+                                  static_cast<cudaStream_t>(stream), make_table(*p)),
+                      "dispatch wait launch");
 }
 
 extern "C" int nvfp4_ep_p2p_signal_done(const nvfp4_ep_peers *p, void *stream) {
   int rc = check_peers(p);
   if (rc) return rc;
-  ep_signal_done_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(make_table(*p));
-  return check_launch(cudaGetLastError(), "done signal launch");
+  return check_launch(launch_pdl(ep_signal_done_kernel, dim3(1), dim3(32), 0,
+                                  static_cast<cudaStream_t>(stream), make_table(*p)),
+                      "done signal launch");
 }
 
 extern "C" int nvfp4_ep_p2p_combine(const nvfp4_ep_peers *p, const int32_t *ids, const float *w,
@@ -411,13 +426,15 @@ extern "C" int nvfp4_ep_p2p_combine(const nvfp4_ep_peers *p, const int32_t *ids,
   const unsigned blocks = (unsigned)std::max<int64_t>(1, (n + 255) / 256);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const uint16_t *res = static_cast<const uint16_t *>(residual);
+  const PeerTable P = make_table(*p);
+  cudaError_t e;
   if (y_dtype == NVFP4_DTYPE_F32)
-    ep_combine_kernel<float><<<blocks, 256, 0, st>>>(make_table(*p), ids, w, res,
-                                                     static_cast<float *>(y), (int)T, k, epr);
+    e = launch_pdl(ep_combine_kernel<float>, dim3(blocks), dim3(256), 0, st, P, ids, w, res,
+                   static_cast<float *>(y), (int)T, k, epr);
   else
-    ep_combine_kernel<uint16_t><<<blocks, 256, 0, st>>>(make_table(*p), ids, w, res,
-                                                        static_cast<uint16_t *>(y), (int)T, k, epr);
-  return check_launch(cudaGetLastError(), "combine launch");
+    e = launch_pdl(ep_combine_kernel<uint16_t>, dim3(blocks), dim3(256), 0, st, P, ids, w, res,
+                   static_cast<uint16_t *>(y), (int)T, k, epr);
+  return check_launch(e, "combine launch");
 }
 
 extern "C" int nvfp4_ep_p2p_error(const nvfp4_ep_peers *p, uint32_t *error, int32_t clear,

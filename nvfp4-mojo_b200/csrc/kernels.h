@@ -102,6 +102,18 @@ cudaError_t launch_gemv_ts(const WeightSpec &ws, const AlphaSpec &al, const uint
                            cudaStream_t st);
 int read_gemv_ts_device_status();
 
+// Decode GEMV for M <= 8 tokens on the block-scaled FP4 tensor cores: the
+// activations as four NVFP4 digits (computed into `scratch`, of
+// gemv_dg_scratch_bytes(K)), the weights fed to the MMA as stored.
+// K % 256 == 0, K <= 16384, 16-byte aligned weights, scales and x rows.
+bool gemv_dg_supported(int M, int N, int K, const void *w, const void *sf, const void *x,
+                       int64_t x_ld);
+size_t gemv_dg_scratch_bytes(int K);
+cudaError_t launch_gemv_dg(const WeightSpec &ws, const AlphaSpec &al, const uint16_t *x,
+                           int64_t x_ld, void *y, int y_dtype, int64_t y_ld, int M,
+                           uint8_t *scratch, size_t scratch_bytes, cudaStream_t st);
+int read_gemv_dg_device_status();
+
 // Grouped MoE expert GEMMs on the decode GEMV kernel (work items of at most
 // 8 token slots): gate_up -> silu(gate) * up as bf16 hi + lo [R, I] (rows in
 // slot order), down on those hi + lo rows -> y rows (dst_row scatter).

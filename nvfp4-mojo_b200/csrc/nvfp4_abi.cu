@@ -66,14 +66,35 @@ static int run_linear(const WeightSpec &ws, const AlphaSpec &al, const void *x, 
     return check_launch(launch_w4a16_tc(ws, al, reinterpret_cast<const uint16_t *>(x), xs_m, y,
                                         y_dt, ys_m, (int)M, st),
                         "tcgen05 GEMM launch");
-  // M <= 8: the decode GEMV on tcgen05 (decoded weights in tensor memory, K
-  // split across a thread-block cluster when the tiles do not fill the GPU).
-  if (!force_f32 && token_major && x_dt == kBF16 && !(flags & NVFP4_FLAG_LEGACY_GEMV) &&
+  // M <= 8 with NVFP4_FLAG_DIGIT_GEMV: the activations as four NVFP4 digits
+  // (stream-ordered scratch, so the call stays asynchronous and capturable),
+  // the weights straight into block-scaled FP4 MMAs.
+  if (!force_f32 && token_major && x_dt == kBF16 && (flags & NVFP4_FLAG_DIGIT_GEMV) &&
+      gemv_dg_supported((int)M, ws.N, ws.K, ws.w, ws.sf, x, xs_m)) {
+    const size_t bytes = gemv_dg_scratch_bytes(ws.K);
+    void *buf = nullptr;
+    cudaError_t e = cudaMallocAsync(&buf, bytes, st);
+    if (e != cudaSuccess) return check_launch(e, "digit GEMV scratch (cudaMallocAsync)");
+    const int rc = check_launch(launch_gemv_dg(ws, al, reinterpret_cast<const uint16_t *>(x), xs_m,
+                                               y, y_dt, ys_m, (int)M, static_cast<uint8_t *>(buf),
+                                               bytes, st),
+                                "digit GEMV launch");
+    e = cudaFreeAsync(buf, st);
+    if (rc == NVFP4_OK && e != cudaSuccess) return check_launch(e, "digit GEMV scratch release");
+    return rc;
+  }
+  // M <= 8 with NVFP4_FLAG_TS_GEMV: the decode GEMV on tcgen05 (decoded
+  // weights in tensor memory, K split across a thread-block cluster when the
+  // tiles do not fill the GPU).  Exact like the default below, but slower on
+  // B200 as measured: the 128 x 16 x 16 MMAs it issues cost about as much as
+  // full-width ones.
+  if (!force_f32 && token_major && x_dt == kBF16 && (flags & NVFP4_FLAG_TS_GEMV) &&
       gemv_ts_supported((int)M, ws.N, ws.K, ws.w, ws.sf, x, xs_m))
     return check_launch(launch_gemv_ts(ws, al, reinterpret_cast<const uint16_t *>(x), xs_m, y,
                                        y_dt, ys_m, (int)M, st),
                         "decode GEMV launch");
-  // The same GEMV on register-fragment mma.sync tensor-core instructions.
+  // M <= 8: the decode GEMV on register-fragment mma.sync tensor-core
+  // instructions fed by the hardware FP4 / FP8 conversions.
   if (!force_f32 && token_major && x_dt == kBF16 &&
       gemv_supported((int)M, ws.K, ws.w, ws.sf, x, xs_m))
     return check_launch(launch_gemv(ws, al, reinterpret_cast<const uint16_t *>(x), xs_m, y, y_dt,
@@ -266,9 +287,9 @@ extern "C" int nvfp4_dequant_tile(const uint8_t *w, const uint8_t *sf, float *ou
 }
 
 extern "C" int nvfp4_device_status(void) {
-  const int words[5] = {read_gemm_device_status(), read_gemv_device_status(),
+  const int words[6] = {read_gemm_device_status(), read_gemv_device_status(),
                         read_moe_tc_device_status(), read_w4a4_device_status(),
-                        read_gemv_ts_device_status()};
+                        read_gemv_ts_device_status(), read_gemv_dg_device_status()};
   int v = 0;
   for (int w : words) {
     if (w < 0) return fail(NVFP4_ERR_CUDA, "could not read the device status word");

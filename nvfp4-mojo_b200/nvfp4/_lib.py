@@ -27,7 +27,8 @@ FLAG_W4A4 = 0x1
 FLAG_FORCE_SKINNY = 0x2
 FLAG_FORCE_TC = 0x4
 FLAG_FORCE_F32 = 0x8
-FLAG_LEGACY_GEMV = 0x10
+FLAG_TS_GEMV = 0x10
+FLAG_DIGIT_GEMV = 0x20
 
 _STATUS_NAMES = {
     NVFP4_ERR_INVALID_ARG: "invalid argument",

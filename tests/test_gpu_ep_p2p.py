@@ -169,6 +169,30 @@ def test_dispatch_wait_times_out(cuda):
         pws[0].close()
 
 
+def test_ranks_with_different_token_counts_are_reported(cuda):
+    """The window layout puts source rank r's slots at r*T*k, so every rank
+    must step with the same T.  Rank 1 dispatches half as many tokens as rank
+    0 (every row still inside the windows): each rank's wait records the
+    other as a shape mismatch."""
+    from nvfp4 import _lib, ep
+    from nvfp4.moe import MoEWeights, moe_route
+
+    full = MoEWeights.from_dict(moe_dict())
+    pws = ep.PeerWindows.emulated(2, T * K, H)
+    try:
+        xs = [tokens(21), tokens(22, T // 2)]
+        for r in range(2):
+            ids, _, _ = moe_route(full, xs[r], top_k=K)
+            ep.p2p_dispatch(pws[r], ids, xs[r], E // 2)
+        for r in range(2):
+            ep.p2p_wait_dispatch(pws[r])
+        torch.cuda.synchronize()
+        assert pws[0].error() == _lib.EP_ERR_SHAPE | (1 << (8 + 1))
+        assert pws[1].error() == _lib.EP_ERR_SHAPE | (1 << (8 + 0))
+    finally:
+        pws[0].close()
+
+
 def test_combine_wait_times_out(cuda):
     """Rank 1 dispatches but never signals its experts done: rank 0's
     combine gives up, records rank 1, and leaves its output untouched."""

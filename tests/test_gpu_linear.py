@@ -128,10 +128,10 @@ def test_decode_gemv_sweep(O, cuda, K, N, M):
     # Exact decode + fp32 accumulation: only summation order differs.
     assert rel_err(y32.cpu().numpy(), ref) <= 1e-5
     assert rel_err(ybf.float().cpu().numpy(), ref) <= TOL_BF16
-    # The mma.sync GEMV (kept selectable) agrees with the oracle too.
-    yl = torch.empty((M, N), dtype=torch.float32, device=cuda)
-    nvfp4.nvfp4_linear_forward(lin, W, SF, X, yl, M, flags=nvfp4._lib.FLAG_LEGACY_GEMV)
-    assert rel_err(yl.cpu().numpy(), ref) <= 1e-5
+    # The tcgen05 GEMV (opt-in) agrees with the oracle too.
+    yt = torch.empty((M, N), dtype=torch.float32, device=cuda)
+    nvfp4.nvfp4_linear_forward(lin, W, SF, X, yt, M, flags=nvfp4._lib.FLAG_TS_GEMV)
+    assert rel_err(yt.cpu().numpy(), ref) <= 1e-5
 
 
 @pytest.mark.parametrize("N,K,M", [(100, 512, 1), (100, 512, 3), (136, 768, 8), (64, 256, 5),
@@ -153,6 +153,11 @@ def test_decode_gemv_shapes(O, cuda, N, K, M):
     assert not torch.isnan(y32).any()
     assert rel_err(y32.cpu().numpy(), ref) <= 1e-5
     assert rel_err(ybf.float().cpu().numpy(), ref) <= TOL_BF16
+    # The tcgen05 GEMV (opt-in) on the same ragged shapes.
+    yt = torch.full((M, N), float("nan"), dtype=torch.float32, device=cuda)
+    nvfp4.nvfp4_linear_forward(lin, W, SF, X, yt, M, flags=nvfp4._lib.FLAG_TS_GEMV)
+    assert not torch.isnan(yt).any()
+    assert rel_err(yt.cpu().numpy(), ref) <= 1e-5
 
 
 def test_decode_gemv_chained_layers(O, cuda):
@@ -354,3 +359,63 @@ def test_decode_gemv_repeatable(cuda, M):
     assert not torch.isnan(first).any()
     for i, y in enumerate(outs[1:], 1):
         assert torch.equal(y, first), f"call {i} differs"
+
+
+DIGIT_TOL = 1e-3  # four FP4 digits: ~5e-4 of RMS measured against the exact linear
+
+
+@pytest.mark.parametrize("K,N", [(2048, 1536), (768, 2048), (4096, 14336), (512, 100),
+                                 (1024, 136), (4096, 1000)])
+@pytest.mark.parametrize("M", [1, 3, 8])
+def test_digit_gemv_against_oracle(O, cuda, K, N, M):
+    """NVFP4_FLAG_DIGIT_GEMV: activations as four NVFP4 digits, weights as
+    stored into block-scaled FP4 MMAs.  An approximation of the bf16
+    operand: fp32 out within 1e-3 of RMS of the exact linear (the oracle),
+    bf16 out within the bf16 tolerance; per-row weight_scale_2 and a scalar
+    input_scale."""
+    import nvfp4
+    from nvfp4 import synthetic
+
+    wd = synthetic.linear_weights(N, K, seed=300 + K + N + M)
+    x = synthetic.bf16_round(synthetic.activations(M, K, seed=M + 11))
+    lin = nvfp4.NvFp4Linear(K, N, input_scale=0.5, weight_scale_2_rows=dev(wd["ws2"]))
+    W, SF, X = dev(wd["w"]), dev(wd["sf"]), dev(x, torch.bfloat16)
+    flags = nvfp4._lib.FLAG_DIGIT_GEMV
+    y32 = torch.full((M, N), float("nan"), dtype=torch.float32, device=cuda)
+    nvfp4.nvfp4_linear_forward(lin, W, SF, X, y32, M, flags=flags)
+    ybf = nvfp4.nvfp4_linear(lin, W, SF, X, flags=flags)
+    torch.cuda.synchronize()
+    assert nvfp4._lib.load().nvfp4_device_status() == 0
+    ref = O.linear(wd["w"], wd["sf"], x, input_scale=0.5, ws2_rows=wd["ws2"])
+    assert not torch.isnan(y32).any()
+    assert rel_err(y32.cpu().numpy(), ref) <= DIGIT_TOL
+    assert rel_err(ybf.float().cpu().numpy(), ref) <= TOL_BF16
+
+
+def test_digit_gemv_repeatable_and_outliers(O, cuda):
+    """Bitwise equal over repeated calls; a token with an outlier channel,
+    an all-zero token and a tiny-magnitude token stay within tolerance."""
+    import nvfp4
+    from nvfp4 import synthetic
+
+    N, K, M = 1536, 2048, 4
+    wd = synthetic.linear_weights(N, K, seed=77)
+    x = synthetic.activations(M, K, seed=78)
+    x[0, 5] = 900.0
+    x[1] = 0.0
+    x[2] *= 1e-20
+    x = synthetic.bf16_round(x)
+    lin = nvfp4.NvFp4Linear(K, N, weight_scale_2_rows=dev(wd["ws2"]))
+    W, SF, X = dev(wd["w"]), dev(wd["sf"]), dev(x, torch.bfloat16)
+    outs = []
+    for _ in range(6):
+        y = torch.empty((M, N), dtype=torch.float32, device=cuda)
+        nvfp4.nvfp4_linear_forward(lin, W, SF, X, y, M, flags=nvfp4._lib.FLAG_DIGIT_GEMV)
+        outs.append(y)
+    torch.cuda.synchronize()
+    assert all(torch.equal(outs[0], o) for o in outs[1:])
+    got = outs[0].cpu().numpy()
+    ref = O.linear(wd["w"], wd["sf"], x, ws2_rows=wd["ws2"])
+    assert np.all(got[1] == 0.0)
+    for t in (0, 2, 3):
+        assert rel_err(got[t], ref[t]) <= DIGIT_TOL, t

@@ -58,6 +58,36 @@ def test_noalloc_matches_workspace_entry_point(cuda):
         assert rel_err(got, ref) <= TOL, call
 
 
+def test_noalloc_largest_layer_that_fits(cuda):
+    """The largest token count whose workspace fits the scratch runs (and uses
+    its top end); one more token is rejected before anything is launched."""
+    from nvfp4 import _lib
+
+    L = _lib.load()
+    cap = 16 * 1024 * 1024
+    layer, _ = _layer(1)
+    T = 1
+    while L.nvfp4_moe_workspace_size(ctypes.byref(layer.desc), T + 1) <= cap:
+        T += 1
+    assert L.nvfp4_moe_workspace_size(ctypes.byref(layer.desc), T) <= cap
+    layer, X = _layer(T)
+    ref = layer(X).float().cpu().numpy()
+    y = torch.full_like(X, float("nan"))
+    stream = torch.cuda.current_stream().cuda_stream
+    rc = L.nvfp4_moe_forward_noalloc(ctypes.byref(layer.desc), ctypes.byref(layer.ptrs),
+                                     X.data_ptr(), None, y.data_ptr(), _lib.DTYPE_BF16, T,
+                                     None, None, stream)
+    assert rc == 0, L.nvfp4_last_error_string()
+    torch.cuda.synchronize()
+    got = y.float().cpu().numpy()
+    assert not np.isnan(got).any() and rel_err(got, ref) <= TOL
+    X2 = torch.zeros((T + 1, X.shape[1]), dtype=X.dtype, device=X.device)
+    rc = L.nvfp4_moe_forward_noalloc(ctypes.byref(layer.desc), ctypes.byref(layer.ptrs),
+                                     X2.data_ptr(), None, X2.data_ptr(), _lib.DTYPE_BF16, T + 1,
+                                     None, None, stream)
+    assert rc == _lib.NVFP4_ERR_WORKSPACE
+
+
 def test_noalloc_rejects_layers_beyond_the_scratch(cuda):
     from nvfp4 import _lib
 
