@@ -85,9 +85,11 @@ constexpr int kStageTx = kOffSB + kDgRows * kBK / 16;  // 23040 bytes landed per
 constexpr int kStage = 23552;                        // stride (1024-aligned)
 constexpr int kTxA = kBM * kBK / 2 + kBM * kBK / 16;  // weight part of a stage
 // TMEM columns: accumulator [0, 32), weight scales 16 per stage, digit
-// scales 4 per stage.
+// scales 16 per stage (a 4-column group per MMA, as the scale-factor
+// operand address of each MMA is 4-column aligned; the 32 digit rows use the
+// group's first column).
 constexpr int kColD = 0, kColSA = 32, kColSB = 32 + 16 * kStages;
-static_assert(kColSB + 4 * kStages <= kTmemCols, "TMEM columns");
+static_assert(kColSB + 16 * kStages <= kTmemCols, "TMEM columns");
 constexpr int kSmemBytes = kStages * kStage + 256;   // + barriers and misc
 constexpr int kMaxC = 8;
 
@@ -115,12 +117,6 @@ __device__ __forceinline__ void tmem_st_x16(uint32_t taddr, const uint32_t (&v)[
       "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
       "r"(v[15])
       : "memory");
-}
-
-__device__ __forceinline__ void tmem_st_x4(uint32_t taddr, const uint32_t (&v)[4]) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(taddr),
-               "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3])
-               : "memory");
 }
 
 __device__ __forceinline__ void tmem_st_wait() {
@@ -358,7 +354,7 @@ __global__ void __launch_bounds__(kThreads, 4)
         for (int j = 0; j < kBK / 64; ++j)
           mma_nvf4(tmem + kColD, sw128_kmajor_desc(st + 32 * j),
                    sw128_kmajor_desc(st + kOffB + 32 * j), tmem + kColSA + 16 * s + 4 * j,
-                   tmem + kColSB + 4 * s + j, (g | j) != 0 ? 1u : 0u);
+                   tmem + kColSB + 16 * s + 4 * j, (g | j) != 0 ? 1u : 0u);
         tc_commit(bar_empty + 8 * s);
       }
       tc_commit(bar_dfull);  // also after an abort: the epilogue waits for every MMA
@@ -378,7 +374,7 @@ __global__ void __launch_bounds__(kThreads, 4)
       const uint8_t *sb = smem + s * kStage + kOffSB;
       // Scale-factor layout (M = 128, and the digit rows): for the MMA j of
       // the stage, row r's four scales (one word) sit in lane r % 32 of
-      // column base + 4j + r / 32 (A) or base + j (B, rows < 32), the
+      // column base + 4j + r / 32 (B: rows < 32, so column base + 4j), the
       // 32-lane pattern repeated in each lane quarter.
       uint32_t va[16];
 #pragma unroll
@@ -390,10 +386,11 @@ __global__ void __launch_bounds__(kThreads, 4)
         va[12 + c] = r.w;
       }
       const uint4 rb = *reinterpret_cast<const uint4 *>(sb + 16 * lane);
-      const uint32_t vb[4] = {rb.x, rb.y, rb.z, rb.w};
+      const uint32_t vb[16] = {rb.x, 0u, 0u, 0u, rb.y, 0u, 0u, 0u,
+                               rb.z, 0u, 0u, 0u, rb.w, 0u, 0u, 0u};
       const uint32_t lq = static_cast<uint32_t>(32 * q) << 16;
       tmem_st_x16(tmem + lq + kColSA + 16 * s, va);
-      tmem_st_x4(tmem + lq + kColSB + 4 * s, vb);
+      tmem_st_x16(tmem + lq + kColSB + 16 * s, vb);
       tmem_st_wait();
       tc_fence_before();
       fence_proxy_async_smem();  // these reads before the next TMA write of the stage
