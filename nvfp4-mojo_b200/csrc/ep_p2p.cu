@@ -21,8 +21,6 @@
 #include "../../include/nvfp4.h"
 #include "../../include/nvfp4_ep.h"
 #include "abi_util.h"
-#include "kernels.h"
-#include "moe.h"
 #include "nvfp4_common.cuh"
 
 namespace nvfp4 {
@@ -203,23 +201,13 @@ template <typename OutT>
 __global__ void __launch_bounds__(256) ep_combine_kernel(PeerTable P, const int32_t *__restrict__ ids,
                                                          const float *__restrict__ w,
                                                          const uint16_t *__restrict__ residual,
-                                                         OutT *__restrict__ y, int T, int k, int epr,
-                                                         int signal) {
+                                                         OutT *__restrict__ y, int T, int k, int epr) {
   __shared__ const float *s_out[kMaxWorld];
   __shared__ int s_ok;
   pdl_wait();
   pdl_trigger();
   EpCtrl *own = ctrl_of(win_at(P, P.rank));
   const uint32_t step = __ldcg(&own->epoch);
-  if (signal) {
-    // Step 5 folded in: this rank's expert rows were written by the kernels
-    // before this one (complete at griddepcontrol.wait); every block raises
-    // this rank's done flag in every window (the same value, so a repeat is
-    // harmless and no block waits on another block's signal).
-    __threadfence_system();
-    if (threadIdx.x < P.world)
-      st_release_sys(&ctrl_of(win_at(P, threadIdx.x))->flag_done[P.rank], step);
-  }
   if (threadIdx.x == 0) s_ok = 1;
   __syncthreads();
   if (threadIdx.x < kMaxWorld) {
@@ -423,26 +411,9 @@ extern "C" int nvfp4_ep_p2p_signal_done(const nvfp4_ep_peers *p, void *stream) {
                       "done signal launch");
 }
 
-namespace nvfp4 {
-// Step 3 as run by the permutation kernel (moe.h): this rank's window fields.
-int ep_p2p_step_wait(const nvfp4_ep_peers *p, PeerStepWait *w) {
-  int rc = check_peers(p);
-  if (rc) return rc;
-  EpCtrl *own = static_cast<EpCtrl *>(p->windows[p->rank]);
-  w->epoch = &own->epoch;
-  w->error = &own->error;
-  w->flags = own->flag_dispatch;
-  w->rows_from = own->rows_from;
-  w->world = p->world;
-  w->rank = p->rank;
-  w->timeout_ns = make_table(*p).timeout_ns;
-  return NVFP4_OK;
-}
-
-// Step 6, with step 5 (the done signal) folded in when `signal` is set.
-int ep_p2p_combine(const nvfp4_ep_peers *p, const int32_t *ids, const float *w, int64_t T,
-                   int32_t k, int32_t epr, const void *residual, void *y, int y_dtype,
-                   void *stream, int signal) {
+extern "C" int nvfp4_ep_p2p_combine(const nvfp4_ep_peers *p, const int32_t *ids, const float *w,
+                                    int64_t T, int32_t k, int32_t epr, const void *residual,
+                                    void *y, int y_dtype, void *stream) {
   int rc = check_step(p, T, k, epr);
   if (rc) return rc;
   if (y_dtype != NVFP4_DTYPE_F32 && y_dtype != NVFP4_DTYPE_BF16)
@@ -459,18 +430,11 @@ int ep_p2p_combine(const nvfp4_ep_peers *p, const int32_t *ids, const float *w, 
   cudaError_t e;
   if (y_dtype == NVFP4_DTYPE_F32)
     e = launch_pdl(ep_combine_kernel<float>, dim3(blocks), dim3(256), 0, st, P, ids, w, res,
-                   static_cast<float *>(y), (int)T, k, epr, signal);
+                   static_cast<float *>(y), (int)T, k, epr);
   else
     e = launch_pdl(ep_combine_kernel<uint16_t>, dim3(blocks), dim3(256), 0, st, P, ids, w, res,
-                   static_cast<uint16_t *>(y), (int)T, k, epr, signal);
+                   static_cast<uint16_t *>(y), (int)T, k, epr);
   return check_launch(e, "combine launch");
-}
-}  // namespace nvfp4
-
-extern "C" int nvfp4_ep_p2p_combine(const nvfp4_ep_peers *p, const int32_t *ids, const float *w,
-                                    int64_t T, int32_t k, int32_t epr, const void *residual,
-                                    void *y, int y_dtype, void *stream) {
-  return ep_p2p_combine(p, ids, w, T, k, epr, residual, y, y_dtype, stream, 0);
 }
 
 extern "C" int nvfp4_ep_p2p_error(const nvfp4_ep_peers *p, uint32_t *error, int32_t clear,

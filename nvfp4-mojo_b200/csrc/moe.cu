@@ -16,7 +16,6 @@
 #include "abi_util.h"
 #include "kernels.h"
 #include "moe.h"
-#include "../../include/nvfp4_ep.h"
 #include "nvfp4_common.cuh"
 
 namespace nvfp4 {
@@ -383,55 +382,13 @@ cudaError_t launch_router(const uint16_t *x, const float *router, float *part, i
 // groups; work items of at most `tpi` rows for the grouped GEMMs.  A single
 // CTA of 1024 threads (R is at most a few tens of thousands of rows).
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t *p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-// PeerStepWait (moe.h): bounded by the global timer and an iteration count.
-__device__ void peer_step_wait(const PeerStepWait &w) {
-  const int lane = threadIdx.x;
-  const uint32_t step = __ldcg(w.epoch) + 1;
-  if (lane < w.world) {
-    unsigned long long t0;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
-    const unsigned long long max_iter = w.timeout_ns / 64 + 1024;
-    bool ok = false;
-    for (unsigned long long it = 0;; ++it) {
-      if ((int32_t)(ld_acquire_sys_u32(w.flags + lane) - step) >= 0) {
-        ok = true;
-        break;
-      }
-      unsigned long long t;
-      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-      if (t - t0 > w.timeout_ns || it >= max_iter) break;
-      __nanosleep(64);
-    }
-    if (!ok)
-      atomicOr(w.error, NVFP4_EP_ERR_DISPATCH_TIMEOUT | (1u << (8 + lane)));
-    else if (ld_acquire_sys_u32(w.rows_from + lane) != ld_acquire_sys_u32(w.rows_from + w.rank))
-      atomicOr(w.error, NVFP4_EP_ERR_SHAPE | (1u << (8 + lane)));
-  }
-  __syncwarp();
-  if (lane == 0) *w.epoch = step;
-}
-
 __global__ void __launch_bounds__(1024) moe_permute_kernel(const int32_t *__restrict__ row_expert,
                                                           const int32_t *__restrict__ x_row_index,
-                                                          int R, int E, int tpi, MoePlan plan,
-                                                          PeerStepWait wait) {
+                                                          int R, int E, int tpi, MoePlan plan) {
   __shared__ int cnt[1024], off[1025], cur[1024], items[1025];
   const int tid = threadIdx.x;
   pdl_wait();  // the routing ids come from the previous kernels
   pdl_trigger();
-  if (wait.epoch) {
-    // Peer exchange: the ids below are the peers' stores into this rank's
-    // window, published by their dispatch flags.
-    if (tid < 32) peer_step_wait(wait);
-    __syncthreads();
-    asm volatile("fence.acq_rel.sys;" ::: "memory");
-  }
   for (int e = tid; e < E; e += blockDim.x) cnt[e] = 0;
   // The first 4 x 1024 routing ids stay in registers for the scatter below.
   int my_e[4];
@@ -520,11 +477,10 @@ __global__ void __launch_bounds__(1024) moe_permute_kernel(const int32_t *__rest
 }
 
 cudaError_t launch_moe_permute(const int32_t *row_expert, const int32_t *x_row_index, int R,
-                               int E, int tpi, const MoePlan &plan, cudaStream_t st,
-                               const PeerStepWait &wait) {
+                               int E, int tpi, const MoePlan &plan, cudaStream_t st) {
   if (E <= 0 || E > 256) return cudaErrorInvalidValue;  // the one-warp scan covers 256 experts
   return launch_pdl(moe_permute_kernel, dim3(1), dim3(1024), 0, st, row_expert, x_row_index, R, E,
-                    tpi, plan, wait);
+                    tpi, plan);
 }
 
 // Slot -> token index for the single-GPU forward: row r = t * k + j reads x[t].

@@ -20,20 +20,6 @@ struct MoePlan {
   int32_t *dst_row;  // [R]
 };
 
-// The peer exchange's dispatch wait, run by the permutation kernel before it
-// reads the received expert ids (include/nvfp4_ep.h step 3): lanes p < world
-// of its first warp wait (bounded) until rank p's dispatch flag reaches
-// epoch + 1 and check that rank p stored as many rows as this rank; then the
-// epoch advances.  Pointers into this rank's own window (ep_p2p.cu).
-struct PeerStepWait {
-  uint32_t *epoch = nullptr;            // null: no wait
-  uint32_t *error = nullptr;
-  const uint32_t *flags = nullptr;      // [world] dispatch flags
-  const uint32_t *rows_from = nullptr;  // [world] row counts of the last dispatches
-  int world = 0, rank = 0;
-  unsigned long long timeout_ns = 0;
-};
-
 // Grouped tensor-core expert GEMM (moe_tc.cu).
 struct MoeTcLaunch {
   const uint8_t *w = nullptr;   // stacked expert codes [E * Nw, K/2]
@@ -63,8 +49,7 @@ cudaError_t launch_router(const uint16_t *x, const float *router, float *part, i
                           float *logits_out, int T, int H, int E, int k, int renormalize,
                           int32_t *ids, float *w, cudaStream_t st);
 cudaError_t launch_moe_permute(const int32_t *row_expert, const int32_t *x_row_index, int R, int E,
-                               int tpi, const MoePlan &plan, cudaStream_t st,
-                               const PeerStepWait &wait = PeerStepWait());
+                               int tpi, const MoePlan &plan, cudaStream_t st);
 cudaError_t launch_slot_token(int32_t *idx, int R, int k, cudaStream_t st);
 // extra (nullable): fp32 rows [T, H] added after the routed sum, before the
 // residual (the shared expert's output).

@@ -139,12 +139,8 @@ int check_weights(const nvfp4_moe_weights *w) {
 
 int run_experts(const nvfp4_moe_desc &d, const nvfp4_moe_weights &w, const uint16_t *x,
                 const int32_t *x_row_index, const int32_t *row_expert, int64_t R,
-                void *y_rows, int y_dtype, uint8_t *ws, cudaStream_t st,
-                const PeerStepWait &wait = PeerStepWait()) {
-  // No rows: nothing to compute, but a peer-exchange step still takes its
-  // dispatch wait (the permutation kernel over zero rows runs it), so that
-  // every rank advances its step counter.
-  if (R == 0 && !wait.epoch) return NVFP4_OK;
+                void *y_rows, int y_dtype, uint8_t *ws, cudaStream_t st) {
+  if (R == 0) return NVFP4_OK;
   const ExpertsLayout L = experts_layout(d, R);
   const int E = d.num_experts, H = d.hidden, I = d.intermediate;
   const ExpertPath path = choose_path(d, w, R);
@@ -161,9 +157,9 @@ int run_experts(const nvfp4_moe_desc &d, const nvfp4_moe_weights &w, const uint1
   // relative per element on the MMA operand).
   uint16_t *inter = reinterpret_cast<uint16_t *>(ws + L.inter);
   uint16_t *inter_lo = reinterpret_cast<uint16_t *>(ws + L.inter_lo);
-  int rc = check_launch(launch_moe_permute(row_expert, x_row_index, (int)R, E, tpi, plan, st, wait),
+  int rc = check_launch(launch_moe_permute(row_expert, x_row_index, (int)R, E, tpi, plan, st),
                         "MoE permutation launch");
-  if (rc || R == 0) return rc;
+  if (rc) return rc;
 
   if (path == ExpertPath::kGemv) {
     MoeGemvLaunch gu;
@@ -594,10 +590,6 @@ extern "C" int nvfp4_stack_rows(const void *const *srcs, const int64_t *rows, in
   return NVFP4_OK;
 }
 namespace nvfp4 {
-int ep_p2p_combine(const nvfp4_ep_peers *p, const int32_t *ids, const float *w, int64_t T,
-                   int32_t k, int32_t epr, const void *residual, void *y, int y_dtype,
-                   void *stream, int signal);
-int ep_p2p_step_wait(const nvfp4_ep_peers *p, PeerStepWait *w);
 namespace {
 
 // Workspace of the expert-parallel step through peer memory: the routing of
@@ -687,17 +679,14 @@ extern "C" int nvfp4_ep_p2p_forward(const nvfp4_moe_desc *d, const nvfp4_moe_wei
     if (rc) return rc;
   }
   if ((rc = nvfp4_ep_p2p_dispatch(p, ids, x, T, k, epr, stream))) return rc;
-  // The wait for every rank's dispatch runs in the permutation kernel.
-  PeerStepWait wait;
-  if ((rc = ep_p2p_step_wait(p, &wait))) return rc;
+  if ((rc = nvfp4_ep_p2p_wait_dispatch(p, stream))) return rc;
   void *recv_x = nullptr;
   int32_t *recv_e = nullptr;
   float *out = nullptr;
   if ((rc = nvfp4_ep_p2p_rows(p, T, k, &recv_x, &recv_e, &out))) return rc;
   rc = run_experts(ep_local_desc(*d, p->world), *local, static_cast<const uint16_t *>(recv_x),
-                   nullptr, recv_e, (int64_t)p->world * T * k, out, kF32, base + L.experts, st,
-                   wait);
+                   nullptr, recv_e, (int64_t)p->world * T * k, out, kF32, base + L.experts, st);
   if (rc) return rc;
-  // Done signal and combine in one launch.
-  return ep_p2p_combine(p, ids, tw, T, k, epr, residual, y, y_dtype, stream, 1);
+  if ((rc = nvfp4_ep_p2p_signal_done(p, stream))) return rc;
+  return nvfp4_ep_p2p_combine(p, ids, tw, T, k, epr, residual, y, y_dtype, stream);
 }
