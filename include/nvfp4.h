@@ -91,7 +91,8 @@ const char *nvfp4_last_error_string(void);
 /*
  * Status word of the tensor-core kernels, read (synchronously) and cleared:
  * 0 = no failure; > 0 = a kernel abandoned a bounded wait (1 TMA stage,
- * 2 decoded operands or blockscales, 3 stage release, 4 accumulator) and
+ * 2 decoded operands or blockscales, 3 stage release, 4 accumulator) or
+ * found its share of the work larger than its launch was sized for (5) and
  * returned early,
  * its output then being undefined; < 0 = the status could not be read.
  * No reference counterpart (the reference has no GPU kernel that runs).

@@ -145,7 +145,22 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(PeerTable P, const int
     if (d >= 0) {
       const uint4 *src = x + (int64_t)(s / k) * row_v;
       uint4 *dst = reinterpret_cast<uint4 *>(s_win[d] + P.off_x) + row * row_v;
-      for (int i = lane; i < row_v; i += 32) dst[i] = __ldcg(src + i);
+      // All of this lane's loads before any store: the store pointer may
+      // alias the loads as far as the compiler can tell, which would
+      // otherwise serialise one L2 round trip per 16 bytes.
+      for (int i0 = 0; i0 < row_v; i0 += 32 * 8) {
+        uint4 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int i = i0 + lane + 32 * j;
+          v[j] = i < row_v ? __ldcg(src + i) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int i = i0 + lane + 32 * j;
+          if (i < row_v) dst[i] = v[j];
+        }
+      }
     }
   }
   __threadfence_system();  // this thread's peer stores, before the block's count

@@ -32,6 +32,7 @@
 //     and the partial sums are multiplied by 2^-s (exact) before the reduction.
 //     Rows of x are stored with a 16-byte-unit XOR swizzle and a 64-byte pad,
 //     which makes the B-fragment loads (LDS.128) bank-conflict free.
+#include <algorithm>
 #include <cooperative_groups.h>
 #include <map>
 #include <mutex>
@@ -133,6 +134,8 @@ struct GemvArgs {
   const int *n_work;
   const int32_t *x_rows;   // kGvGateUp: slot -> activation row
   const int32_t *y_rows;   // kGvDown: slot -> output row
+  int ggroups;             // gemv_grouped_kernel: row groups per item
+  int max_items;           // gemv_grouped_kernel: items one CTA may meet
 };
 
 // Consumer view of one staged chunk: codes of rows g and g+8 of the warp's
@@ -320,6 +323,148 @@ struct GemvSmem {
   }
 };
 
+// Staging of an item's activations: M (<= 8) token rows of nunits 16-byte
+// units (8 consecutive k each) -> f16 in shared memory (row tt at xs + tt *
+// xstride, units XOR-swizzled), each token scaled by a power of two 2^s
+// chosen from its largest exponent (warp max, then shared atomicMax into
+// emax[], which must be zero on entry).  load(tt, u, v, vl) fetches unit u of
+// token tt (vl: the low part, kGvDown's x = hi + lo, kept as f16 hi + f16 lo).
+// Called by the nthr consumer threads (tid < nthr) together: they meet at
+// named barrier 1 between the two passes.  With `regs`, up to 4 units per
+// thread stay in registers (one read of the source); else the source is
+// read twice.  nunits is a multiple of 32, so every warp-wide test below is
+// uniform over the warp.
+template <int MODE, class Load>
+__device__ __forceinline__ void gv_stage_units(const Load &load, int M, int nunits, int xstride,
+                                               uint8_t *xs, uint8_t *xs_lo, int *emax, int tid,
+                                               int nthr, bool regs) {
+  constexpr bool kSplit = MODE == kGvDown;
+  const int total_units = M * nunits;
+  auto load_units = [&](int base, uint4 (&v)[4], uint4 (&vl)[4]) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = base + j * nthr;
+      v[j] = make_uint4(0u, 0u, 0u, 0u);
+      vl[j] = make_uint4(0u, 0u, 0u, 0u);
+      if (i < total_units) {
+        const int tt = i / nunits;
+        load(tt, i - tt * nunits, v[j], vl[j]);
+      }
+    }
+  };
+  // fp32 values of a unit (x, or hi + lo).
+  auto unit_f32 = [&](const uint4 &v, const uint4 &vl, float (&f)[8]) {
+    const uint32_t in[4] = {v.x, v.y, v.z, v.w};
+    const uint32_t il[4] = {vl.x, vl.y, vl.z, vl.w};
+#pragma unroll
+    for (int q2 = 0; q2 < 4; ++q2) {
+      f[2 * q2] = bf16lo(in[q2]);
+      f[2 * q2 + 1] = bf16hi(in[q2]);
+      if constexpr (kSplit) {
+        f[2 * q2] += bf16lo(il[q2]);
+        f[2 * q2 + 1] += bf16hi(il[q2]);
+      }
+    }
+  };
+  auto max_units = [&](int base, const uint4 (&v)[4], const uint4 (&vl)[4]) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = base + j * nthr;
+      if (i < total_units) {
+        uint32_t m;
+        if constexpr (kSplit) {
+          float f[8];
+          unit_f32(v[j], vl[j], f);
+          float mx = 0.0f;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) mx = fmaxf(mx, fabsf(f[e]));
+          m = (__float_as_uint(mx) >> 23) & 0xFFu;  // biased f32 exponent = bf16's
+        } else {
+          m = __vmaxu2(__vmaxu2(v[j].x & 0x7F807F80u, v[j].y & 0x7F807F80u),
+                       __vmaxu2(v[j].z & 0x7F807F80u, v[j].w & 0x7F807F80u));
+          m = max(m & 0xFFFFu, m >> 16) >> 7;
+        }
+        // The warp's 32 units belong to one token (nunits % 32 == 0).
+        m = __reduce_max_sync(0xffffffffu, m);
+        if ((tid & 31) == 0) atomicMax(&emax[i / nunits], (int)m);
+      }
+    }
+  };
+  auto convert_units = [&](int base, const uint4 (&v)[4], const uint4 (&vl)[4]) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = base + j * nthr;
+      if (i < total_units) {
+        const int tt = i / nunits, u = i - tt * nunits;
+        const int e = max(emax[tt], 1);  // biased exponent of max|x|
+        const int sc = min(max(141 - e, -126), 127);
+        const float fs = __int_as_float((sc + 127) << 23);
+        float f[8];
+        unit_f32(v[j], vl[j], f);
+        uint32_t o[4], ol[4];
+#pragma unroll
+        for (int q2 = 0; q2 < 4; ++q2) {
+          const float x0 = f[2 * q2] * fs, x1 = f[2 * q2 + 1] * fs;
+          const __half2 h2 = __floats2half2_rn(x0, x1);
+          o[q2] = *reinterpret_cast<const uint32_t *>(&h2);
+          if constexpr (kSplit) {
+            const __half2 l2 = __floats2half2_rn(x0 - __low2float(h2), x1 - __high2float(h2));
+            ol[q2] = *reinterpret_cast<const uint32_t *>(&l2);
+          }
+        }
+        const int off = tt * xstride + 16 * xs_unit(u);
+        *reinterpret_cast<uint4 *>(xs + off) = make_uint4(o[0], o[1], o[2], o[3]);
+        if constexpr (kSplit)
+          *reinterpret_cast<uint4 *>(xs_lo + off) = make_uint4(ol[0], ol[1], ol[2], ol[3]);
+      }
+    }
+  };
+  if (regs && total_units <= 4 * nthr) {
+    uint4 v[4], vl[4];
+    load_units(tid, v, vl);
+    max_units(tid, v, vl);
+    asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
+    convert_units(tid, v, vl);
+  } else {
+    for (int base = tid; base < total_units; base += 4 * nthr) {
+      uint4 v[4], vl[4];
+      load_units(base, v, vl);
+      max_units(base, v, vl);
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
+    for (int base = tid; base < total_units; base += 4 * nthr) {
+      uint4 v[4], vl[4];
+      load_units(base, v, vl);
+      convert_units(base, v, vl);
+    }
+  }
+}
+
+// gv_stage_units over the x slice [k0, k0 + ks) in global memory: kGvGateUp
+// reads token tt from row x_rows[slot0 + tt] (or slot0 + tt), kGvDown from
+// row slot0 + tt of x (+ x_lo), plain mode from row tt.
+template <int MODE>
+__device__ __forceinline__ void gv_stage_x(const GemvArgs &a, int slot0, int M, int k0, int ks,
+                                           int xstride, uint8_t *xs, uint8_t *xs_lo, int *emax,
+                                           int tid, int nthr) {
+  auto load = [&](int tt, int u, uint4 &v, uint4 &vl) {
+    int64_t row = tt;
+    if constexpr (MODE == kGvGateUp) row = a.x_rows ? __ldcg(a.x_rows + slot0 + tt) : slot0 + tt;
+    if constexpr (MODE == kGvDown) row = slot0 + tt;
+    const int64_t off = row * a.x_ld + k0 + 8 * u;
+    v = __ldcg(reinterpret_cast<const uint4 *>(a.x + off));
+    if constexpr (MODE == kGvDown) vl = __ldcg(reinterpret_cast<const uint4 *>(a.x_lo + off));
+  };
+  gv_stage_units<MODE>(load, M, ks / 8, xstride, xs, xs_lo, emax, tid, nthr, true);
+}
+
+// 1 / 2^s of token t's staging scale (0 for tokens >= M).
+__device__ __forceinline__ float gv_inv_scale(const int *emax, int t, int M) {
+  const int e = max(emax[t], 1);
+  const int sc = min(max(141 - e, -126), 127);
+  return t < M ? __frcp_rn(__int_as_float((sc + 127) << 23)) : 0.0f;
+}
+
 // Cluster q of a K split into gridDim.x slices owns row tiles
 // [q * nt / nq, (q + 1) * nt / nq) (nq = gridDim.y clusters, nt = 16-row
 // tiles; in kGvGateUp a "tile" is a pair: gate rows and the matching up
@@ -452,122 +597,9 @@ __global__ void __launch_bounds__(32 * (kGvMaxWarps + 1), 2)
     if constexpr (MODE == kGvPlain) asm volatile("griddepcontrol.wait;" ::: "memory");
   } else {
     if constexpr (MODE == kGvPlain) asm volatile("griddepcontrol.wait;" ::: "memory");
-    // x slice -> f16 with a per-token power-of-two scale.  The M * ks / 8
-    // 16-byte units of the slice are spread over all consumer threads: the
-    // largest exponent per token is taken with shared atomicMax, then the
-    // units are converted (kGvDown: x = hi + lo, kept as f16 hi + f16 lo).
-    // Up to 4 units per thread stay in registers (one read of x); beyond
-    // that x is read twice.
-    const int nunits = a.ks / 8, total_units = M * nunits, nthr = 32 * W;
-    auto xrow_of = [&](int tt) -> int64_t {
-      if constexpr (MODE == kGvGateUp) return a.x_rows ? __ldcg(a.x_rows + slot0 + tt) : slot0 + tt;
-      if constexpr (MODE == kGvDown) return slot0 + tt;
-      return tt;
-    };
-    auto load_units = [&](int base, uint4 (&v)[4], uint4 (&vl)[4]) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int i = base + j * nthr;
-        v[j] = make_uint4(0u, 0u, 0u, 0u);
-        vl[j] = make_uint4(0u, 0u, 0u, 0u);
-        if (i < total_units) {
-          const int tt = i / nunits, u = i - tt * nunits;
-          const int64_t off = xrow_of(tt) * a.x_ld + k0 + 8 * u;
-          v[j] = __ldcg(reinterpret_cast<const uint4 *>(a.x + off));
-          if constexpr (kSplit) vl[j] = __ldcg(reinterpret_cast<const uint4 *>(a.x_lo + off));
-        }
-      }
-    };
-    // fp32 values of a unit (x, or hi + lo).
-    auto unit_f32 = [&](const uint4 &v, const uint4 &vl, float (&f)[8]) {
-      const uint32_t in[4] = {v.x, v.y, v.z, v.w};
-      const uint32_t il[4] = {vl.x, vl.y, vl.z, vl.w};
-#pragma unroll
-      for (int q2 = 0; q2 < 4; ++q2) {
-        f[2 * q2] = bf16lo(in[q2]);
-        f[2 * q2 + 1] = bf16hi(in[q2]);
-        if constexpr (kSplit) {
-          f[2 * q2] += bf16lo(il[q2]);
-          f[2 * q2 + 1] += bf16hi(il[q2]);
-        }
-      }
-    };
-    auto max_units = [&](int base, const uint4 (&v)[4], const uint4 (&vl)[4]) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int i = base + j * nthr;
-        if (i < total_units) {
-          uint32_t m;
-          if constexpr (kSplit) {
-            float f[8];
-            unit_f32(v[j], vl[j], f);
-            float mx = 0.0f;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) mx = fmaxf(mx, fabsf(f[e]));
-            m = (__float_as_uint(mx) >> 23) & 0xFFu;  // biased f32 exponent = bf16's
-          } else {
-            m = __vmaxu2(__vmaxu2(v[j].x & 0x7F807F80u, v[j].y & 0x7F807F80u),
-                         __vmaxu2(v[j].z & 0x7F807F80u, v[j].w & 0x7F807F80u));
-            m = max(m & 0xFFFFu, m >> 16) >> 7;
-          }
-          atomicMax(&emax[i / nunits], (int)m);
-        }
-      }
-    };
-    auto convert_units = [&](int base, const uint4 (&v)[4], const uint4 (&vl)[4]) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int i = base + j * nthr;
-        if (i < total_units) {
-          const int tt = i / nunits, u = i - tt * nunits;
-          const int e = max(emax[tt], 1);  // biased exponent of max|x|
-          const int sc = min(max(141 - e, -126), 127);
-          const float fs = __int_as_float((sc + 127) << 23);
-          float f[8];
-          unit_f32(v[j], vl[j], f);
-          uint32_t o[4], ol[4];
-#pragma unroll
-          for (int q2 = 0; q2 < 4; ++q2) {
-            const float x0 = f[2 * q2] * fs, x1 = f[2 * q2 + 1] * fs;
-            const __half2 h2 = __floats2half2_rn(x0, x1);
-            o[q2] = *reinterpret_cast<const uint32_t *>(&h2);
-            if constexpr (kSplit) {
-              const __half2 l2 =
-                  __floats2half2_rn(x0 - __low2float(h2), x1 - __high2float(h2));
-              ol[q2] = *reinterpret_cast<const uint32_t *>(&l2);
-            }
-          }
-          const int off = tt * a.xstride + 16 * xs_unit(u);
-          *reinterpret_cast<uint4 *>(xs + off) = make_uint4(o[0], o[1], o[2], o[3]);
-          if constexpr (kSplit)
-            *reinterpret_cast<uint4 *>(xs_lo + off) = make_uint4(ol[0], ol[1], ol[2], ol[3]);
-        }
-      }
-    };
-    if (total_units <= 4 * nthr) {
-      uint4 v[4], vl[4];
-      load_units(tid, v, vl);
-      max_units(tid, v, vl);
-      asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
-      convert_units(tid, v, vl);
-    } else {
-      for (int base = tid; base < total_units; base += 4 * nthr) {
-        uint4 v[4], vl[4];
-        load_units(base, v, vl);
-        max_units(base, v, vl);
-      }
-      asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
-      for (int base = tid; base < total_units; base += 4 * nthr) {
-        uint4 v[4], vl[4];
-        load_units(base, v, vl);
-        convert_units(base, v, vl);
-      }
-    }
-    if (tid < kGvTok) {
-      const int e = max(emax[tid], 1);
-      const int sc = min(max(141 - e, -126), 127);
-      inv_scale[tid] = tid < M ? __frcp_rn(__int_as_float((sc + 127) << 23)) : 0.0f;
-    }
+    // x slice -> f16 with a per-token power-of-two scale (gv_stage_x).
+    gv_stage_x<MODE>(a, slot0, M, k0, a.ks, a.xstride, xs, xs_lo, emax, tid, 32 * W);
+    if (tid < kGvTok) inv_scale[tid] = gv_inv_scale(emax, tid, M);
     asm volatile("bar.sync 1, %0;" ::"r"(32 * W) : "memory");  // consumer warps only
     // The next kernel in the stream may start its prologue now.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -683,6 +715,356 @@ __global__ void __launch_bounds__(32 * (kGvMaxWarps + 1), 2)
         else
           reinterpret_cast<float *>(a.y)[row * a.y_ld + n] = v[0];
       }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Persistent grouped GEMV of the MoE experts (kGvGateUp / kGvDown).
+//
+// The work of one call is n_work items (expert, up to 8 token slots) x G row
+// groups of the expert's matrix; a "unit" is one (item, row group) over the
+// whole K.  The grid is one CTA per SM; CTA b takes the contiguous unit range
+// [b U / P, (b + 1) U / P) of the U = n_work * G units (item-major, so a CTA
+// meets few item changes and the items of one expert run side by side, their
+// weights shared through L2).  Row group q of an expert owns tiles
+// [q nt / G, (q + 1) nt / G): the groups differ by at most one tile, which
+// the two tensor maps (W and W - 1 tiles per part) cover.
+//
+// Nothing on the consumer warps' path reads global memory, whose latency
+// under the kernel's own TMA stream is several microseconds:
+//   * at the start, all threads load the CTA's items into a shared table
+//     (expert, slots, input_scale, the slots' activation or output rows);
+//   * the producer warp streams the 256-k chunks of unit after unit through
+//     one S-stage ring (so the TMA queue stays full across unit boundaries),
+//     and with a unit's first chunk the unit's weight_scale_2 rows;
+//   * for each item it copies the item's bf16 activation rows into shared
+//     memory with bulk copies (one item ahead), which the consumers then
+//     convert to scaled f16 in shared memory (gv_stage_units);
+//   * the consumer warps (one per 16-row tile of the row group; gate and up
+//     tiles of the same rows in kGvGateUp) accumulate over all of K in
+//     registers (no K split, no cluster reduction) and write their rows at
+//     the end of the unit.
+// ---------------------------------------------------------------------------
+constexpr int kGgSmemCap = 226 * 1024 - 64;  // dynamic smem: 227 KB less the static 1 KB
+constexpr int kGgMaxStages = 8;
+constexpr int kGgMaxItems = 64;  // items one CTA may meet (the shared table)
+
+// One row of the item table: expert, first slot, slots, alpha's input_scale
+// and, per slot, the activation row (kGvGateUp) or output row (kGvDown).
+struct GgItem {
+  int g, slot0, M;
+  float ins;
+  int rows[kGvTok];
+};
+
+// Shared memory of a grouped CTA with w consumer warps, `stages` ring stages
+// (each: codes, blockscales and the weight_scale_2 rows of w tiles), K and
+// at most `items` items: the ring, the f16 activations of one item (twice
+// for hi + lo), the bf16 rows they are converted from (twice for hi + lo),
+// kGvGateUp's two alternating buffers of per-row partial sums ([part][16 w /
+// 2 rows][8 tokens] fp32), the token scales, the item table, the mbarriers.
+struct GgSmem {
+  int stage, codes, ws2, xstride, xs, xs_lo, raw, raw_lo, recv, inv, emax, items, bars, total;
+  __host__ __device__ GgSmem(int w, int stages, int K, int parts, bool split, int n_items) {
+    codes = w * kGvTileCodes;
+    ws2 = codes + w * kGvTileScales;
+    stage = (ws2 + 64 * w + 1023) & ~1023;
+    xstride = 2 * K + 64;
+    xs = stages * stage;
+    xs_lo = xs + kGvTok * xstride;
+    raw = xs_lo + (split ? kGvTok * xstride : 0);
+    raw_lo = raw + kGvTok * 2 * K;
+    recv = raw_lo + (split ? kGvTok * 2 * K : 0);
+    inv = recv + (parts == 2 ? (int)sizeof(float) * 2 * 16 * w * kGvTok : 0);
+    emax = inv + (int)sizeof(float) * kGvTok;
+    items = emax + (int)sizeof(int) * kGvTok;
+    bars = (items + (int)sizeof(GgItem) * n_items + 7) & ~7;
+    total = bars + 16 * stages + 16;
+  }
+};
+
+template <int MODE>
+__global__ void __launch_bounds__(32 * (kGvMaxWarps + 1), 1)
+    gemv_grouped_kernel(const __grid_constant__ CUtensorMap tmW_hi,
+                        const __grid_constant__ CUtensorMap tmS_hi,
+                        const __grid_constant__ CUtensorMap tmW_lo,
+                        const __grid_constant__ CUtensorMap tmS_lo, GemvArgs a) {
+  static_assert(MODE == kGvGateUp || MODE == kGvDown, "grouped modes only");
+  constexpr bool kSplit = MODE == kGvDown;
+  constexpr int kParts = MODE == kGvGateUp ? 2 : 1;
+  extern __shared__ __align__(1024) uint8_t gsm_raw[];
+  uint8_t *gsm = reinterpret_cast<uint8_t *>(((uintptr_t)gsm_raw + 1023) & ~(uintptr_t)1023);
+  __shared__ int abort_flag;
+
+  const int W = (int)(blockDim.x >> 5) - 1;  // consumer warps = kParts * tiles of a full group
+  const int S = a.stages;
+  const GgSmem L(W, S, a.K, kParts, kSplit, a.max_items);
+  uint8_t *ring = gsm;
+  uint8_t *xs = gsm + L.xs;
+  uint8_t *xs_lo = gsm + L.xs_lo;
+  float *recv = reinterpret_cast<float *>(gsm + L.recv);
+  float *inv_scale = reinterpret_cast<float *>(gsm + L.inv);
+  int *emax = reinterpret_cast<int *>(gsm + L.emax);
+  GgItem *tab = reinterpret_cast<GgItem *>(gsm + L.items);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(gsm + L.bars);  // full[S], empty[S], x full, x empty
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int gq = lane >> 2, c = lane & 3;
+  const int G = a.ggroups;
+  const int nt = (MODE == kGvGateUp ? a.N / 2 : a.N + 15) / 16;
+  const int nch = a.K / kGvChunk;
+  const int rowb = 2 * a.K;  // bytes of one bf16 activation row
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + S);
+  const uint32_t xfull = smem_u32(bars + 2 * S), xempty = smem_u32(bars + 2 * S + 1);
+  const bool ws2_copy = a.al.ws2_rows != nullptr;
+  volatile int *abort = &abort_flag;
+
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, W);  // every consumer warp releases every stage
+    }
+    mbar_init(xfull, 1);
+    mbar_init(xempty, 1);
+    abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (tid < kGvTok) emax[tid] = 0;
+  // The work items come from the previous kernel (griddepcontrol.wait), and
+  // so do the activations.  The next kernel may launch now: its CTAs take
+  // the SMs this grid's CTAs leave and wait for this grid's completion.
+  pdl_wait();
+  pdl_trigger();
+  const int64_t U = (int64_t)__ldcg(a.n_work) * G;
+  const int P = gridDim.x, b = blockIdx.x;
+  const int u_begin = (int)(U * b / P), u_end = (int)(U * (b + 1) / P);
+  if (u_begin >= u_end) return;
+  const int i0 = u_begin / G, n_items = (u_end - 1) / G - i0 + 1;
+  if (n_items > a.max_items) {  // the launch sized the table for fewer items
+    if (tid == 0) atomicCAS(&g_gemv_status, 0, (int)kDevBadPlan);
+    return;
+  }
+  for (int j = tid; j < n_items; j += blockDim.x) {
+    const int *it = reinterpret_cast<const int *>(a.work + i0 + j);
+    GgItem e;
+    e.g = __ldcg(it);
+    e.slot0 = __ldcg(it + 1);
+    e.M = __ldcg(it + 2);
+    e.ins = a.al.input_scales ? __ldg(a.al.input_scales + e.g) : a.al.input_scale;
+    const int32_t *map = MODE == kGvGateUp ? a.x_rows : a.y_rows;
+#pragma unroll
+    for (int t = 0; t < kGvTok; ++t)
+      e.rows[t] = t < e.M ? (map ? __ldcg(map + e.slot0 + t) : e.slot0 + t) : 0;
+    tab[j] = e;
+  }
+  __syncthreads();
+  auto tile_lo = [&](int q) { return (int)((int64_t)q * nt / G); };
+
+  if (warp == W) {
+    // Producer: one thread issues the bulk copies of every item's activation
+    // rows and the TMA loads of every chunk of every unit, up to S chunks
+    // ahead of the consumers.
+    if (lane == 0) {
+      const uint64_t pol = l2_evict_first_policy();
+      prefetch_tmap(&tmW_hi);
+      prefetch_tmap(&tmS_hi);
+      prefetch_tmap(&tmW_lo);
+      prefetch_tmap(&tmS_lo);
+      int gc = 0, k = 0;
+      bool alive = true;
+      for (int u = u_begin; u < u_end && alive; ++u) {
+        const int q = u % G;
+        const GgItem &e = tab[u / G - i0];
+        if (u == u_begin || q == 0) {
+          // The item's activation rows, once the consumers have converted the
+          // previous item's.
+          if (k > 0 && !mbar_wait(xempty, (k - 1) & 1, &g_gemv_status, kDevTimeoutEmpty, abort)) {
+            alive = false;
+            break;
+          }
+          mbar_arrive_expect_tx(xfull, e.M * rowb * (kSplit ? 2 : 1));
+          const uint32_t raw = smem_u32(gsm + L.raw), raw_lo = smem_u32(gsm + L.raw_lo);
+          for (int t = 0; t < e.M; ++t) {
+            const int64_t row = MODE == kGvGateUp ? e.rows[t] : e.slot0 + t;
+            bulk_load(raw + t * rowb, a.x + row * a.x_ld, rowb, xfull);
+            if constexpr (kSplit) bulk_load(raw_lo + t * rowb, a.x_lo + row * a.x_ld, rowb, xfull);
+          }
+          ++k;
+        }
+        const int tile0 = tile_lo(q), ntiles = tile_lo(q + 1) - tile0;
+        const bool full_count = kParts * ntiles == W;
+        const CUtensorMap *tmW = full_count ? &tmW_hi : &tmW_lo;
+        const CUtensorMap *tmS = full_count ? &tmS_hi : &tmS_lo;
+        const int64_t grow0 = (int64_t)e.g * a.N + 16 * tile0;
+        for (int ch = 0; ch < nch; ++ch, ++gc) {
+          const int s = gc % S, r = gc / S;
+          if (r > 0 && !mbar_wait(empty0 + 8 * s, (r - 1) & 1, &g_gemv_status, kDevTimeoutEmpty,
+                                  abort)) {
+            alive = false;
+            break;
+          }
+          const uint32_t st = smem_u32(ring + s * L.stage);
+          const bool w2 = ch == 0 && ws2_copy;
+          mbar_arrive_expect_tx(full0 + 8 * s, kParts * ntiles * (kGvTileCodes + kGvTileScales +
+                                                                  (w2 ? 64 : 0)));
+#pragma unroll
+          for (int part = 0; part < kParts; ++part) {
+            const int row = (int)(grow0 + (part ? a.N / 2 : 0));
+            tma_load_2d_hint(st + part * ntiles * kGvTileCodes, tmW, ch * (kGvChunk / 2), row,
+                             full0 + 8 * s, pol);
+            tma_load_2d_hint(st + L.codes + part * ntiles * kGvTileScales, tmS,
+                             ch * (kGvChunk / kGroup), row, full0 + 8 * s, pol);
+            if (w2)
+              bulk_load(st + L.ws2 + part * ntiles * 64,
+                        a.al.ws2_rows + (int64_t)e.g * a.al.ws2_group_stride + 16 * tile0 +
+                            (part ? a.N / 2 : 0),
+                        ntiles * 64, full0 + 8 * s);
+          }
+        }
+      }
+      // Wait (bounded) for the copies still in flight before the CTA exits.
+      volatile int no_abort = 0;
+      for (int i = max(gc - S, 0); i < gc; ++i)
+        mbar_wait(full0 + 8 * (i % S), (i / S) & 1, &g_gemv_status, kDevTimeoutFull, &no_abort);
+      if (k > 0) mbar_wait(xfull, (k - 1) & 1, &g_gemv_status, kDevTimeoutFull, &no_abort);
+    }
+    return;
+  }
+
+  // Consumers.  Every consumer warp takes every named barrier of every unit
+  // (after a timeout they skip the waits and the math, not the barriers).
+  const int nthr = 32 * W;
+  const uint8_t *raw = gsm + L.raw, *raw_lo = gsm + L.raw_lo;
+  auto load_raw = [&](int tt, int u, uint4 &v, uint4 &vl) {
+    v = *reinterpret_cast<const uint4 *>(raw + tt * rowb + 16 * u);
+    if constexpr (kSplit) vl = *reinterpret_cast<const uint4 *>(raw_lo + tt * rowb + 16 * u);
+  };
+  int gc = 0, k = 0, buf = 0;
+  bool ok_all = true;
+  for (int u = u_begin; u < u_end; ++u) {
+    const int q = u % G;
+    const GgItem &e = tab[u / G - i0];
+    const int g = e.g, slot0 = e.slot0, M = e.M;
+    const float ins = e.ins;
+    if (u == u_begin || q == 0) {
+      asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");  // xs of the last item is dead
+      if (ok_all) {
+        const bool ok = mbar_wait(xfull, k & 1, &g_gemv_status, kDevTimeoutFull, abort);
+        ok_all = __all_sync(0xffffffffu, ok);
+      }
+      // Its barriers are taken by all; a warp that gave up converts garbage.
+      gv_stage_units<MODE>(load_raw, M, a.K / 8, L.xstride, xs, xs_lo, emax, tid, nthr, false);
+      fence_proxy_async_smem();  // the reads of raw before the next item's bulk copies
+      asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");  // emax complete, raw read
+      if (tid < kGvTok) {
+        inv_scale[tid] = gv_inv_scale(emax, tid, M);
+        emax[tid] = 0;  // for the next item
+      }
+      if (tid == 0) mbar_arrive(xempty);
+      asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
+      ++k;
+    }
+    const int tile0 = tile_lo(q), ntiles = tile_lo(q + 1) - tile0;
+    const bool has_tile = warp < kParts * ntiles;
+    const int rows = 16 * ntiles;
+    // weight_scale_2 of the epilogue's rows, read from the unit's first stage:
+    // kGvDown, this lane's rows (h = 0, 1); kGvGateUp, the gate and up rows of
+    // this thread's first two (row, token) elements.
+    float w2a[2] = {a.al.ws2, a.al.ws2}, w2b[2] = {a.al.ws2, a.al.ws2};
+    const bool has_x = gq < M;  // tokens >= M: zero B fragments
+    const uint32_t xrow = smem_u32(xs + (has_x ? gq : 0) * L.xstride);
+    const uint32_t xrow_lo = smem_u32(xs_lo + (has_x ? gq : 0) * L.xstride);
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int ch = 0; ch < nch; ++ch, ++gc) {
+      const int s = gc % S, r = gc / S;
+      if (!ok_all) continue;
+      const bool ok = mbar_wait(full0 + 8 * s, r & 1, &g_gemv_status, kDevTimeoutFull, abort);
+      ok_all = __all_sync(0xffffffffu, ok);
+      if (!ok_all) continue;
+      const uint32_t st = smem_u32(ring + s * L.stage);
+      if (ch == 0 && ws2_copy) {
+        const float *w2s = reinterpret_cast<const float *>(ring + s * L.stage + L.ws2);
+        if constexpr (MODE == kGvDown) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) w2a[h] = w2s[16 * warp + gq + 8 * h];
+        } else {
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int i = tid + j * nthr;
+            w2a[j] = w2s[i % rows];
+            w2b[j] = w2s[rows + i % rows];
+          }
+        }
+      }
+      GemvChunk bch;
+      if (has_tile)
+        gemv_fetch(bch, st + warp * kGvTileCodes, st + L.codes + warp * kGvTileScales, gq, c);
+      fence_proxy_async_smem();  // generic reads before the TMA refill (see gemv_kernel)
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty0 + 8 * s);
+      if (has_tile) {
+        float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        gemv_compute<kSplit>(bch, part, xrow, xrow_lo, has_x, ch, c);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[i] += part[i];
+      }
+    }
+    const float is0 = inv_scale[2 * c], is1 = inv_scale[2 * c + 1];
+    if constexpr (MODE == kGvDown) {
+      if (has_tile) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int n = 16 * (tile0 + warp) + gq + 8 * h;
+          if (n >= a.N) continue;
+          const float al = ins * w2a[h];
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            const int tok = 2 * c + t;
+            if (tok >= M) continue;
+            const float v = acc[2 * h + t] * (t ? is1 : is0) * al;
+            const int64_t row = e.rows[tok];
+            if (a.y_dtype == kBF16)
+              reinterpret_cast<uint16_t *>(a.y)[row * a.y_ld + n] = f32_to_bf16_bits(v);
+            else
+              reinterpret_cast<float *>(a.y)[row * a.y_ld + n] = v;
+          }
+        }
+      }
+    } else {
+      // Gate and up sums of the unit's rows meet in shared memory (buffer
+      // `buf`; the two buffers alternate, so one barrier per unit orders the
+      // writes of a unit after the reads of the unit two back).
+      const int half = 16 * (W / 2);  // rows per part in a buffer
+      float *rb = recv + buf * (2 * half * kGvTok);
+      if (has_tile) {
+        const int part = warp / ntiles, wt = warp - part * ntiles;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          float *dst = rb + ((size_t)part * half + wt * 16 + gq + 8 * h) * kGvTok + 2 * c;
+          dst[0] = acc[2 * h] * is0;
+          dst[1] = acc[2 * h + 1] * is1;
+        }
+      }
+      asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
+      // rows * M <= 2 * nthr (rows <= 16 W / 2, M <= 8, nthr = 32 W).
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int i = tid + j * nthr;
+        if (i >= rows * M) break;
+        const int r = i % rows, tok = i / rows;
+        const int n = 16 * tile0 + r;
+        const float vg = rb[(size_t)r * kGvTok + tok] * (ins * w2a[j]);
+        const float vu = rb[((size_t)half + r) * kGvTok + tok] * (ins * w2b[j]);
+        // silu(gate) * up as bf16 hi + lo (the down projection's operand).
+        const float o = silu_f32(vg) * vu;
+        const uint16_t hb = f32_to_bf16_bits(o);
+        const float hf = __uint_as_float((uint32_t)hb << 16);
+        const int64_t idx = (int64_t)(slot0 + tok) * a.y_ld + n;
+        reinterpret_cast<uint16_t *>(a.y)[idx] = hb;
+        a.y_lo[idx] = f32_to_bf16_bits(o - hf);
+      }
+      buf ^= 1;
     }
   }
 }
@@ -858,6 +1240,92 @@ cudaError_t launch_mode(GemvArgs a, int items, int64_t total_rows, cudaStream_t 
   return cudaLaunchKernelEx(&cfg, gemv_kernel<MODE>, tm[0], tm[1], tm[2], tm[3], a);
 }
 
+// Plan of the persistent grouped kernel: row groups G per item, consumer
+// warps W, ring stages S (as many as fit beside one item's activations, at
+// most kGgMaxStages), grid P and the item-table size.  False when the shapes
+// or alignments do not suit it (then one cluster grid per item runs).
+struct GgPlan {
+  int G, W, S, P, max_items;
+};
+
+template <int MODE>
+bool grouped_plan(const GemvArgs &a, int items, GgPlan &p) {
+  constexpr int kParts = MODE == kGvGateUp ? 2 : 1;
+  constexpr bool kSplit = MODE == kGvDown;
+  const int N = a.N, K = a.K;
+  const int nt = (MODE == kGvGateUp ? N / 2 : N + 15) / 16;
+  const int max_tiles = kGvMaxWarps / kParts;
+  auto al16 = [](const void *q) { return ((uintptr_t)q & 15) == 0; };
+  // Bulk copies: 16-byte aligned activation rows; weight_scale_2 rows in
+  // 64-byte tiles (16 rows), each part's at a multiple of 16 rows.
+  if (nt <= 0 || K % kGvChunk || N % 32 || !al16(a.x) || (a.x_ld * 2) % 16 ||
+      (kSplit && !al16(a.x_lo)) ||
+      (a.al.ws2_rows && (!al16(a.al.ws2_rows) || a.al.ws2_group_stride % 16)))
+    return false;
+  p.G = (nt + max_tiles - 1) / max_tiles;
+  p.W = kParts * ((nt + p.G - 1) / p.G);
+  const int64_t units = (int64_t)items * p.G;
+  p.P = (int)std::min<int64_t>(tc_sm_count(), units);
+  if (p.P <= 0) return false;
+  // A CTA's units span at most ceil(units / P) / G + 2 items.
+  p.max_items = (int)(((units + p.P - 1) / p.P + p.G - 1) / p.G + 2);
+  if (p.max_items > kGgMaxItems) return false;
+  p.S = kGgMaxStages;
+  while (p.S >= 2 &&
+         1024 + GgSmem(p.W, p.S, K, kParts, kSplit, p.max_items).total > kGgSmemCap)
+    --p.S;
+  return p.S >= 2;
+}
+
+template <int MODE>
+cudaError_t launch_grouped(GemvArgs a, const GgPlan &p, int64_t total_rows, cudaStream_t st) {
+  constexpr int kParts = MODE == kGvGateUp ? 2 : 1;
+  constexpr bool kSplit = MODE == kGvDown;
+  {
+    static std::mutex mu;
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!attr_set[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(gemv_grouped_kernel<MODE>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           kGgSmemCap);
+      if (e != cudaSuccess) return e;
+      attr_set[dev] = true;
+    }
+  }
+  a.ks = a.K;
+  a.stages = p.S;
+  a.ggroups = p.G;
+  a.max_items = p.max_items;
+  // Boxes of W / kParts and one tile fewer per part (row groups differ by at
+  // most one tile).
+  CUtensorMap tm[4];
+  for (int i = 0; i < 2; ++i) {
+    const int t = p.W / kParts - i;
+    const int rows = 16 * (t > 0 ? t : 1);
+    if (!make_tmap_2d(&tm[2 * i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.w, total_rows, a.K / 2,
+                      a.K / 2, kGvChunk / 2, rows, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_tmap_2d(&tm[2 * i + 1], CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.sf, total_rows,
+                      a.K / kGroup, a.K / kGroup, kGvChunk / kGroup, rows,
+                      CU_TENSOR_MAP_SWIZZLE_NONE))
+      return cudaErrorInvalidValue;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.P, 1, 1);
+  cfg.blockDim = dim3(32 * (p.W + 1), 1, 1);
+  cfg.dynamicSmemBytes = 1024 + (size_t)GgSmem(p.W, p.S, a.K, kParts, kSplit, p.max_items).total;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemv_grouped_kernel<MODE>, tm[0], tm[1], tm[2], tm[3], a);
+}
+
 }  // namespace
 
 bool gemv_supported(int M, int K, const void *w, const void *sf, const void *x, int64_t x_ld) {
@@ -924,6 +1392,13 @@ cudaError_t launch_moe_gemv(const MoeGemvLaunch &m, cudaStream_t st) {
   a.x_rows = m.x_rows;
   a.y_rows = m.y_rows;
   const int64_t total_rows = (int64_t)m.groups * m.N;
+  // The persistent kernel when one item's activations fit beside a ring of
+  // two or more stages; else one cluster grid per item (K split over CTAs).
+  GgPlan p;
+  if (m.gate_up && grouped_plan<kGvGateUp>(a, m.items, p))
+    return launch_grouped<kGvGateUp>(a, p, total_rows, st);
+  if (!m.gate_up && grouped_plan<kGvDown>(a, m.items, p))
+    return launch_grouped<kGvDown>(a, p, total_rows, st);
   return m.gate_up ? launch_mode<kGvGateUp>(a, m.items, total_rows, st)
                    : launch_mode<kGvDown>(a, m.items, total_rows, st);
 }

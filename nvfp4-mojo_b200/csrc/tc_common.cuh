@@ -19,6 +19,7 @@ enum DeviceStatus : int {
   kDevTimeoutDec = 2,    // waited too long for decoded operands
   kDevTimeoutEmpty = 3,  // waited too long for the MMA to release a stage
   kDevTimeoutAcc = 4,    // waited too long for the accumulator
+  kDevBadPlan = 5,       // a CTA's share of the work exceeds what its launch was sized for
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -111,6 +112,17 @@ __device__ __forceinline__ void tma_load_2d_hint(uint32_t dst, const CUtensorMap
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       ".L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar), "l"(policy)
+      : "memory");
+}
+
+// Untiled bulk copy of `bytes` (a multiple of 16) from global memory to this
+// CTA's shared memory, completing on `bar`; both addresses 16-byte aligned.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes,
+                                          uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
       : "memory");
 }
 
