@@ -30,8 +30,11 @@
 //     max|x| * 2^s lies in [2^14, 2^15): bf16 values are then exact in f16
 //     (apart from elements below max|x| * 2^-28, which become f16 subnormals),
 //     and the partial sums are multiplied by 2^-s (exact) before the reduction.
-//     Rows of x are stored with a 16-byte-unit XOR swizzle and a 64-byte pad,
-//     which makes the B-fragment loads (LDS.128) bank-conflict free.
+//     Rows of x are stored with their 16-byte units permuted within each
+//     chunk (lane quad c's unit p of the chunk at 4p + c) and a 64-byte pad:
+//     the B-fragment loads (LDS.128) are bank-conflict free and a lane's 8
+//     loads of a chunk sit at one base plus immediate offsets.  Lanes of
+//     tokens >= M read a zeroed row instead.
 #include <algorithm>
 #include <cooperative_groups.h>
 #include <map>
@@ -81,14 +84,6 @@ __device__ __forceinline__ uint32_t scale_pair_f16x2(uint32_t sw, int h) {
   return r;
 }
 
-// a * (s.lo, s.lo) or a * (s.hi, s.hi): the broadcast folds into the multiply.
-__device__ __forceinline__ uint32_t hmul2_bcast(uint32_t a, uint32_t s, int hi) {
-  const __half2 av = *reinterpret_cast<const __half2 *>(&a);
-  const __half2 sv = *reinterpret_cast<const __half2 *>(&s);
-  const __half2 r = __hmul2(av, hi ? __high2half2(sv) : __low2half2(sv));
-  return *reinterpret_cast<const uint32_t *>(&r);
-}
-
 __device__ __forceinline__ void mma_f16_16816(float (&c)[4], uint32_t a0, uint32_t a1,
                                               uint32_t a2, uint32_t a3, uint32_t b0,
                                               uint32_t b1) {
@@ -104,8 +99,11 @@ __device__ __forceinline__ float *cluster_map(float *p, int rank) {
   return cg::this_cluster().map_shared_rank(p, rank);
 }
 
-// Physical 16-byte unit of logical unit u in a token row of x (XOR swizzle).
-__device__ __forceinline__ int xs_unit(int u) { return u ^ ((u >> 3) & 3); }
+// Physical 16-byte unit of logical unit u = 32 ch + 8 c + p (c < 4, p < 8)
+// in a token row of x: 32 ch + 4 p + c.
+__device__ __forceinline__ int xs_unit(int u) {
+  return (u & ~31) | ((u & 7) << 2) | ((u >> 3) & 3);
+}
 
 // Kernel modes: the plain linear, and the two grouped MoE expert GEMMs over
 // work items (expert, up to 8 token slots) from the MoE permutation.
@@ -160,31 +158,42 @@ __device__ __forceinline__ void gemv_fetch(GemvChunk &b, uint32_t codes, uint32_
   b.sh = lds_u32(scales + 16u * (rl + 8) + 4u * c);
 }
 
+// f16 multiply of the pair a by a scale pair already broadcast.
+__device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t s) {
+  const __half2 r = __hmul2(*reinterpret_cast<const __half2 *>(&a),
+                            *reinterpret_cast<const __half2 *>(&s));
+  return *reinterpret_cast<const uint32_t *>(&r);
+}
+
+// (s.lo, s.lo) and (s.hi, s.hi) of an f16 pair.
+__device__ __forceinline__ uint32_t bcast_lo(uint32_t s) { return __byte_perm(s, 0, 0x1010); }
+__device__ __forceinline__ uint32_t bcast_hi(uint32_t s) { return __byte_perm(s, 0, 0x3232); }
+
 // One 256-k chunk of a warp's tile; SPLIT adds the MMAs of the low parts.
+// xb (xb_lo): this lane's x units of the chunk, logical 32 ch + 8 c + p at
+// xb + 64 p (xs_unit), i.e. xrow + 16 (32 ch + c).
 template <bool SPLIT>
-__device__ __forceinline__ void gemv_compute(const GemvChunk &b, float (&acc)[4], uint32_t xrow,
-                                             uint32_t xrow_lo, bool has_x, int ch, int c) {
-  // This lane's x units for the chunk: logical 32*ch + 8c + p, p = 0..7.
-  const int ub = 32 * ch + 8 * c;
+__device__ __forceinline__ void gemv_compute(const GemvChunk &b, float (&acc)[4], uint32_t xb,
+                                             uint32_t xb_lo) {
 #pragma unroll
   for (int hh = 0; hh < 2; ++hh) {  // blockscales 2hh, 2hh+1 of the lane's 64 k
     const uint32_t s_g = scale_pair_f16x2(b.sg, hh), s_h = scale_pair_f16x2(b.sh, hh);
+    const uint32_t sg[2] = {bcast_lo(s_g), bcast_hi(s_g)}, sh[2] = {bcast_lo(s_h), bcast_hi(s_h)};
 #pragma unroll
     for (int p4 = 0; p4 < 4; ++p4) {  // code word p = 4hh + p4: MMAs j = 2p, 2p+1
       const int p = 4 * hh + p4, hi = p4 >> 1;  // blockscale q = p / 2 = 2hh + hi
-      const uint32_t xo = 16u * (uint32_t)xs_unit(ub + p);
-      const uint4 xv = has_x ? lds_v4(xrow + xo) : make_uint4(0u, 0u, 0u, 0u);
+      const uint4 xv = lds_v4(xb + 64u * p);
       uint32_t dg[4], dh[4];
       e2m1x8_to_f16x2(b.wg[p], dg);
       e2m1x8_to_f16x2(b.wh[p], dh);
-      const uint32_t a0 = hmul2_bcast(dg[0], s_g, hi), a1 = hmul2_bcast(dh[0], s_h, hi);
-      const uint32_t a2 = hmul2_bcast(dg[1], s_g, hi), a3 = hmul2_bcast(dh[1], s_h, hi);
-      const uint32_t a4 = hmul2_bcast(dg[2], s_g, hi), a5 = hmul2_bcast(dh[2], s_h, hi);
-      const uint32_t a6 = hmul2_bcast(dg[3], s_g, hi), a7 = hmul2_bcast(dh[3], s_h, hi);
+      const uint32_t a0 = hmul2_u32(dg[0], sg[hi]), a1 = hmul2_u32(dh[0], sh[hi]);
+      const uint32_t a2 = hmul2_u32(dg[1], sg[hi]), a3 = hmul2_u32(dh[1], sh[hi]);
+      const uint32_t a4 = hmul2_u32(dg[2], sg[hi]), a5 = hmul2_u32(dh[2], sh[hi]);
+      const uint32_t a6 = hmul2_u32(dg[3], sg[hi]), a7 = hmul2_u32(dh[3], sh[hi]);
       mma_f16_16816(acc, a0, a1, a2, a3, xv.x, xv.y);
       mma_f16_16816(acc, a4, a5, a6, a7, xv.z, xv.w);
       if constexpr (SPLIT) {
-        const uint4 xl = has_x ? lds_v4(xrow_lo + xo) : make_uint4(0u, 0u, 0u, 0u);
+        const uint4 xl = lds_v4(xb_lo + 64u * p);
         mma_f16_16816(acc, a0, a1, a2, a3, xl.x, xl.y);
         mma_f16_16816(acc, a4, a5, a6, a7, xl.z, xl.w);
       }
@@ -238,16 +247,17 @@ __device__ __forceinline__ uint2 lds_v2(uint32_t a) {
 // column then accumulates one block's products over the 8 MMAs of equal
 // parity, and the lane's own D columns are exactly its own blocks, so the
 // lane scales them with its own blockscales (8 FMAs per chunk).  Slot 0 of
-// lane quad c reads x units ub + {0..3} (ub = 32 ch + 8c: its blocks 4c,
-// 4c + 1), slot 1 units ub + {4..7} (blocks 4c + 2, 4c + 3); lanes that own
-// neither read the 64-byte zero row.  The codes of rows rl and rl + 8 are
+// lane quad c reads logical x units 32 ch + 8 c + {0..3} (its blocks 4c,
+// 4c + 1) at xb + 64 {0..3} (xb = xrow + 16 (32 ch + c), see xs_unit), slot 1
+// units 32 ch + 8 c + {4..7} (blocks 4c + 2, 4c + 3) at xb + 64 {4..7}; lanes
+// that own neither read the zero row.  The codes of rows rl and rl + 8 are
 // read from the staged 128-byte-swizzled tile per parity (8 words at a
 // time); `release` runs once all of the chunk's operands are in registers.
 template <class Release>
 __device__ __forceinline__ void gemv_compute_m1(uint32_t codes, uint32_t sgw, uint32_t shw,
                                                 int rl, int c, float (&tot)[2],
-                                                uint32_t xrow, uint32_t zero, bool own_a,
-                                                bool own_b, int ub, Release release) {
+                                                uint32_t xb, uint32_t zero, bool own_a,
+                                                bool own_b, Release release) {
   const int sw = rl & 7;
   const uint32_t rg = codes + 128u * rl, rh = rg + 128u * 8;
   const uint32_t u0 = 16u * ((2 * c) ^ sw), u1 = 16u * ((2 * c + 1) ^ sw);
@@ -269,8 +279,8 @@ __device__ __forceinline__ void gemv_compute_m1(uint32_t codes, uint32_t sgw, ui
       // of its block par (slot 0) and 2 + par (slot 1).
       const int v = 2 * par + hf;
       const uint32_t za = zero + 16u * (uint32_t)v;
-      const uint4 va = lds_v4(own_a ? xrow + 16u * (uint32_t)xs_unit(ub + v) : za);
-      const uint4 vb = lds_v4(own_b ? xrow + 16u * (uint32_t)xs_unit(ub + 4 + v) : za);
+      const uint4 va = lds_v4(own_a ? xb + 64u * (uint32_t)v : za);
+      const uint4 vb = lds_v4(own_b ? xb + 64u * (uint32_t)(4 + v) : za);
       const uint32_t g0 = hf ? g01.y : g01.x, g1 = hf ? g23.y : g23.x;
       const uint32_t h0 = hf ? h01.y : h01.x, h1 = hf ? h23.y : h23.x;
       mma_f16_16816(d, e2m1_byte_to_f16x2<0>(g0), e2m1_byte_to_f16x2<0>(h0),
@@ -298,8 +308,8 @@ constexpr int kGvSmemCap = 110 * 1024;  // dynamic shared memory per CTA (two pe
 
 // Shared memory of a CTA with `w` consumer warps, `stages` ring stages, `m`
 // token rows of x (twice for hi + lo), a K split of `cs` and `parts` partial
-// sums per owned row (2 for gate + up): the ring, the f16 x slice(s), 64 zero
-// bytes (single-token B fragments), the receive buffer of the cluster
+// sums per owned row (2 for gate + up): the ring, the f16 x slice(s), a zero
+// row of x (tokens >= M), the receive buffer of the cluster
 // reduction ([cs][per][parts][8] fp32, per =
 // ceil(16 w / parts / cs)), per-token scales and exponents, alpha of the rows
 // this CTA finalises, the mbarriers.
@@ -313,7 +323,7 @@ struct GemvSmem {
     xs = stages * stage;
     xs_lo = xs + m * xstride;
     zero = xs_lo + (split ? m * xstride : 0);
-    recv = zero + 64;
+    recv = zero + xstride;
     const int per = (16 * w / parts + cs - 1) / cs;
     inv = recv + (int)sizeof(float) * cs * per * parts * kGvTok;
     emax = inv + (int)sizeof(float) * kGvTok;
@@ -525,7 +535,8 @@ __global__ void __launch_bounds__(32 * (kGvMaxWarps + 1), 2)
     mbar_fence_init();
   }
   if (tid < kGvTok) emax[tid] = 0;
-  if (tid < 16) zero_row[tid] = 0u;
+  for (int i = tid; i < a.xstride / 16; i += blockDim.x)
+    reinterpret_cast<uint4 *>(zero_row)[i] = make_uint4(0u, 0u, 0u, 0u);
   __syncthreads();
   // Programmatic dependent launch: everything above overlapped the previous
   // kernel.  What that kernel may have written (activations, work items,
@@ -606,9 +617,9 @@ __global__ void __launch_bounds__(32 * (kGvMaxWarps + 1), 2)
 
     if (warp < nwarps_used) {
       float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-      const bool has_x = gq < M;  // tokens >= M: zero B fragments
-      const uint32_t xrow = smem_u32(xs + (has_x ? gq : 0) * a.xstride);
-      const uint32_t xrow_lo = smem_u32(xs_lo + (has_x ? gq : 0) * a.xstride);
+      const bool has_x = gq < M;  // tokens >= M: the zero row (zero B fragments)
+      const uint32_t xrow = has_x ? smem_u32(xs + gq * a.xstride) : smem_u32(zero_row);
+      const uint32_t xrow_lo = has_x ? smem_u32(xs_lo + gq * a.xstride) : smem_u32(zero_row);
       if (MODE == kGvPlain && M == 1) {
         // One token: blockscales applied per block after the MMAs
         // (gemv_compute_m1); per lane, sums over its own blocks of rows g
@@ -624,8 +635,8 @@ __global__ void __launch_bounds__(32 * (kGvMaxWarps + 1), 2)
           const uint32_t scales = st + L.codes + warp * kGvTileScales;
           const uint32_t sgw = lds_u32(scales + 16u * gq + 4u * c);
           const uint32_t shw = lds_u32(scales + 16u * (gq + 8) + 4u * c);
-          gemv_compute_m1(st + warp * kGvTileCodes, sgw, shw, gq, c, tot, x0, zero, own_a, own_b,
-                          32 * ch + 8 * c, [&] {
+          gemv_compute_m1(st + warp * kGvTileCodes, sgw, shw, gq, c, tot,
+                          x0 + 16u * (uint32_t)(32 * ch + c), zero, own_a, own_b, [&] {
                             fence_proxy_async_smem();  // as in the general path below
                             __syncwarp();
                             if (lane == 0) mbar_arrive(empty0 + 8 * s);
@@ -656,7 +667,8 @@ __global__ void __launch_bounds__(32 * (kGvMaxWarps + 1), 2)
           // The MMA's fp32 accumulation is not IEEE round-to-nearest: chains are
           // kept to one chunk (16 or 32 MMAs) and chunk sums added with fp32 adds.
           float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-          gemv_compute<kSplit>(b, part, xrow, xrow_lo, has_x, ch, c);
+          const uint32_t xo = 16u * (uint32_t)(32 * ch + c);
+          gemv_compute<kSplit>(b, part, xrow + xo, xrow_lo + xo);
 #pragma unroll
           for (int i = 0; i < 4; ++i) acc[i] += part[i];
         }
@@ -761,11 +773,12 @@ struct GgItem {
 // Shared memory of a grouped CTA with w consumer warps, `stages` ring stages
 // (each: codes, blockscales and the weight_scale_2 rows of w tiles), K and
 // at most `items` items: the ring, the f16 activations of one item (twice
-// for hi + lo), the bf16 rows they are converted from (twice for hi + lo),
+// for hi + lo), a zero row (tokens >= M), the bf16 rows they are converted
+// from (twice for hi + lo),
 // kGvGateUp's two alternating buffers of per-row partial sums ([part][16 w /
 // 2 rows][8 tokens] fp32), the token scales, the item table, the mbarriers.
 struct GgSmem {
-  int stage, codes, ws2, xstride, xs, xs_lo, raw, raw_lo, recv, inv, emax, items, bars, total;
+  int stage, codes, ws2, xstride, xs, xs_lo, zero, raw, raw_lo, recv, inv, emax, items, bars, total;
   __host__ __device__ GgSmem(int w, int stages, int K, int parts, bool split, int n_items) {
     codes = w * kGvTileCodes;
     ws2 = codes + w * kGvTileScales;
@@ -773,7 +786,8 @@ struct GgSmem {
     xstride = 2 * K + 64;
     xs = stages * stage;
     xs_lo = xs + kGvTok * xstride;
-    raw = xs_lo + (split ? kGvTok * xstride : 0);
+    zero = xs_lo + (split ? kGvTok * xstride : 0);
+    raw = zero + xstride;
     raw_lo = raw + kGvTok * 2 * K;
     recv = raw_lo + (split ? kGvTok * 2 * K : 0);
     inv = recv + (parts == 2 ? (int)sizeof(float) * 2 * 16 * w * kGvTok : 0);
@@ -831,6 +845,8 @@ __global__ void __launch_bounds__(32 * (kGvMaxWarps + 1), 1)
     mbar_fence_init();
   }
   if (tid < kGvTok) emax[tid] = 0;
+  for (int i = tid; i < L.xstride / 16; i += blockDim.x)
+    reinterpret_cast<uint4 *>(gsm + L.zero)[i] = make_uint4(0u, 0u, 0u, 0u);
   // The work items come from the previous kernel (griddepcontrol.wait), and
   // so do the activations.  The next kernel may launch now: its CTAs take
   // the SMs this grid's CTAs leave and wait for this grid's completion.
@@ -972,9 +988,9 @@ __global__ void __launch_bounds__(32 * (kGvMaxWarps + 1), 1)
     // kGvDown, this lane's rows (h = 0, 1); kGvGateUp, the gate and up rows of
     // this thread's first two (row, token) elements.
     float w2a[2] = {a.al.ws2, a.al.ws2}, w2b[2] = {a.al.ws2, a.al.ws2};
-    const bool has_x = gq < M;  // tokens >= M: zero B fragments
-    const uint32_t xrow = smem_u32(xs + (has_x ? gq : 0) * L.xstride);
-    const uint32_t xrow_lo = smem_u32(xs_lo + (has_x ? gq : 0) * L.xstride);
+    const bool has_x = gq < M;  // tokens >= M: the zero row (zero B fragments)
+    const uint32_t xrow = smem_u32(has_x ? xs + gq * L.xstride : gsm + L.zero);
+    const uint32_t xrow_lo = smem_u32(has_x ? xs_lo + gq * L.xstride : gsm + L.zero);
     float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     for (int ch = 0; ch < nch; ++ch, ++gc) {
       const int s = gc % S, r = gc / S;
@@ -1005,7 +1021,8 @@ __global__ void __launch_bounds__(32 * (kGvMaxWarps + 1), 1)
       if (lane == 0) mbar_arrive(empty0 + 8 * s);
       if (has_tile) {
         float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        gemv_compute<kSplit>(bch, part, xrow, xrow_lo, has_x, ch, c);
+        const uint32_t xo = 16u * (uint32_t)(32 * ch + c);
+        gemv_compute<kSplit>(bch, part, xrow + xo, xrow_lo + xo);
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[i] += part[i];
       }
