@@ -163,9 +163,14 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(PeerTable P, const int
       }
     }
   }
-  __threadfence_system();  // this thread's peer stores, before the block's count
+  // The block's peer stores, then one system fence before the block's count:
+  // the barrier orders every thread's stores before thread 0's fence, which
+  // is cumulative over them (a fence in each of the 256 threads cost ~6 us).
   __syncthreads();
-  if (threadIdx.x == 0) s_last = atomicAdd(&own->blocks_done, 1u) == gridDim.x - 1;
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    s_last = atomicAdd(&own->blocks_done, 1u) == gridDim.x - 1;
+  }
   __syncthreads();
   if (s_last) {
     if (threadIdx.x == 0) own->blocks_done = 0;  // the next step's launch starts after this one
