@@ -21,7 +21,9 @@
 #include "../../include/nvfp4.h"
 #include "../../include/nvfp4_ep.h"
 #include "abi_util.h"
+#include "moe.h"
 #include "nvfp4_common.cuh"
+#include "router_topk.cuh"
 
 namespace nvfp4 {
 namespace {
@@ -119,10 +121,63 @@ __device__ __forceinline__ char *win_at(const PeerTable &P, int r) {
   return w;
 }
 
-// Step 2: one warp per slot s = t*k + j of this rank.  The row of x[t] goes
-// to row rank*R + s of the destination's window, the expert id to the same
-// row of every window (-1 where the slot does not go).  The last block to
-// finish raises this rank's dispatch flag in every window.
+// One warp: slot s (expert e) of this rank.  The row of x[s / k] goes to row
+// rank*R + s of the destination's window, the expert id to the same row of
+// every window (-1 where the slot does not go).
+__device__ __forceinline__ void dispatch_slot(const PeerTable &P, char *const *s_win, int s, int e,
+                                              int R, int k, int epr, const uint4 *__restrict__ x,
+                                              int lane) {
+  const int E = epr * P.world, row_v = P.H / 8;  // uint4 per bf16 row
+  const int d = (e >= 0 && e < E) ? e / epr : -1;
+  const int64_t row = (int64_t)P.rank * R + s;
+  if (lane < P.world)
+    reinterpret_cast<int32_t *>(s_win[lane] + P.off_expert)[row] = lane == d ? e - d * epr : -1;
+  if (d < 0) return;
+  const uint4 *src = x + (int64_t)(s / k) * row_v;
+  uint4 *dst = reinterpret_cast<uint4 *>(s_win[d] + P.off_x) + row * row_v;
+  // All of this lane's loads before any store: the store pointer may alias
+  // the loads as far as the compiler can tell, which would otherwise
+  // serialise one L2 round trip per 16 bytes.
+  for (int i0 = 0; i0 < row_v; i0 += 32 * 8) {
+    uint4 v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int i = i0 + lane + 32 * j;
+      v[j] = i < row_v ? __ldcg(src + i) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int i = i0 + lane + 32 * j;
+      if (i < row_v) dst[i] = v[j];
+    }
+  }
+}
+
+// The block's peer stores, then one system fence before the block's count:
+// the barrier orders every thread's stores before thread 0's fence, which is
+// cumulative over them (a fence in each of the 256 threads cost ~6 us).  The
+// last block to count raises this rank's dispatch flag in every window, with
+// the row count R (the release orders it first, so that every owner can check
+// that all ranks step with the same T).
+__device__ __forceinline__ void dispatch_publish(const PeerTable &P, char *const *s_win,
+                                                 EpCtrl *own, uint32_t step, int R, int *s_last) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    *s_last = atomicAdd(&own->blocks_done, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (*s_last) {
+    if (threadIdx.x == 0) own->blocks_done = 0;  // the next step's launch starts after this one
+    if (threadIdx.x < P.world) ctrl_of(s_win[threadIdx.x])->rows_from[P.rank] = (uint32_t)R;
+    __threadfence_system();
+    if (threadIdx.x < P.world) st_release_sys(&ctrl_of(s_win[threadIdx.x])->flag_dispatch[P.rank], step);
+  }
+}
+
+// Step 2: one warp per slot s = t*k + j of this rank (dispatch_slot); the
+// last block to finish raises this rank's dispatch flag in every window
+// (dispatch_publish).
 __global__ void __launch_bounds__(256) ep_dispatch_kernel(PeerTable P, const int32_t *__restrict__ ids,
                                                           const uint4 *__restrict__ x, int T, int k,
                                                           int epr) {
@@ -134,52 +189,53 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(PeerTable P, const int
   __syncthreads();
   EpCtrl *own = ctrl_of(s_win[P.rank]);
   const uint32_t step = __ldcg(&own->epoch) + 1;
-  const int R = T * k, E = epr * P.world, row_v = P.H / 8;  // uint4 per bf16 row
+  const int R = T * k;
   const int lane = threadIdx.x & 31;
-  for (int s = blockIdx.x * 8 + (threadIdx.x >> 5); s < R; s += gridDim.x * 8) {
-    const int e = __ldcg(ids + s);
-    const int d = (e >= 0 && e < E) ? e / epr : -1;
-    const int64_t row = (int64_t)P.rank * R + s;
-    if (lane < P.world)
-      reinterpret_cast<int32_t *>(s_win[lane] + P.off_expert)[row] = lane == d ? e - d * epr : -1;
-    if (d >= 0) {
-      const uint4 *src = x + (int64_t)(s / k) * row_v;
-      uint4 *dst = reinterpret_cast<uint4 *>(s_win[d] + P.off_x) + row * row_v;
-      // All of this lane's loads before any store: the store pointer may
-      // alias the loads as far as the compiler can tell, which would
-      // otherwise serialise one L2 round trip per 16 bytes.
-      for (int i0 = 0; i0 < row_v; i0 += 32 * 8) {
-        uint4 v[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int i = i0 + lane + 32 * j;
-          v[j] = i < row_v ? __ldcg(src + i) : make_uint4(0, 0, 0, 0);
-        }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int i = i0 + lane + 32 * j;
-          if (i < row_v) dst[i] = v[j];
-        }
-      }
+  for (int s = blockIdx.x * 8 + (threadIdx.x >> 5); s < R; s += gridDim.x * 8)
+    dispatch_slot(P, s_win, s, __ldcg(ids + s), R, k, epr, x, lane);
+  dispatch_publish(P, s_win, own, step, R, &s_last);
+}
+
+// Top-k + step 2 in one launch, one block per token t: warp 0 runs the
+// token's softmax top-k from the router's partial logits (the arithmetic of
+// the router's own top-k kernel, router_topk.cuh) into the ids / weights of
+// the combine and the block's shared memory, then the block's warps dispatch
+// its k slots (dispatch_slot) and the flag goes up as in ep_dispatch_kernel.
+// One kernel boundary less than top-k, dispatch.
+__global__ void __launch_bounds__(256) ep_topk_dispatch_kernel(PeerTable P, const float *__restrict__ part,
+                                                               int nslices,
+                                                               const uint4 *__restrict__ x, int T,
+                                                               int k, int renormalize, int epr,
+                                                               int32_t *__restrict__ ids,
+                                                               float *__restrict__ w) {
+  __shared__ char *s_win[kMaxWorld];
+  __shared__ int s_last;
+  __shared__ int32_t s_ids[32];
+  pdl_wait();  // the partial logits, x and the step counter come from earlier kernels
+  pdl_trigger();
+  if (threadIdx.x < kMaxWorld) s_win[threadIdx.x] = win_at(P, threadIdx.x < P.world ? threadIdx.x : 0);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int t = blockIdx.x, E = epr * P.world;
+  if (warp == 0 && t < T) {
+    float p[8];
+    router_sum_slices(part, nslices, T, t, E, lane, p, nullptr);
+    int id_sel;
+    float w_sel;
+    router_softmax_topk(p, lane, E, k, renormalize, id_sel, w_sel);
+    if (lane < k) {
+      ids[(int64_t)t * k + lane] = id_sel;
+      w[(int64_t)t * k + lane] = w_sel;
+      s_ids[lane] = id_sel;
     }
   }
-  // The block's peer stores, then one system fence before the block's count:
-  // the barrier orders every thread's stores before thread 0's fence, which
-  // is cumulative over them (a fence in each of the 256 threads cost ~6 us).
   __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    s_last = atomicAdd(&own->blocks_done, 1u) == gridDim.x - 1;
-  }
-  __syncthreads();
-  if (s_last) {
-    if (threadIdx.x == 0) own->blocks_done = 0;  // the next step's launch starts after this one
-    // The row count goes out with the flag (the release orders it first), so
-    // that every owner can check that all ranks step with the same T.
-    if (threadIdx.x < P.world) ctrl_of(s_win[threadIdx.x])->rows_from[P.rank] = (uint32_t)R;
-    __threadfence_system();
-    if (threadIdx.x < P.world) st_release_sys(&ctrl_of(s_win[threadIdx.x])->flag_dispatch[P.rank], step);
-  }
+  EpCtrl *own = ctrl_of(s_win[P.rank]);
+  const uint32_t step = __ldcg(&own->epoch) + 1;
+  const int R = T * k;
+  if (t < T)
+    for (int j = warp; j < k; j += blockDim.x >> 5)
+      dispatch_slot(P, s_win, t * k + j, s_ids[j], R, k, epr, x, lane);
+  dispatch_publish(P, s_win, own, step, R, &s_last);
 }
 
 // Step 3: one warp; lane p waits for rank p's dispatch flag and checks that
@@ -336,6 +392,25 @@ int check_step(const nvfp4_ep_peers *p, int64_t T, int32_t k, int32_t epr) {
 }
 
 }  // namespace
+
+int ep_p2p_topk_dispatch(const nvfp4_ep_peers *p, const uint16_t *x, const float *part,
+                         int nslices, int64_t T, int k, int renormalize, int epr, int32_t *ids,
+                         float *w, cudaStream_t st) {
+  int rc = check_step(p, T, k, epr);
+  if (rc) return rc;
+  if (T > 0 && (!x || !part || !ids || !w))
+    return fail(NVFP4_ERR_INVALID_ARG, "null activations, logits, ids or weights");
+  if (!aligned(x, 16)) return fail(NVFP4_ERR_INVALID_ARG, "x must be 16-byte aligned");
+  if (epr * p->world > 256 || nslices < 1)
+    return fail(NVFP4_ERR_INVALID_ARG, "the fused top-k takes at most 256 experts");
+  // At least one block, so the flags go up even for an empty step.
+  const unsigned blocks = (unsigned)std::max<int64_t>(1, T);
+  return check_launch(launch_pdl(ep_topk_dispatch_kernel, dim3(blocks), dim3(256), 0, st,
+                                 make_table(*p), part, nslices, reinterpret_cast<const uint4 *>(x),
+                                 (int)T, k, renormalize, epr, ids, w),
+                      "top-k + dispatch launch");
+}
+
 }  // namespace nvfp4
 
 using namespace nvfp4;

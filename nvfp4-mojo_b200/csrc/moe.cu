@@ -17,6 +17,7 @@
 #include "kernels.h"
 #include "moe.h"
 #include "nvfp4_common.cuh"
+#include "router_topk.cuh"
 
 namespace nvfp4 {
 
@@ -235,8 +236,8 @@ __global__ void __launch_bounds__(128) router_logits_tc_kernel(const uint16_t *_
   }
 }
 
-// One warp per token: softmax over E (E <= 256: 8 logits per lane), top-k by
-// repeated warp arg-max (ties to the lower index), optional renormalisation.
+// One warp per token: the slices' partial logits added in z order, then the
+// softmax top-k (router_topk.cuh).
 __global__ void router_topk_kernel(const float *__restrict__ part, int nslices,
                                    float *__restrict__ logits_out, int T, int E, int k,
                                    int renormalize, int32_t *__restrict__ topk_ids,
@@ -246,83 +247,13 @@ __global__ void router_topk_kernel(const float *__restrict__ part, int nslices,
   pdl_trigger();
   if (warp >= T) return;
   float p[8];
-  float mx = -FLT_MAX;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int e = lane + 32 * i;
-    float v = 0.0f;
-    if (e < E) {
-      // All slices' loads first (up to 16 in flight), then the sum in z order.
-      float pz[16];
-#pragma unroll
-      for (int z = 0; z < 16; ++z)
-        pz[z] = z < nslices ? __ldcg(part + ((int64_t)z * T + warp) * E + e) : 0.0f;
-#pragma unroll
-      for (int z = 0; z < 16; ++z)
-        if (z < nslices) v += pz[z];
-      for (int z = 16; z < nslices; ++z) v += __ldcg(part + ((int64_t)z * T + warp) * E + e);
-      if (logits_out) logits_out[(int64_t)warp * E + e] = v;
-    }
-    p[i] = e < E ? v : -FLT_MAX;
-    mx = fmaxf(mx, p[i]);
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  float sum = 0.0f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int e = lane + 32 * i;
-    p[i] = e < E ? expf(p[i] - mx) : 0.0f;
-    sum += p[i];
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) p[i] = p[i] / sum;
-
-  // NaN probabilities rank below every number (and are still selectable, so
-  // k valid ids are always produced); taken experts are marked -inf.
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-    if (p[i] != p[i]) p[i] = -1.0e30f;
-  float wsum = 0.0f, wsel = 0.0f;
-  int id_sel = 0;
-  for (int j = 0; j < k; ++j) {
-    // Best of this lane (lowest expert index among equals), then across lanes.
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int e = lane + 32 * i;
-      if (e < E && (p[i] > bv)) {
-        bv = p[i];
-        bi = e;
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ov > bv || (ov == bv && oi < bi)) {
-        bv = ov;
-        bi = oi;
-      }
-    }
-    if ((bi & 31) == lane) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-        if (lane + 32 * i == bi) p[i] = -INFINITY;  // taken
-    }
-    const float wv = bv < -1.0e29f ? __int_as_float(0x7fc00000) : bv;  // NaN stays NaN
-    wsum += wv;
-    if (lane == j) {
-      wsel = wv;
-      id_sel = bi;
-    }
-  }
+  router_sum_slices(part, nslices, T, warp, E, lane, p, logits_out);
+  int id_sel;
+  float w_sel;
+  router_softmax_topk(p, lane, E, k, renormalize, id_sel, w_sel);
   if (lane < k) {
     topk_ids[(int64_t)warp * k + lane] = id_sel;
-    topk_w[(int64_t)warp * k + lane] = renormalize ? wsel / wsum : wsel;
+    topk_w[(int64_t)warp * k + lane] = w_sel;
   }
 }
 
@@ -346,35 +277,42 @@ int router_slices(int T, int H, int E) {
   return hs;
 }
 
+cudaError_t launch_router_logits(const uint16_t *x, const float *router, float *part,
+                                 int nslices, int T, int H, int E, cudaStream_t st, int *used) {
+  if (nslices < 1) nslices = 1;
+  *used = nslices;
+  if (T == 0) return cudaSuccess;
+  const bool aligned16 = (((uintptr_t)x | (uintptr_t)router) & 15) == 0;
+  if (router_tc_ok(T, H, E) && aligned16 && H % (nslices * kRtcK) == 0) {
+    dim3 grid((E + kRtcExp - 1) / kRtcExp, (T + kRtcTok - 1) / kRtcTok, nslices);
+    return launch_pdl(router_logits_tc_kernel, grid, dim3(128), 0, st, x, router, part, T, H, E,
+                      H / nslices);
+  }
+  while (nslices > 1 && H % (nslices * kRouterWarps) != 0) nslices >>= 1;
+  *used = nslices;
+  const int hslice = H / nslices;
+  const size_t smem = sizeof(float) * ((size_t)hslice * kRouterTok + kRouterWarps * kRouterTok * 32);
+  static size_t configured = 48 * 1024;
+  if (smem > configured) {
+    cudaError_t e = cudaFuncSetAttribute(router_logits_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    configured = smem;
+  }
+  dim3 grid((E + 31) / 32, (T + kRouterTok - 1) / kRouterTok, nslices);
+  return launch_pdl(router_logits_kernel, grid, dim3(32 * kRouterWarps), smem, st, x, router,
+                    part, T, H, E, hslice);
+}
+
 cudaError_t launch_router(const uint16_t *x, const float *router, float *part, int nslices,
                           float *logits_out, int T, int H, int E, int k, int renormalize,
                           int32_t *ids, float *w, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
-  if (nslices < 1) nslices = 1;
-  const bool aligned16 = (((uintptr_t)x | (uintptr_t)router) & 15) == 0;
-  if (router_tc_ok(T, H, E) && aligned16 && H % (nslices * kRtcK) == 0) {
-    dim3 grid((E + kRtcExp - 1) / kRtcExp, (T + kRtcTok - 1) / kRtcTok, nslices);
-    cudaError_t e = launch_pdl(router_logits_tc_kernel, grid, dim3(128), 0, st, x, router, part, T,
-                               H, E, H / nslices);
-    if (e != cudaSuccess) return e;
-  } else {
-    while (nslices > 1 && H % (nslices * kRouterWarps) != 0) nslices >>= 1;
-    const int hslice = H / nslices;
-    const size_t smem = sizeof(float) * ((size_t)hslice * kRouterTok + kRouterWarps * kRouterTok * 32);
-    static size_t configured = 48 * 1024;
-    if (smem > configured) {
-      cudaError_t e = cudaFuncSetAttribute(router_logits_kernel,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e != cudaSuccess) return e;
-      configured = smem;
-    }
-    dim3 grid((E + 31) / 32, (T + kRouterTok - 1) / kRouterTok, nslices);
-    cudaError_t e = launch_pdl(router_logits_kernel, grid, dim3(32 * kRouterWarps), smem, st, x,
-                               router, part, T, H, E, hslice);
-    if (e != cudaSuccess) return e;
-  }
-  return launch_pdl(router_topk_kernel, dim3((T * 32 + 255) / 256), dim3(256), 0, st, part,
-                    nslices, logits_out, T, E, k, renormalize, ids, w);
+  int used = 0;
+  cudaError_t e = launch_router_logits(x, router, part, nslices, T, H, E, st, &used);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(router_topk_kernel, dim3((T * 32 + 255) / 256), dim3(256), 0, st, part, used,
+                    logits_out, T, E, k, renormalize, ids, w);
 }
 
 // ---------------------------------------------------------------------------

@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "../../include/nvfp4_ep.h"
+
 #include "kernels.h"
 
 namespace nvfp4 {
@@ -45,6 +47,10 @@ int moe_tc_rows_per_item();
 // router_slices), summed in slice order by the top-k kernel, which also
 // writes the logits to logits_out (nullable).
 int router_slices(int T, int H, int E);
+// The partial-logits kernel of launch_router alone (its top-k left to the
+// caller); returns the slice count it used (<= nslices) in *used.
+cudaError_t launch_router_logits(const uint16_t *x, const float *router, float *part,
+                                 int nslices, int T, int H, int E, cudaStream_t st, int *used);
 cudaError_t launch_router(const uint16_t *x, const float *router, float *part, int nslices,
                           float *logits_out, int T, int H, int E, int k, int renormalize,
                           int32_t *ids, float *w, cudaStream_t st);
@@ -57,6 +63,14 @@ cudaError_t launch_moe_combine(const void *ys, int ys_dtype, const float *w,
                                const uint16_t *residual, const int32_t *slot_pos,
                                const float *extra, void *y, int y_dtype, int T, int k, int H,
                                cudaStream_t st);
+// Expert-parallel top-k + dispatch in one launch (ep_p2p.cu), after the
+// router's partial logits (launch_router_logits): blocks of 8 tokens run the
+// softmax top-k of their tokens (router_topk.cuh) and dispatch the tokens'
+// slots into the peers' windows.  Writes ids / weights [T, k] for the
+// combine.
+int ep_p2p_topk_dispatch(const nvfp4_ep_peers *p, const uint16_t *x, const float *part,
+                         int nslices, int64_t T, int k, int renormalize, int epr, int32_t *ids,
+                         float *w, cudaStream_t st);
 cudaError_t launch_ep_plan(const int32_t *ids, int R, int k, int epr, int world, int32_t *counts,
                            int32_t *send_token, int32_t *send_expert, int32_t *slot_pos,
                            cudaStream_t st);

@@ -668,17 +668,20 @@ extern "C" int nvfp4_ep_p2p_forward(const nvfp4_moe_desc *d, const nvfp4_moe_wei
   int32_t *ids = reinterpret_cast<int32_t *>(base + L.ids);
   float *tw = reinterpret_cast<float *>(base + L.w);
   const int epr = d->num_experts / p->world, k = d->top_k;
-  // Every rank takes every step, also with no tokens: the peers wait on its flags.
+  // Every rank takes every step, also with no tokens: the peers wait on its
+  // flags.  The top-k runs inside the dispatch kernel.
+  float *part = reinterpret_cast<float *>(base + L.part);
+  int nslices = 1;
   if (T > 0) {
-    rc = check_launch(launch_router(static_cast<const uint16_t *>(x), local->router,
-                                    reinterpret_cast<float *>(base + L.part),
-                                    router_slices((int)T, d->hidden, d->num_experts), nullptr,
-                                    (int)T, d->hidden, d->num_experts, k, d->renormalize, ids, tw,
-                                    st),
+    rc = check_launch(launch_router_logits(static_cast<const uint16_t *>(x), local->router, part,
+                                           router_slices((int)T, d->hidden, d->num_experts),
+                                           (int)T, d->hidden, d->num_experts, st, &nslices),
                       "router launch");
     if (rc) return rc;
   }
-  if ((rc = nvfp4_ep_p2p_dispatch(p, ids, x, T, k, epr, stream))) return rc;
+  if ((rc = ep_p2p_topk_dispatch(p, static_cast<const uint16_t *>(x), part, nslices, T, k,
+                                 d->renormalize, epr, ids, tw, st)))
+    return rc;
   if ((rc = nvfp4_ep_p2p_wait_dispatch(p, stream))) return rc;
   void *recv_x = nullptr;
   int32_t *recv_e = nullptr;
