@@ -48,10 +48,25 @@ __global__ void __launch_bounds__(32 * kRouterWarps)
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   pdl_wait();  // x may come from the previous kernel
   pdl_trigger();
-  for (int i = threadIdx.x; i < hslice * kRouterTok; i += blockDim.x) {
-    const int h = i / kRouterTok, tt = i % kRouterTok;
-    const int t = t0 + tt;
-    xs[i] = t < T ? __uint_as_float((uint32_t)__ldcg(x + (int64_t)t * H + h0 + h) << 16) : 0.0f;
+  if (hslice % 8 == 0 && H % 8 == 0 && ((uintptr_t)x & 15) == 0) {
+    // 8 bf16 at a time: thread i takes token i % 8 and rows 8 (i / 8) .. + 7.
+    for (int i = threadIdx.x; i < hslice; i += blockDim.x) {
+      const int tt = i % kRouterTok, h = 8 * (i / kRouterTok), t = t0 + tt;
+      const uint4 v = t < T ? __ldcg(reinterpret_cast<const uint4 *>(x + (int64_t)t * H + h0 + h))
+                            : make_uint4(0u, 0u, 0u, 0u);
+      const uint32_t q[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        xs[(h + 2 * j) * kRouterTok + tt] = __uint_as_float(q[j] << 16);
+        xs[(h + 2 * j + 1) * kRouterTok + tt] = __uint_as_float(q[j] & 0xFFFF0000u);
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < hslice * kRouterTok; i += blockDim.x) {
+      const int h = i / kRouterTok, tt = i % kRouterTok;
+      const int t = t0 + tt;
+      xs[i] = t < T ? __uint_as_float((uint32_t)__ldcg(x + (int64_t)t * H + h0 + h) << 16) : 0.0f;
+    }
   }
   __syncthreads();
   const int e = min(e0 + lane, E - 1);
@@ -60,19 +75,26 @@ __global__ void __launch_bounds__(32 * kRouterWarps)
 #pragma unroll
   for (int i = 0; i < kRouterTok; ++i) acc[i] = 0.0f;
   const float *rp = router + (int64_t)(h0 + hb) * E + e;
-#pragma unroll 8
-  for (int h = 0; h < hs; ++h) {
-    const float r = __ldg(rp + (int64_t)h * E);
-    const float4 xa = *reinterpret_cast<const float4 *>(xs + (hb + h) * kRouterTok);
-    const float4 xb = *reinterpret_cast<const float4 *>(xs + (hb + h) * kRouterTok + 4);
-    acc[0] = fmaf(xa.x, r, acc[0]);
-    acc[1] = fmaf(xa.y, r, acc[1]);
-    acc[2] = fmaf(xa.z, r, acc[2]);
-    acc[3] = fmaf(xa.w, r, acc[3]);
-    acc[4] = fmaf(xb.x, r, acc[4]);
-    acc[5] = fmaf(xb.y, r, acc[5]);
-    acc[6] = fmaf(xb.z, r, acc[6]);
-    acc[7] = fmaf(xb.w, r, acc[7]);
+  // 32 router rows per batch: all 32 loads in flight before their FMAs (the
+  // warp's rows are one latency-bound stream otherwise).
+  for (int hc = 0; hc < hs; hc += 32) {
+    float r[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) r[j] = hc + j < hs ? __ldg(rp + (int64_t)(hc + j) * E) : 0.0f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (hc + j >= hs) break;
+      const float4 xa = *reinterpret_cast<const float4 *>(xs + (hb + hc + j) * kRouterTok);
+      const float4 xb = *reinterpret_cast<const float4 *>(xs + (hb + hc + j) * kRouterTok + 4);
+      acc[0] = fmaf(xa.x, r[j], acc[0]);
+      acc[1] = fmaf(xa.y, r[j], acc[1]);
+      acc[2] = fmaf(xa.z, r[j], acc[2]);
+      acc[3] = fmaf(xa.w, r[j], acc[3]);
+      acc[4] = fmaf(xb.x, r[j], acc[4]);
+      acc[5] = fmaf(xb.y, r[j], acc[5]);
+      acc[6] = fmaf(xb.z, r[j], acc[6]);
+      acc[7] = fmaf(xb.w, r[j], acc[7]);
+    }
   }
 #pragma unroll
   for (int i = 0; i < kRouterTok; ++i) red[(warp * kRouterTok + i) * 32 + lane] = acc[i];
