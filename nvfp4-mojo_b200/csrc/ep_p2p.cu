@@ -4,8 +4,9 @@
 // cross-GPU flags that order the steps, and the windows' IPC plumbing.
 //
 // Memory ordering.  A rank writes into a peer's window only with plain
-// stores followed by a system-scope fence, and publishes them with one
-// st.release.sys of a flag in that window; the owner polls its own flags
+// stores ordered by a system-scope release (a fence, or a release
+// read-modify-write that the publishing thread acquires), and publishes them
+// with one st.release.sys of a flag in that window; the owner polls its own flags
 // with ld.acquire.sys (local memory, bounded by time) and every later read
 // of the published rows follows that acquire in the same stream.  All waits
 // are on this GPU's memory, all signals are remote stores, so no kernel ever
@@ -153,25 +154,30 @@ __device__ __forceinline__ void dispatch_slot(const PeerTable &P, char *const *s
   }
 }
 
-// The block's peer stores, then one system fence before the block's count:
-// the barrier orders every thread's stores before thread 0's fence, which is
-// cumulative over them (a fence in each of the 256 threads cost ~6 us).  The
-// last block to count raises this rank's dispatch flag in every window, with
-// the row count R (the release orders it first, so that every owner can check
-// that all ranks step with the same T).
+__device__ __forceinline__ uint32_t atom_add_acq_rel_sys(uint32_t *p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.sys.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
+// Publication of a dispatch.  After the block barrier, thread 0 counts the
+// block with a release (acq_rel, system scope) add on the rank's own block
+// counter: the release is cumulative over the block's peer stores, which the
+// barrier ordered before it (one such release per block; a system fence in
+// each of the 256 threads cost ~6 us, a fence.sc.sys per block ~1.6 us more
+// than this).  The block whose add completes the count acquires every other
+// block's release through the counter, and its thread 0 then raises this
+// rank's dispatch flag in every window with st.release.sys, after the row
+// count R (so that every owner can check that all ranks step with the same
+// T); each release is cumulative over all it acquired.
 __device__ __forceinline__ void dispatch_publish(const PeerTable &P, char *const *s_win,
-                                                 EpCtrl *own, uint32_t step, int R, int *s_last) {
+                                                 EpCtrl *own, uint32_t step, int R) {
   __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    *s_last = atomicAdd(&own->blocks_done, 1u) == gridDim.x - 1;
-  }
-  __syncthreads();
-  if (*s_last) {
-    if (threadIdx.x == 0) own->blocks_done = 0;  // the next step's launch starts after this one
-    if (threadIdx.x < P.world) ctrl_of(s_win[threadIdx.x])->rows_from[P.rank] = (uint32_t)R;
-    __threadfence_system();
-    if (threadIdx.x < P.world) st_release_sys(&ctrl_of(s_win[threadIdx.x])->flag_dispatch[P.rank], step);
+  if (threadIdx.x == 0 && atom_add_acq_rel_sys(&own->blocks_done, 1u) == gridDim.x - 1) {
+    own->blocks_done = 0;  // the next step's launch starts after this one
+    for (int r = 0; r < P.world; ++r) ctrl_of(s_win[r])->rows_from[P.rank] = (uint32_t)R;
+    for (int r = 0; r < P.world; ++r)
+      st_release_sys(&ctrl_of(s_win[r])->flag_dispatch[P.rank], step);
   }
 }
 
@@ -182,7 +188,6 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(PeerTable P, const int
                                                           const uint4 *__restrict__ x, int T, int k,
                                                           int epr) {
   __shared__ char *s_win[kMaxWorld];
-  __shared__ int s_last;
   pdl_wait();  // ids, x and the step counter come from earlier kernels
   pdl_trigger();
   if (threadIdx.x < kMaxWorld) s_win[threadIdx.x] = win_at(P, threadIdx.x < P.world ? threadIdx.x : 0);
@@ -193,7 +198,7 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(PeerTable P, const int
   const int lane = threadIdx.x & 31;
   for (int s = blockIdx.x * 8 + (threadIdx.x >> 5); s < R; s += gridDim.x * 8)
     dispatch_slot(P, s_win, s, __ldcg(ids + s), R, k, epr, x, lane);
-  dispatch_publish(P, s_win, own, step, R, &s_last);
+  dispatch_publish(P, s_win, own, step, R);
 }
 
 // Top-k + step 2 in one launch, one block per token t: warp 0 runs the
@@ -209,13 +214,14 @@ __global__ void __launch_bounds__(256) ep_topk_dispatch_kernel(PeerTable P, cons
                                                                int32_t *__restrict__ ids,
                                                                float *__restrict__ w) {
   __shared__ char *s_win[kMaxWorld];
-  __shared__ int s_last;
   __shared__ int32_t s_ids[32];
   pdl_wait();  // the partial logits, x and the step counter come from earlier kernels
   pdl_trigger();
   if (threadIdx.x < kMaxWorld) s_win[threadIdx.x] = win_at(P, threadIdx.x < P.world ? threadIdx.x : 0);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int t = blockIdx.x, E = epr * P.world;
+  // The step counter's load goes out before the top-k (it is used after).
+  const uint32_t step = __ldcg(&ctrl_of(win_at(P, P.rank))->epoch) + 1;
   if (warp == 0 && t < T) {
     float p[8];
     router_sum_slices(part, nslices, T, t, E, lane, p, nullptr);
@@ -230,12 +236,11 @@ __global__ void __launch_bounds__(256) ep_topk_dispatch_kernel(PeerTable P, cons
   }
   __syncthreads();
   EpCtrl *own = ctrl_of(s_win[P.rank]);
-  const uint32_t step = __ldcg(&own->epoch) + 1;
   const int R = T * k;
   if (t < T)
     for (int j = warp; j < k; j += blockDim.x >> 5)
       dispatch_slot(P, s_win, t * k + j, s_ids[j], R, k, epr, x, lane);
-  dispatch_publish(P, s_win, own, step, R, &s_last);
+  dispatch_publish(P, s_win, own, step, R);
 }
 
 // Step 3: one warp; lane p waits for rank p's dispatch flag and checks that

@@ -11,27 +11,36 @@ namespace nvfp4 {
 #ifdef __CUDACC__
 // Logits of token t for the lane's experts lane + 32 i (-FLT_MAX beyond E):
 // the router's nslices partial sums part[z][T][E], added in slice order
-// (all slices' loads first, up to 16 in flight); written to logits_out
-// [T, E] when it is not null.
+// (each expert's sum starts at 0 and adds slices 0, 1, 2, ...).  Loads go
+// out 4 slices x 8 experts at a time, so a token costs ceil(nslices / 4) L2
+// round trips instead of one per expert.  Written to logits_out [T, E] when
+// it is not null.
 __device__ __forceinline__ void router_sum_slices(const float *__restrict__ part, int nslices,
                                                   int T, int t, int E, int lane, float (&p)[8],
                                                   float *__restrict__ logits_out) {
+  float v[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+  for (int z0 = 0; z0 < nslices; z0 += 4) {
+    float q[4][8];
+#pragma unroll
+    for (int zz = 0; zz < 4; ++zz)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int z = z0 + zz, e = lane + 32 * i;
+        q[zz][i] = (z < nslices && e < E) ? __ldcg(part + ((int64_t)z * T + t) * E + e) : 0.0f;
+      }
+#pragma unroll
+    for (int zz = 0; zz < 4; ++zz)
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (z0 + zz < nslices) v[i] += q[zz][i];
+  }
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int e = lane + 32 * i;
-    float v = 0.0f;
-    if (e < E) {
-      float pz[16];
-#pragma unroll
-      for (int z = 0; z < 16; ++z)
-        pz[z] = z < nslices ? __ldcg(part + ((int64_t)z * T + t) * E + e) : 0.0f;
-#pragma unroll
-      for (int z = 0; z < 16; ++z)
-        if (z < nslices) v += pz[z];
-      for (int z = 16; z < nslices; ++z) v += __ldcg(part + ((int64_t)z * T + t) * E + e);
-      if (logits_out) logits_out[(int64_t)t * E + e] = v;
-    }
-    p[i] = e < E ? v : -FLT_MAX;
+    if (e < E && logits_out) logits_out[(int64_t)t * E + e] = v[i];
+    p[i] = e < E ? v[i] : -FLT_MAX;
   }
 }
 
