@@ -136,33 +136,53 @@ class GemvSweep:
                 "(4096,14336)}, bf16 activations ~N(0,1), NVFP4 weights (nibbles uniform, "
                 "e4m3 scales U(0.25,4), per-row fp32 scale_2 U(1e-3,1e-2)); bf16 out")
 
-    def __init__(self, device, seed=0):
+    def __init__(self, device, seed=0, split=None, world=1, rank=0):
         import torch
         import nvfp4
         from nvfp4 import synthetic
+        from nvfp4.column_split import shard_bounds
 
         self.torch, self.nvfp4 = torch, nvfp4
         self.dev = device
+        # Column split: this GPU holds output rows [n0, n1) of every shape
+        # (nvfp4.column_split's bounds) and computes that slice of y, no
+        # collective; the job's work is the whole sweep (strong scaling).
+        split = split if world > 1 else None
+        self.scaling = "strong" if split else "weak"
         self.sets = 2  # two weight sets alternate per step: reuse distance > L2
         self.calls = []  # per set: list of (lin, W, SF, X, Y, bytes, is_dominant)
+        full_bytes = 0
         for s in range(self.sets):
             calls = []
             for (K, N) in GEMV_SHAPES:
+                n0, n1 = shard_bounds(N, world, rank) if split else (0, N)
+                n = n1 - n0
                 for M in GEMV_MS:
-                    wd = synthetic.linear_weights_cuda(N, K, seed=seed + 1000 * s + 7 * M + K + N,
+                    wd = synthetic.linear_weights_cuda(n, K, seed=seed + 1000 * s + 7 * M + K + N,
                                                        device=device)
                     x = torch.randn((M, K), device=device).to(torch.bfloat16)
-                    y = torch.empty((M, N), device=device, dtype=torch.bfloat16)
-                    lin = nvfp4.NvFp4Linear(K, N, weight_scale_2_rows=wd["ws2"])
-                    calls.append((lin, wd["w"], wd["sf"], x, y, gemv_bytes(K, N),
+                    y = torch.empty((M, n), device=device, dtype=torch.bfloat16)
+                    lin = nvfp4.NvFp4Linear(K, n, weight_scale_2_rows=wd["ws2"])
+                    calls.append((lin, wd["w"], wd["sf"], x, y, gemv_bytes(K, n),
                                   (K, N) == (4096, 14336)))
+                    if s == 0:
+                        full_bytes += gemv_bytes(K, N)
             self.calls.append(calls)
-        self.bytes_per_step = sum(c[5] for c in self.calls[0])
+        # Per-rank units: the harness multiplies by the world size, so a split
+        # counts the whole sweep once (the slices differ by at most one tile).
+        self.bytes_per_step = (full_bytes / world if split else
+                               sum(c[5] for c in self.calls[0]))
         self.launches_per_step = len(self.calls[0])
-        self.dominant_bytes = gemv_bytes(4096, 14336)
-        self.dominant_name = "gemv_kernel (decode GEMV, K=4096 N=14336)"
+        dn0, dn1 = shard_bounds(14336, world, rank) if split else (0, 14336)
+        self.dominant_bytes = gemv_bytes(4096, dn1 - dn0)
+        self.dominant_name = (f"gemv_kernel (decode GEMV, K=4096 N={dn1 - dn0}"
+                              + (f", this GPU's column slice of N=14336)" if split else ")"))
         self.config = {"workload": self.workload, "shapes_KN": GEMV_SHAPES, "M": GEMV_MS,
                        "l2": "inputs larger than L2: two weight sets (2 x 143 MB) alternate per step"}
+        if split:
+            self.config["split"] = (f"columns: each of {world} GPUs holds N/{world} output rows "
+                                    "of every shape (16-row tiles) and writes its slice of y, "
+                                    "no collective")
 
     def run_step(self, i):
         for (lin, W, SF, X, Y, _b, _dom) in self.calls[i % self.sets]:
@@ -724,10 +744,11 @@ class EPStackBench:
         g.manual_seed(77 + rank)
         self.x = torch.randn((self.T_local, MOE_H), generator=g, device=device).to(torch.bfloat16)
         if exchange == "p2p":
-            # router (2), dispatch, wait, permutation, 2 expert GEMVs, done signal, combine
+            # router logits, top-k + dispatch, wait, permutation, 2 expert GEMVs,
+            # done signal, combine
             self.graphable = True
             self.exchange = "peer memory, CUDA graph"
-            self.launches_per_step = layers * 9
+            self.launches_per_step = layers * 8
         else:
             # Fixed-capacity exchange (no host-side counts) for small batches:
             # the whole step, NCCL calls included, is replayed from a CUDA graph.
@@ -761,7 +782,10 @@ class EPStackBench:
         layer_s = ms_per_step / 1e3 / self.n_layers
         achieved = self.layer_bytes / layer_s / 1e9
         return {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / peaks["hbm_gbs"], "traffic": load_traffic(self.name),
+                "frac": achieved / peaks["hbm_gbs"],
+                # The committed capture is of one layer at one GPU (its 8 launches).
+                "traffic": load_traffic(self.name) if self.world == 1 and self.exchange.startswith(
+                    "peer") else None,
                 "kernel": (f"one expert-parallel MoE layer ({self.launches_per_step // self.n_layers}"
                            f" launches), per GPU"),
                 "algorithmic_bytes_per_launch": self.layer_bytes,
@@ -1119,6 +1143,9 @@ def main():
                     help="MoE: tokens per step (default 4096); EP stack: global tokens (default "
                          "64); DeltaNet: sequences per step (default 4)")
     ap.add_argument("--layers", type=int, default=48, help="EP stack: number of MoE layers")
+    ap.add_argument("--split", default=None, choices=["columns"],
+                    help="gemv at N > 1: split every linear by output rows over the GPUs "
+                         "(default: independent replicas)")
     ap.add_argument("--exchange", default="p2p", choices=["nccl", "p2p"],
                     help="EP stack: device-initiated peer-memory exchange or NCCL all-to-all")
     ap.add_argument("--clock-window", type=float, default=0.6,
@@ -1141,6 +1168,8 @@ def main():
     torch.cuda.set_device(device)
     peaks = load_peaks()
     kw = {"tokens": args.tokens} if args.workload in ("moe", "ep", "deltanet") else {}
+    if args.workload == "gemv":
+        kw.update(split=args.split, world=world, rank=rank)
     if args.workload == "ep":
         kw["layers"] = args.layers
         kw["exchange"] = args.exchange
@@ -1229,7 +1258,8 @@ def main():
             "higher_is_better": True, "scaling": getattr(wl, "scaling", "weak"),
             "vs_baseline": None, "dtype": getattr(wl, "dtype", "bf16"),
             "data": "synthetic", "config": dict({"parallelism": (
-                "replicas" if world > 1 else "single GPU")}, **wl.config, graph=used_graph),
+                ("column split" if wl.config.get("split") else "replicas") if world > 1
+                else "single GPU")}, **wl.config, graph=used_graph),
             "roofline": roof, "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": wl.unit, "h2d_bytes_per_step": wl.h2d,
                     "d2h_bytes_per_step": wl.d2h},
