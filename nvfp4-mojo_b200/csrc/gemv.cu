@@ -3,7 +3,11 @@
 // batch_seq_len <= 8: nvfp4/deltanet.mojo:549-584, nvfp4/nvfp4_gemm_gpu.mojo:185-224).
 //
 // HBM-bound: every weight byte is read once, so the kernel is organised around
-// keeping enough bytes in flight with few instructions per byte.
+// keeping enough bytes in flight with few instructions per byte.  Two kernels
+// share the decode and MMA code below: gemv_kernel (the plain linear, and the
+// MoE experts' work items one cluster grid each where the persistent form
+// does not fit) and gemv_grouped_kernel (the MoE expert GEMMs as a
+// persistent grid, see its comment).  Notes on gemv_kernel:
 //
 //   * Two CTAs per SM.  A cluster of C CTAs (grid.x = C) splits K into C
 //     slices and reduces the fp32 partial sums through distributed shared
