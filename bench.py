@@ -506,7 +506,7 @@ class MoELayerBench:
         for L in self.layers:
             L.workspace(tokens, device)
         self.sets = len(self.layers)
-        self.launches_per_step = 7  # router x2, slot index, permute, gate_up, down, combine
+        self.launches_per_step = 6  # router x2, permute, gate_up, down, combine
         # Distinct experts touched: expectation under uniform routing.
         touched = MOE_E * (1.0 - (1.0 - MOE_K / MOE_E) ** tokens)
         self.dominant_bytes = touched * moe_expert_bytes()

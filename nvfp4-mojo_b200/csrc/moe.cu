@@ -344,7 +344,8 @@ cudaError_t launch_router(const uint16_t *x, const float *router, float *part, i
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(1024) moe_permute_kernel(const int32_t *__restrict__ row_expert,
                                                           const int32_t *__restrict__ x_row_index,
-                                                          int R, int E, int tpi, MoePlan plan) {
+                                                          int row_div, int R, int E, int tpi,
+                                                          MoePlan plan) {
   __shared__ int cnt[1024], off[1025], cur[1024], items[1025];
   const int tid = threadIdx.x;
   pdl_wait();  // the routing ids come from the previous kernels
@@ -424,7 +425,7 @@ __global__ void __launch_bounds__(1024) moe_permute_kernel(const int32_t *__rest
     const int e = i < 4 ? my_e[i] : __ldcg(row_expert + r);
     if (e >= 0 && e < E) {
       const int p = atomicAdd(&cur[e], 1);
-      plan.src_row[p] = x_row_index ? __ldcg(x_row_index + r) : r;
+      plan.src_row[p] = x_row_index ? __ldcg(x_row_index + r) : r / row_div;
       plan.dst_row[p] = r;
     }
   }
@@ -436,26 +437,16 @@ __global__ void __launch_bounds__(1024) moe_permute_kernel(const int32_t *__rest
   }
 }
 
-cudaError_t launch_moe_permute(const int32_t *row_expert, const int32_t *x_row_index, int R,
-                               int E, int tpi, const MoePlan &plan, cudaStream_t st) {
+cudaError_t launch_moe_permute(const int32_t *row_expert, const int32_t *x_row_index,
+                               int row_div, int R, int E, int tpi, const MoePlan &plan,
+                               cudaStream_t st) {
   if (E <= 0 || E > 256) return cudaErrorInvalidValue;  // the one-warp scan covers 256 experts
-  return launch_pdl(moe_permute_kernel, dim3(1), dim3(1024), 0, st, row_expert, x_row_index, R, E,
-                    tpi, plan);
+  if (row_div < 1) return cudaErrorInvalidValue;
+  return launch_pdl(moe_permute_kernel, dim3(1), dim3(1024), 0, st, row_expert, x_row_index,
+                    row_div, R, E, tpi, plan);
 }
 
 // Slot -> token index for the single-GPU forward: row r = t * k + j reads x[t].
-__global__ void slot_token_kernel(int32_t *__restrict__ idx, int R, int k) {
-  const int r = blockIdx.x * blockDim.x + threadIdx.x;
-  pdl_wait();  // keeps the chain of programmatic launches ordered
-  pdl_trigger();
-  if (r < R) idx[r] = r / k;
-}
-
-cudaError_t launch_slot_token(int32_t *idx, int R, int k, cudaStream_t st) {
-  if (R == 0) return cudaSuccess;
-  return launch_pdl(slot_token_kernel, dim3((R + 255) / 256), dim3(256), 0, st, idx, R, k);
-}
-
 // ---------------------------------------------------------------------------
 // Expert-parallel dispatch plan.  Slot r (= token r / k, choice r % k) goes to
 // rank dst = id / experts_per_rank as local expert id % experts_per_rank.

@@ -54,9 +54,11 @@ cudaError_t launch_router_logits(const uint16_t *x, const float *router, float *
 cudaError_t launch_router(const uint16_t *x, const float *router, float *part, int nslices,
                           float *logits_out, int T, int H, int E, int k, int renormalize,
                           int32_t *ids, float *w, cudaStream_t st);
-cudaError_t launch_moe_permute(const int32_t *row_expert, const int32_t *x_row_index, int R, int E,
+// Slot r's activation row: x_row_index[r], or r / row_div when it is null
+// (row_div = top_k: slot r of the layer is token r / k).
+cudaError_t launch_moe_permute(const int32_t *row_expert, const int32_t *x_row_index, int row_div,
+                               int R, int E,
                                int tpi, const MoePlan &plan, cudaStream_t st);
-cudaError_t launch_slot_token(int32_t *idx, int R, int k, cudaStream_t st);
 // extra (nullable): fp32 rows [T, H] added after the routed sum, before the
 // residual (the shared expert's output).
 cudaError_t launch_moe_combine(const void *ys, int ys_dtype, const float *w,

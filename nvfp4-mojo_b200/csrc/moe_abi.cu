@@ -92,7 +92,7 @@ ExpertsLayout experts_layout(const nvfp4_moe_desc &d, int64_t R) {
 }
 
 struct ForwardLayout {
-  size_t ids, w, logits, slot_tok, y_slot, experts, total;
+  size_t ids, w, logits, y_slot, experts, total;
 };
 
 ForwardLayout forward_layout(const nvfp4_moe_desc &d, int64_t T) {
@@ -105,8 +105,6 @@ ForwardLayout forward_layout(const nvfp4_moe_desc &d, int64_t T) {
   o = up(o + sizeof(float) * R);
   L.logits = o;  // router partial sums, one [T, E] slice per H slice
   o = up(o + sizeof(float) * T * d.num_experts * router_slices((int)T, d.hidden, d.num_experts));
-  L.slot_tok = o;
-  o = up(o + sizeof(int32_t) * R);
   L.y_slot = o;
   o = up(o + sizeof(float) * R * d.hidden);
   L.experts = o;
@@ -137,8 +135,10 @@ int check_weights(const nvfp4_moe_weights *w) {
   return NVFP4_OK;
 }
 
+// Slot r's activation row is x_row_index[r], or r / row_div when x_row_index
+// is null.
 int run_experts(const nvfp4_moe_desc &d, const nvfp4_moe_weights &w, const uint16_t *x,
-                const int32_t *x_row_index, const int32_t *row_expert, int64_t R,
+                const int32_t *x_row_index, int row_div, const int32_t *row_expert, int64_t R,
                 void *y_rows, int y_dtype, uint8_t *ws, cudaStream_t st) {
   if (R == 0) return NVFP4_OK;
   const ExpertsLayout L = experts_layout(d, R);
@@ -157,7 +157,8 @@ int run_experts(const nvfp4_moe_desc &d, const nvfp4_moe_weights &w, const uint1
   // relative per element on the MMA operand).
   uint16_t *inter = reinterpret_cast<uint16_t *>(ws + L.inter);
   uint16_t *inter_lo = reinterpret_cast<uint16_t *>(ws + L.inter_lo);
-  int rc = check_launch(launch_moe_permute(row_expert, x_row_index, (int)R, E, tpi, plan, st),
+  int rc = check_launch(launch_moe_permute(row_expert, x_row_index, row_div, (int)R, E, tpi, plan,
+                                           st),
                         "MoE permutation launch");
   if (rc) return rc;
 
@@ -363,7 +364,8 @@ extern "C" int nvfp4_moe_experts(const nvfp4_moe_desc *d, const nvfp4_moe_weight
   if (ws_bytes < experts_layout(*d, R).total)
     return fail(NVFP4_ERR_WORKSPACE, "workspace of %zu bytes, %zu needed", ws_bytes,
                 experts_layout(*d, R).total);
-  return run_experts(*d, *w, static_cast<const uint16_t *>(x), x_row_index, row_expert, R, y_rows,
+  return run_experts(*d, *w, static_cast<const uint16_t *>(x), x_row_index, 1, row_expert, R,
+                     y_rows,
                      y_dtype, static_cast<uint8_t *>(ws), static_cast<cudaStream_t>(stream));
 }
 
@@ -443,7 +445,7 @@ namespace {
 // expert id (0) and the x row (t) of each of its T slots, and its own expert
 // workspace.
 struct SharedLayout {
-  size_t y_shared, ids0, idx, experts, total;
+  size_t y_shared, ids0, experts, total;
 };
 
 nvfp4_moe_desc shared_desc(const nvfp4_moe_desc &d, int32_t shared_intermediate) {
@@ -461,8 +463,6 @@ SharedLayout shared_layout(const nvfp4_moe_desc &ds, int64_t T) {
   L.y_shared = o;
   o = up(o + sizeof(float) * T * ds.hidden);
   L.ids0 = o;
-  o = up(o + sizeof(int32_t) * T);
-  L.idx = o;
   o = up(o + sizeof(int32_t) * T);
   L.experts = o;
   o = up(o + experts_layout(ds, T).total);
@@ -503,7 +503,6 @@ int moe_forward_impl(const nvfp4_moe_desc *d, const nvfp4_moe_weights *w,
   int32_t *ids = topk_ids ? topk_ids : reinterpret_cast<int32_t *>(base + L.ids);
   float *tw = topk_w ? topk_w : reinterpret_cast<float *>(base + L.w);
   float *logits = reinterpret_cast<float *>(base + L.logits);
-  int32_t *slot_tok = reinterpret_cast<int32_t *>(base + L.slot_tok);
   float *y_slot = reinterpret_cast<float *>(base + L.y_slot);
   const int64_t R = T * d->top_k;
   rc = check_launch(launch_router(static_cast<const uint16_t *>(x), w->router, logits,
@@ -512,9 +511,8 @@ int moe_forward_impl(const nvfp4_moe_desc *d, const nvfp4_moe_weights *w,
                                   ids, tw, st),
                     "router launch");
   if (rc) return rc;
-  rc = check_launch(launch_slot_token(slot_tok, (int)R, d->top_k, st), "slot index launch");
-  if (rc) return rc;
-  rc = run_experts(*d, *w, static_cast<const uint16_t *>(x), slot_tok, ids, R, y_slot, kF32,
+  // Slot r = t * k + j reads token r / k (the permutation computes it).
+  rc = run_experts(*d, *w, static_cast<const uint16_t *>(x), nullptr, d->top_k, ids, R, y_slot, kF32,
                    base + L.experts, st);
   if (rc) return rc;
   float *y_shared = nullptr;
@@ -524,12 +522,10 @@ int moe_forward_impl(const nvfp4_moe_desc *d, const nvfp4_moe_weights *w,
     const SharedLayout SL = shared_layout(ds, T);
     y_shared = reinterpret_cast<float *>(sb + SL.y_shared);
     int32_t *ids0 = reinterpret_cast<int32_t *>(sb + SL.ids0);
-    int32_t *idx = reinterpret_cast<int32_t *>(sb + SL.idx);
     rc = check_launch(cudaMemsetAsync(ids0, 0, sizeof(int32_t) * T, st), "shared expert ids");
     if (rc) return rc;
-    rc = check_launch(launch_slot_token(idx, (int)T, 1, st), "shared expert rows");
-    if (rc) return rc;
-    rc = run_experts(ds, *shared, static_cast<const uint16_t *>(x), idx, ids0, T, y_shared, kF32,
+    rc = run_experts(ds, *shared, static_cast<const uint16_t *>(x), nullptr, 1, ids0, T, y_shared,
+                     kF32,
                      sb + SL.experts, st);
     if (rc) return rc;
   }
@@ -688,7 +684,7 @@ extern "C" int nvfp4_ep_p2p_forward(const nvfp4_moe_desc *d, const nvfp4_moe_wei
   float *out = nullptr;
   if ((rc = nvfp4_ep_p2p_rows(p, T, k, &recv_x, &recv_e, &out))) return rc;
   rc = run_experts(ep_local_desc(*d, p->world), *local, static_cast<const uint16_t *>(recv_x),
-                   nullptr, recv_e, (int64_t)p->world * T * k, out, kF32, base + L.experts, st);
+                   nullptr, 1, recv_e, (int64_t)p->world * T * k, out, kF32, base + L.experts, st);
   if (rc) return rc;
   if ((rc = nvfp4_ep_p2p_signal_done(p, stream))) return rc;
   return nvfp4_ep_p2p_combine(p, ids, tw, T, k, epr, residual, y, y_dtype, stream);

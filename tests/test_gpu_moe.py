@@ -91,11 +91,11 @@ def test_moe_config3(O, cuda, T):
     check_layer(O, wd, x, w, k=8)
 
 
-@pytest.mark.parametrize("E,H,I,T", [(8, 512, 3072, 5), (4, 8192, 256, 3)])
+@pytest.mark.parametrize("E,H,I,T", [(8, 512, 3072, 5), (4, 6144, 256, 3)])
 def test_moe_clustered_expert_gemv_fallback(O, cuda, E, H, I, T):
     """Shapes whose work-item activations do not fit beside a two-stage ring
     in one CTA's shared memory: the down GEMV (I = 3072) or the gate_up GEMV
-    (H = 8192) runs as one cluster grid per item instead of the persistent
+    (H = 6144) runs as one cluster grid per item instead of the persistent
     grouped kernel; the other GEMV of the layer stays persistent."""
     wd, x, w = setup(E=E, H=H, I=I, T=T, seed=400 + T)
     check_layer(O, wd, x, w, k=2)
