@@ -147,19 +147,27 @@ struct GemvChunk {
   uint32_t sg, sh;
 };
 
-__device__ __forceinline__ void gemv_fetch(GemvChunk &b, uint32_t codes, uint32_t scales, int rl,
-                                           int c) {
-  // 128-byte swizzle of the TMA box: 16-byte unit u of row r sits at u ^ (r & 7).
-  const int sw = rl & 7;
-  const uint32_t rg = codes + 128u * rl, rh = rg + 128u * 8;
-  const uint4 a0 = lds_v4(rg + 16u * ((2 * c) ^ sw)), a1 = lds_v4(rg + 16u * ((2 * c + 1) ^ sw));
-  const uint4 b0 = lds_v4(rh + 16u * ((2 * c) ^ sw)), b1 = lds_v4(rh + 16u * ((2 * c + 1) ^ sw));
+// The lane's words of two staged rows (byte offsets rowA, rowB of
+// 128-byte-swizzled rows: 16-byte unit u of a row whose box row index is R
+// sits at u ^ (R & 7), swA / swB) and their scale words.
+__device__ __forceinline__ void gemv_fetch_rows(GemvChunk &b, uint32_t rowA, uint32_t rowB,
+                                                int swA, int swB, uint32_t scA, uint32_t scB,
+                                                int c) {
+  const uint4 a0 = lds_v4(rowA + 16u * ((2 * c) ^ swA)), a1 = lds_v4(rowA + 16u * ((2 * c + 1) ^ swA));
+  const uint4 b0 = lds_v4(rowB + 16u * ((2 * c) ^ swB)), b1 = lds_v4(rowB + 16u * ((2 * c + 1) ^ swB));
   b.wg[0] = a0.x; b.wg[1] = a0.y; b.wg[2] = a0.z; b.wg[3] = a0.w;
   b.wg[4] = a1.x; b.wg[5] = a1.y; b.wg[6] = a1.z; b.wg[7] = a1.w;
   b.wh[0] = b0.x; b.wh[1] = b0.y; b.wh[2] = b0.z; b.wh[3] = b0.w;
   b.wh[4] = b1.x; b.wh[5] = b1.y; b.wh[6] = b1.z; b.wh[7] = b1.w;
-  b.sg = lds_u32(scales + 16u * rl + 4u * c);
-  b.sh = lds_u32(scales + 16u * (rl + 8) + 4u * c);
+  b.sg = lds_u32(scA);
+  b.sh = lds_u32(scB);
+}
+
+// Rows rl and rl + 8 of a warp's 16-row tile (codes: the tile's first row).
+__device__ __forceinline__ void gemv_fetch(GemvChunk &b, uint32_t codes, uint32_t scales, int rl,
+                                           int c) {
+  gemv_fetch_rows(b, codes + 128u * rl, codes + 128u * (rl + 8), rl & 7, rl & 7,
+                  scales + 16u * rl + 4u * c, scales + 16u * (rl + 8) + 4u * c, c);
 }
 
 // f16 multiply of the pair a by a scale pair already broadcast.
@@ -745,7 +753,11 @@ __global__ void __launch_bounds__(32 * (kGvMaxWarps + 1), 2)
 // meets few item changes and the items of one expert run side by side, their
 // weights shared through L2).  Row group q of an expert owns tiles
 // [q nt / G, (q + 1) nt / G): the groups differ by at most one tile, which
-// the two tensor maps (W and W - 1 tiles per part) cover.
+// the two tensor maps (W and W - 1 tiles) cover.  A tile is the 16 rows of
+// one MMA: kGvDown, 16 consecutive down rows; kGvGateUp, 8 gate rows and the
+// same 8 rows of up (MMA rows 0-7 and 8-15), so that every lane holds the
+// gate and the up sums of its output rows and applies silu(gate) * up in
+// registers (no exchange between warps, no barrier per unit).
 //
 // Nothing on the consumer warps' path reads global memory, whose latency
 // under the kernel's own TMA stream is several microseconds:
@@ -757,8 +769,7 @@ __global__ void __launch_bounds__(32 * (kGvMaxWarps + 1), 2)
 //   * for each item it copies the item's bf16 activation rows into shared
 //     memory with bulk copies (one item ahead), which the consumers then
 //     convert to scaled f16 in shared memory (gv_stage_units);
-//   * the consumer warps (one per 16-row tile of the row group; gate and up
-//     tiles of the same rows in kGvGateUp) accumulate over all of K in
+//   * the consumer warps (one per tile) accumulate over all of K in
 //     registers (no K split, no cluster reduction) and write their rows at
 //     the end of the unit.
 // ---------------------------------------------------------------------------
@@ -774,16 +785,16 @@ struct GgItem {
   int rows[kGvTok];
 };
 
-// Shared memory of a grouped CTA with w consumer warps, `stages` ring stages
-// (each: codes, blockscales and the weight_scale_2 rows of w tiles), K and
-// at most `items` items: the ring, the f16 activations of one item (twice
-// for hi + lo), a zero row (tokens >= M), the bf16 rows they are converted
-// from (twice for hi + lo),
-// kGvGateUp's two alternating buffers of per-row partial sums ([part][16 w /
-// 2 rows][8 tokens] fp32), the token scales, the item table, the mbarriers.
+// Shared memory of a grouped CTA with w consumer warps (tiles), `stages` ring
+// stages (each: codes, blockscales and the weight_scale_2 rows of w tiles;
+// kGvGateUp: the gate half of each at offset 0, the up half at half its
+// size), K and at most `items` items: the ring, the f16 activations of one
+// item (twice for hi + lo), a zero row (tokens >= M), the bf16 rows they are
+// converted from (twice for hi + lo), the token scales, the item table, the
+// mbarriers.
 struct GgSmem {
-  int stage, codes, ws2, xstride, xs, xs_lo, zero, raw, raw_lo, recv, inv, emax, items, bars, total;
-  __host__ __device__ GgSmem(int w, int stages, int K, int parts, bool split, int n_items) {
+  int stage, codes, ws2, xstride, xs, xs_lo, zero, raw, raw_lo, inv, emax, items, bars, total;
+  __host__ __device__ GgSmem(int w, int stages, int K, bool split, int n_items) {
     codes = w * kGvTileCodes;
     ws2 = codes + w * kGvTileScales;
     stage = (ws2 + 64 * w + 1023) & ~1023;
@@ -793,14 +804,20 @@ struct GgSmem {
     zero = xs_lo + (split ? kGvTok * xstride : 0);
     raw = zero + xstride;
     raw_lo = raw + kGvTok * 2 * K;
-    recv = raw_lo + (split ? kGvTok * 2 * K : 0);
-    inv = recv + (parts == 2 ? (int)sizeof(float) * 2 * 16 * w * kGvTok : 0);
+    inv = raw_lo + (split ? kGvTok * 2 * K : 0);
     emax = inv + (int)sizeof(float) * kGvTok;
     items = emax + (int)sizeof(int) * kGvTok;
     bars = (items + (int)sizeof(GgItem) * n_items + 7) & ~7;
     total = bars + 16 * stages + 16;
   }
 };
+
+// Rows of the weight matrix per tile: 16 (kGvDown), 8 of gate and the same 8
+// of up (kGvGateUp).
+template <int MODE>
+__host__ __device__ constexpr int gg_tile_rows() {
+  return MODE == kGvGateUp ? 8 : 16;
+}
 
 template <int MODE>
 __global__ void __launch_bounds__(32 * (kGvMaxWarps + 1), 1)
@@ -810,18 +827,18 @@ __global__ void __launch_bounds__(32 * (kGvMaxWarps + 1), 1)
                         const __grid_constant__ CUtensorMap tmS_lo, GemvArgs a) {
   static_assert(MODE == kGvGateUp || MODE == kGvDown, "grouped modes only");
   constexpr bool kSplit = MODE == kGvDown;
-  constexpr int kParts = MODE == kGvGateUp ? 2 : 1;
+  constexpr bool kPair = MODE == kGvGateUp;
+  constexpr int kTR = gg_tile_rows<MODE>();
   extern __shared__ __align__(1024) uint8_t gsm_raw[];
   uint8_t *gsm = reinterpret_cast<uint8_t *>(((uintptr_t)gsm_raw + 1023) & ~(uintptr_t)1023);
   __shared__ int abort_flag;
 
-  const int W = (int)(blockDim.x >> 5) - 1;  // consumer warps = kParts * tiles of a full group
+  const int W = (int)(blockDim.x >> 5) - 1;  // consumer warps = tiles of a full group
   const int S = a.stages;
-  const GgSmem L(W, S, a.K, kParts, kSplit, a.max_items);
+  const GgSmem L(W, S, a.K, kSplit, a.max_items);
   uint8_t *ring = gsm;
   uint8_t *xs = gsm + L.xs;
   uint8_t *xs_lo = gsm + L.xs_lo;
-  float *recv = reinterpret_cast<float *>(gsm + L.recv);
   float *inv_scale = reinterpret_cast<float *>(gsm + L.inv);
   int *emax = reinterpret_cast<int *>(gsm + L.emax);
   GgItem *tab = reinterpret_cast<GgItem *>(gsm + L.items);
@@ -830,9 +847,12 @@ __global__ void __launch_bounds__(32 * (kGvMaxWarps + 1), 1)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int gq = lane >> 2, c = lane & 3;
   const int G = a.ggroups;
-  const int nt = (MODE == kGvGateUp ? a.N / 2 : a.N + 15) / 16;
+  const int nt = kPair ? a.N / 2 / kTR : (a.N + kTR - 1) / kTR;
   const int nch = a.K / kGvChunk;
   const int rowb = 2 * a.K;  // bytes of one bf16 activation row
+  // kGvGateUp stage layout: the up half of codes, blockscales and
+  // weight_scale_2 starts half a full group's size after the gate half.
+  const uint32_t up_codes = 128u * kTR * W, up_scales = 16u * kTR * W, up_ws2 = 4u * kTR * W;
   const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + S);
   const uint32_t xfull = smem_u32(bars + 2 * S), xempty = smem_u32(bars + 2 * S + 1);
   const bool ws2_copy = a.al.ws2_rows != nullptr;
@@ -913,10 +933,12 @@ __global__ void __launch_bounds__(32 * (kGvMaxWarps + 1), 1)
           ++k;
         }
         const int tile0 = tile_lo(q), ntiles = tile_lo(q + 1) - tile0;
-        const bool full_count = kParts * ntiles == W;
+        const bool full_count = ntiles == W;
         const CUtensorMap *tmW = full_count ? &tmW_hi : &tmW_lo;
         const CUtensorMap *tmS = full_count ? &tmS_hi : &tmS_lo;
-        const int64_t grow0 = (int64_t)e.g * a.N + 16 * tile0;
+        const int64_t grow0 = (int64_t)e.g * a.N + kTR * tile0;
+        const int box_rows = kTR * ntiles;  // rows per box (per half in kGvGateUp)
+        constexpr int kHalves = kPair ? 2 : 1;
         for (int ch = 0; ch < nch; ++ch, ++gc) {
           const int s = gc % S, r = gc / S;
           if (r > 0 && !mbar_wait(empty0 + 8 * s, (r - 1) & 1, &g_gemv_status, kDevTimeoutEmpty,
@@ -926,20 +948,19 @@ __global__ void __launch_bounds__(32 * (kGvMaxWarps + 1), 1)
           }
           const uint32_t st = smem_u32(ring + s * L.stage);
           const bool w2 = ch == 0 && ws2_copy;
-          mbar_arrive_expect_tx(full0 + 8 * s, kParts * ntiles * (kGvTileCodes + kGvTileScales +
-                                                                  (w2 ? 64 : 0)));
+          mbar_arrive_expect_tx(full0 + 8 * s,
+                                kHalves * box_rows * (128 + 16 + (w2 ? 4 : 0)));
 #pragma unroll
-          for (int part = 0; part < kParts; ++part) {
-            const int row = (int)(grow0 + (part ? a.N / 2 : 0));
-            tma_load_2d_hint(st + part * ntiles * kGvTileCodes, tmW, ch * (kGvChunk / 2), row,
+          for (int h = 0; h < kHalves; ++h) {
+            const int row = (int)(grow0 + (h ? a.N / 2 : 0));
+            tma_load_2d_hint(st + h * up_codes, tmW, ch * (kGvChunk / 2), row, full0 + 8 * s, pol);
+            tma_load_2d_hint(st + L.codes + h * up_scales, tmS, ch * (kGvChunk / kGroup), row,
                              full0 + 8 * s, pol);
-            tma_load_2d_hint(st + L.codes + part * ntiles * kGvTileScales, tmS,
-                             ch * (kGvChunk / kGroup), row, full0 + 8 * s, pol);
             if (w2)
-              bulk_load(st + L.ws2 + part * ntiles * 64,
-                        a.al.ws2_rows + (int64_t)e.g * a.al.ws2_group_stride + 16 * tile0 +
-                            (part ? a.N / 2 : 0),
-                        ntiles * 64, full0 + 8 * s);
+              bulk_load(st + L.ws2 + h * up_ws2,
+                        a.al.ws2_rows + (int64_t)e.g * a.al.ws2_group_stride + kTR * tile0 +
+                            (h ? a.N / 2 : 0),
+                        4 * box_rows, full0 + 8 * s);
           }
         }
       }
@@ -952,21 +973,30 @@ __global__ void __launch_bounds__(32 * (kGvMaxWarps + 1), 1)
     return;
   }
 
-  // Consumers.  Every consumer warp takes every named barrier of every unit
-  // (after a timeout they skip the waits and the math, not the barriers).
+  // Consumers.  Every consumer warp takes every named barrier of every item
+  // change (after a timeout they skip the waits and the math, not the
+  // barriers).  Warp w's tile: MMA rows gq and gq + 8 of the lane are
+  // kGvDown, rows 16 w + gq and 16 w + gq + 8 of the row group; kGvGateUp,
+  // gate row 8 w + gq and up row 8 w + gq.
   const int nthr = 32 * W;
   const uint8_t *raw = gsm + L.raw, *raw_lo = gsm + L.raw_lo;
   auto load_raw = [&](int tt, int u, uint4 &v, uint4 &vl) {
     v = *reinterpret_cast<const uint4 *>(raw + tt * rowb + 16 * u);
     if constexpr (kSplit) vl = *reinterpret_cast<const uint4 *>(raw_lo + tt * rowb + 16 * u);
   };
-  int gc = 0, k = 0, buf = 0;
+  // This lane's two weight rows within a stage (row index in the box) and
+  // their byte offsets.
+  const int rA = kPair ? kTR * warp + gq : kTR * warp + gq;
+  const int rB = kPair ? kTR * warp + gq : kTR * warp + gq + 8;
+  const uint32_t offA = 128u * rA, offB = (kPair ? up_codes : 0u) + 128u * rB;
+  const uint32_t sofA = 16u * rA + 4u * c, sofB = (kPair ? up_scales : 0u) + 16u * rB + 4u * c;
+  const int swA = rA & 7, swB = rB & 7;
+  int gc = 0, k = 0;
   bool ok_all = true;
   for (int u = u_begin; u < u_end; ++u) {
     const int q = u % G;
     const GgItem &e = tab[u / G - i0];
-    const int g = e.g, slot0 = e.slot0, M = e.M;
-    const float ins = e.ins;
+    const int M = e.M;
     if (u == u_begin || q == 0) {
       asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");  // xs of the last item is dead
       if (ok_all) {
@@ -986,12 +1016,10 @@ __global__ void __launch_bounds__(32 * (kGvMaxWarps + 1), 1)
       ++k;
     }
     const int tile0 = tile_lo(q), ntiles = tile_lo(q + 1) - tile0;
-    const bool has_tile = warp < kParts * ntiles;
-    const int rows = 16 * ntiles;
-    // weight_scale_2 of the epilogue's rows, read from the unit's first stage:
-    // kGvDown, this lane's rows (h = 0, 1); kGvGateUp, the gate and up rows of
-    // this thread's first two (row, token) elements.
-    float w2a[2] = {a.al.ws2, a.al.ws2}, w2b[2] = {a.al.ws2, a.al.ws2};
+    const bool has_tile = warp < ntiles;
+    // weight_scale_2 of the lane's rows A and B, read from the unit's first
+    // stage (the stage is refilled later).
+    float w2a = a.al.ws2, w2b = a.al.ws2;
     const bool has_x = gq < M;  // tokens >= M: the zero row (zero B fragments)
     const uint32_t xrow = smem_u32(has_x ? xs + gq * L.xstride : gsm + L.zero);
     const uint32_t xrow_lo = smem_u32(has_x ? xs_lo + gq * L.xstride : gsm + L.zero);
@@ -1003,23 +1031,15 @@ __global__ void __launch_bounds__(32 * (kGvMaxWarps + 1), 1)
       ok_all = __all_sync(0xffffffffu, ok);
       if (!ok_all) continue;
       const uint32_t st = smem_u32(ring + s * L.stage);
-      if (ch == 0 && ws2_copy) {
+      if (ch == 0 && ws2_copy && has_tile) {
         const float *w2s = reinterpret_cast<const float *>(ring + s * L.stage + L.ws2);
-        if constexpr (MODE == kGvDown) {
-#pragma unroll
-          for (int h = 0; h < 2; ++h) w2a[h] = w2s[16 * warp + gq + 8 * h];
-        } else {
-#pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            const int i = tid + j * nthr;
-            w2a[j] = w2s[i % rows];
-            w2b[j] = w2s[rows + i % rows];
-          }
-        }
+        w2a = w2s[rA];
+        w2b = w2s[(kPair ? up_ws2 / 4 : 0) + rB];
       }
       GemvChunk bch;
       if (has_tile)
-        gemv_fetch(bch, st + warp * kGvTileCodes, st + L.codes + warp * kGvTileScales, gq, c);
+        gemv_fetch_rows(bch, st + offA, st + offB, swA, swB, st + L.codes + sofA,
+                        st + L.codes + sofB, c);
       fence_proxy_async_smem();  // generic reads before the TMA refill (see gemv_kernel)
       __syncwarp();
       if (lane == 0) mbar_arrive(empty0 + 8 * s);
@@ -1031,61 +1051,46 @@ __global__ void __launch_bounds__(32 * (kGvMaxWarps + 1), 1)
         for (int i = 0; i < 4; ++i) acc[i] += part[i];
       }
     }
+    if (!has_tile) continue;
     const float is0 = inv_scale[2 * c], is1 = inv_scale[2 * c + 1];
+    const float ins = e.ins;
     if constexpr (MODE == kGvDown) {
-      if (has_tile) {
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int n = 16 * (tile0 + warp) + gq + 8 * h;
-          if (n >= a.N) continue;
-          const float al = ins * w2a[h];
+      for (int h = 0; h < 2; ++h) {
+        const int n = kTR * (tile0 + warp) + gq + 8 * h;
+        if (n >= a.N) continue;
+        const float al = ins * (h ? w2b : w2a);
 #pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            const int tok = 2 * c + t;
-            if (tok >= M) continue;
-            const float v = acc[2 * h + t] * (t ? is1 : is0) * al;
-            const int64_t row = e.rows[tok];
-            if (a.y_dtype == kBF16)
-              reinterpret_cast<uint16_t *>(a.y)[row * a.y_ld + n] = f32_to_bf16_bits(v);
-            else
-              reinterpret_cast<float *>(a.y)[row * a.y_ld + n] = v;
-          }
+        for (int t = 0; t < 2; ++t) {
+          const int tok = 2 * c + t;
+          if (tok >= M) continue;
+          const float v = acc[2 * h + t] * (t ? is1 : is0) * al;
+          const int64_t row = e.rows[tok];
+          if (a.y_dtype == kBF16)
+            reinterpret_cast<uint16_t *>(a.y)[row * a.y_ld + n] = f32_to_bf16_bits(v);
+          else
+            reinterpret_cast<float *>(a.y)[row * a.y_ld + n] = v;
         }
       }
     } else {
-      // Gate and up sums of the unit's rows meet in shared memory (buffer
-      // `buf`; the two buffers alternate, so one barrier per unit orders the
-      // writes of a unit after the reads of the unit two back).
-      const int half = 16 * (W / 2);  // rows per part in a buffer
-      float *rb = recv + buf * (2 * half * kGvTok);
-      if (has_tile) {
-        const int part = warp / ntiles, wt = warp - part * ntiles;
+      // The lane's gate (acc[0..1]) and up (acc[2..3]) sums of output row n
+      // for tokens 2c, 2c + 1: silu(gate) * up as bf16 hi + lo (the down
+      // projection's operand).
+      const int n = kTR * (tile0 + warp) + gq;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          float *dst = rb + ((size_t)part * half + wt * 16 + gq + 8 * h) * kGvTok + 2 * c;
-          dst[0] = acc[2 * h] * is0;
-          dst[1] = acc[2 * h + 1] * is1;
-        }
-      }
-      asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
-      // rows * M <= 2 * nthr (rows <= 16 W / 2, M <= 8, nthr = 32 W).
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int i = tid + j * nthr;
-        if (i >= rows * M) break;
-        const int r = i % rows, tok = i / rows;
-        const int n = 16 * tile0 + r;
-        const float vg = rb[(size_t)r * kGvTok + tok] * (ins * w2a[j]);
-        const float vu = rb[((size_t)half + r) * kGvTok + tok] * (ins * w2b[j]);
-        // silu(gate) * up as bf16 hi + lo (the down projection's operand).
+      for (int t = 0; t < 2; ++t) {
+        const int tok = 2 * c + t;
+        if (tok >= M) continue;
+        const float is = t ? is1 : is0;
+        const float vg = acc[t] * is * (ins * w2a);
+        const float vu = acc[2 + t] * is * (ins * w2b);
         const float o = silu_f32(vg) * vu;
         const uint16_t hb = f32_to_bf16_bits(o);
         const float hf = __uint_as_float((uint32_t)hb << 16);
-        const int64_t idx = (int64_t)(slot0 + tok) * a.y_ld + n;
+        const int64_t idx = (int64_t)(e.slot0 + tok) * a.y_ld + n;
         reinterpret_cast<uint16_t *>(a.y)[idx] = hb;
         a.y_lo[idx] = f32_to_bf16_bits(o - hf);
       }
-      buf ^= 1;
     }
   }
 }
@@ -1271,20 +1276,19 @@ struct GgPlan {
 
 template <int MODE>
 bool grouped_plan(const GemvArgs &a, int items, GgPlan &p) {
-  constexpr int kParts = MODE == kGvGateUp ? 2 : 1;
   constexpr bool kSplit = MODE == kGvDown;
+  constexpr int kTR = gg_tile_rows<MODE>();
   const int N = a.N, K = a.K;
-  const int nt = (MODE == kGvGateUp ? N / 2 : N + 15) / 16;
-  const int max_tiles = kGvMaxWarps / kParts;
+  const int nt = MODE == kGvGateUp ? N / 2 / kTR : (N + kTR - 1) / kTR;
   auto al16 = [](const void *q) { return ((uintptr_t)q & 15) == 0; };
   // Bulk copies: 16-byte aligned activation rows; weight_scale_2 rows in
-  // 64-byte tiles (16 rows), each part's at a multiple of 16 rows.
+  // whole tiles (32 or 64 bytes), the up half at a multiple of 16 rows.
   if (nt <= 0 || K % kGvChunk || N % 32 || !al16(a.x) || (a.x_ld * 2) % 16 ||
       (kSplit && !al16(a.x_lo)) ||
       (a.al.ws2_rows && (!al16(a.al.ws2_rows) || a.al.ws2_group_stride % 16)))
     return false;
-  p.G = (nt + max_tiles - 1) / max_tiles;
-  p.W = kParts * ((nt + p.G - 1) / p.G);
+  p.G = (nt + kGvMaxWarps - 1) / kGvMaxWarps;
+  p.W = (nt + p.G - 1) / p.G;
   const int64_t units = (int64_t)items * p.G;
   p.P = (int)std::min<int64_t>(tc_sm_count(), units);
   if (p.P <= 0) return false;
@@ -1292,16 +1296,14 @@ bool grouped_plan(const GemvArgs &a, int items, GgPlan &p) {
   p.max_items = (int)(((units + p.P - 1) / p.P + p.G - 1) / p.G + 2);
   if (p.max_items > kGgMaxItems) return false;
   p.S = kGgMaxStages;
-  while (p.S >= 2 &&
-         1024 + GgSmem(p.W, p.S, K, kParts, kSplit, p.max_items).total > kGgSmemCap)
-    --p.S;
+  while (p.S >= 2 && 1024 + GgSmem(p.W, p.S, K, kSplit, p.max_items).total > kGgSmemCap) --p.S;
   return p.S >= 2;
 }
 
 template <int MODE>
 cudaError_t launch_grouped(GemvArgs a, const GgPlan &p, int64_t total_rows, cudaStream_t st) {
-  constexpr int kParts = MODE == kGvGateUp ? 2 : 1;
   constexpr bool kSplit = MODE == kGvDown;
+  constexpr int kTR = gg_tile_rows<MODE>();
   {
     static std::mutex mu;
     static bool attr_set[64] = {};
@@ -1321,12 +1323,12 @@ cudaError_t launch_grouped(GemvArgs a, const GgPlan &p, int64_t total_rows, cuda
   a.stages = p.S;
   a.ggroups = p.G;
   a.max_items = p.max_items;
-  // Boxes of W / kParts and one tile fewer per part (row groups differ by at
-  // most one tile).
+  // Boxes of W tiles and of one tile fewer (row groups differ by at most one
+  // tile); kTR rows per tile (per half in kGvGateUp).
   CUtensorMap tm[4];
   for (int i = 0; i < 2; ++i) {
-    const int t = p.W / kParts - i;
-    const int rows = 16 * (t > 0 ? t : 1);
+    const int t = p.W - i;
+    const int rows = kTR * (t > 0 ? t : 1);
     if (!make_tmap_2d(&tm[2 * i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.w, total_rows, a.K / 2,
                       a.K / 2, kGvChunk / 2, rows, CU_TENSOR_MAP_SWIZZLE_128B) ||
         !make_tmap_2d(&tm[2 * i + 1], CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.sf, total_rows,
@@ -1337,7 +1339,7 @@ cudaError_t launch_grouped(GemvArgs a, const GgPlan &p, int64_t total_rows, cuda
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.P, 1, 1);
   cfg.blockDim = dim3(32 * (p.W + 1), 1, 1);
-  cfg.dynamicSmemBytes = 1024 + (size_t)GgSmem(p.W, p.S, a.K, kParts, kSplit, p.max_items).total;
+  cfg.dynamicSmemBytes = 1024 + (size_t)GgSmem(p.W, p.S, a.K, kSplit, p.max_items).total;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
