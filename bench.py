@@ -748,11 +748,11 @@ class EPStackBench:
         g.manual_seed(77 + rank)
         self.x = torch.randn((self.T_local, MOE_H), generator=g, device=device).to(torch.bfloat16)
         if exchange == "p2p":
-            # router logits, top-k + dispatch, wait, permutation, 2 expert GEMVs,
+            # router logits, top-k + dispatch + wait, permutation, 2 expert GEMVs,
             # done signal, combine
             self.graphable = True
             self.exchange = "peer memory, CUDA graph"
-            self.launches_per_step = layers * 8
+            self.launches_per_step = layers * 7
         else:
             # Fixed-capacity exchange (no host-side counts) for small batches:
             # the whole step, NCCL calls included, is replayed from a CUDA graph.
@@ -787,7 +787,7 @@ class EPStackBench:
         achieved = self.layer_bytes / layer_s / 1e9
         return {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": achieved / peaks["hbm_gbs"],
-                # The committed capture is of one layer at one GPU (its 8 launches).
+                # The committed capture is of one layer at one GPU (its 7 launches).
                 "traffic": load_traffic(self.name) if self.world == 1 and self.exchange.startswith(
                     "peer") else None,
                 "kernel": (f"one expert-parallel MoE layer ({self.launches_per_step // self.n_layers}"

@@ -160,6 +160,23 @@ __device__ __forceinline__ uint32_t atom_add_acq_rel_sys(uint32_t *p, uint32_t v
   return old;
 }
 
+// Step 3 in the lanes of one warp: lane p waits for rank p's dispatch flag
+// and checks that rank p stored as many rows as this rank did (the fixed row
+// layout needs the same T on every rank), then lane 0 advances the step
+// counter (also after a timeout or a shape mismatch, which the error word
+// records).
+__device__ __forceinline__ void wait_dispatch_warp(const PeerTable &P, EpCtrl *own, uint32_t step,
+                                                   int lane) {
+  if (lane < P.world) {
+    if (!wait_flag(&own->flag_dispatch[lane], step, P.timeout_ns))
+      atomicOr(&own->error, NVFP4_EP_ERR_DISPATCH_TIMEOUT | (1u << (8 + lane)));
+    else if (ld_acquire_sys(&own->rows_from[lane]) != ld_acquire_sys(&own->rows_from[P.rank]))
+      atomicOr(&own->error, NVFP4_EP_ERR_SHAPE | (1u << (8 + lane)));
+  }
+  __syncwarp();
+  if (lane == 0) own->epoch = step;
+}
+
 // Publication of a dispatch.  After the block barrier, thread 0 counts the
 // block with a release (acq_rel, system scope) add on the rank's own block
 // counter: the release is cumulative over the block's peer stores, which the
@@ -170,15 +187,29 @@ __device__ __forceinline__ uint32_t atom_add_acq_rel_sys(uint32_t *p, uint32_t v
 // rank's dispatch flag in every window with st.release.sys, after the row
 // count R (so that every owner can check that all ranks step with the same
 // T); each release is cumulative over all it acquired.
+// With `wait_all`, the completing block's first warp then runs step 3
+// (wait_dispatch_warp): the launch ends once every rank has dispatched, and
+// the separate wait launch is not needed.  The other blocks are done by then,
+// so the wait holds one block; it waits only on flags that other GPUs' kernels
+// raise (or, for this rank's own flag, its thread 0 just did).
 __device__ __forceinline__ void dispatch_publish(const PeerTable &P, char *const *s_win,
-                                                 EpCtrl *own, uint32_t step, int R) {
+                                                 EpCtrl *own, uint32_t step, int R,
+                                                 bool wait_all) {
+  __shared__ int s_last;
   __syncthreads();
-  if (threadIdx.x == 0 && atom_add_acq_rel_sys(&own->blocks_done, 1u) == gridDim.x - 1) {
-    own->blocks_done = 0;  // the next step's launch starts after this one
-    for (int r = 0; r < P.world; ++r) ctrl_of(s_win[r])->rows_from[P.rank] = (uint32_t)R;
-    for (int r = 0; r < P.world; ++r)
-      st_release_sys(&ctrl_of(s_win[r])->flag_dispatch[P.rank], step);
+  if (threadIdx.x == 0) {
+    const bool last = atom_add_acq_rel_sys(&own->blocks_done, 1u) == gridDim.x - 1;
+    if (last) {
+      own->blocks_done = 0;  // the next step's launch starts after this one
+      for (int r = 0; r < P.world; ++r) ctrl_of(s_win[r])->rows_from[P.rank] = (uint32_t)R;
+      for (int r = 0; r < P.world; ++r)
+        st_release_sys(&ctrl_of(s_win[r])->flag_dispatch[P.rank], step);
+    }
+    s_last = last;
   }
+  if (!wait_all) return;
+  __syncthreads();
+  if (s_last && threadIdx.x < 32) wait_dispatch_warp(P, own, step, threadIdx.x);
 }
 
 // Step 2: one warp per slot s = t*k + j of this rank (dispatch_slot); the
@@ -198,7 +229,7 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(PeerTable P, const int
   const int lane = threadIdx.x & 31;
   for (int s = blockIdx.x * 8 + (threadIdx.x >> 5); s < R; s += gridDim.x * 8)
     dispatch_slot(P, s_win, s, __ldcg(ids + s), R, k, epr, x, lane);
-  dispatch_publish(P, s_win, own, step, R);
+  dispatch_publish(P, s_win, own, step, R, false);
 }
 
 // Top-k + step 2 in one launch, one block per token t: warp 0 runs the
@@ -206,13 +237,15 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(PeerTable P, const int
 // the router's own top-k kernel, router_topk.cuh) into the ids / weights of
 // the combine and the block's shared memory, then the block's warps dispatch
 // its k slots (dispatch_slot) and the flag goes up as in ep_dispatch_kernel.
-// One kernel boundary less than top-k, dispatch.
+// With `wait_all` the completing block also runs step 3 (dispatch_publish).
+// Two kernel boundaries less than top-k, dispatch, wait.
 __global__ void __launch_bounds__(256) ep_topk_dispatch_kernel(PeerTable P, const float *__restrict__ part,
                                                                int nslices,
                                                                const uint4 *__restrict__ x, int T,
                                                                int k, int renormalize, int epr,
                                                                int32_t *__restrict__ ids,
-                                                               float *__restrict__ w) {
+                                                               float *__restrict__ w,
+                                                               int wait_all) {
   __shared__ char *s_win[kMaxWorld];
   __shared__ int32_t s_ids[32];
   pdl_wait();  // the partial logits, x and the step counter come from earlier kernels
@@ -240,27 +273,16 @@ __global__ void __launch_bounds__(256) ep_topk_dispatch_kernel(PeerTable P, cons
   if (t < T)
     for (int j = warp; j < k; j += blockDim.x >> 5)
       dispatch_slot(P, s_win, t * k + j, s_ids[j], R, k, epr, x, lane);
-  dispatch_publish(P, s_win, own, step, R);
+  dispatch_publish(P, s_win, own, step, R, wait_all);
 }
 
-// Step 3: one warp; lane p waits for rank p's dispatch flag and checks that
-// rank p stored as many rows as this rank did (the fixed row layout needs the
-// same T on every rank), then the step counter advances (also after a timeout
-// or a shape mismatch, which the error word records).
+// Step 3 as its own launch (for callers that dispatch with
+// ep_dispatch_kernel): one warp, wait_dispatch_warp.
 __global__ void ep_wait_dispatch_kernel(PeerTable P) {
   pdl_wait();
   pdl_trigger();
   EpCtrl *own = ctrl_of(win_at(P, P.rank));
-  const int lane = threadIdx.x;
-  const uint32_t step = __ldcg(&own->epoch) + 1;
-  if (lane < P.world) {
-    if (!wait_flag(&own->flag_dispatch[lane], step, P.timeout_ns))
-      atomicOr(&own->error, NVFP4_EP_ERR_DISPATCH_TIMEOUT | (1u << (8 + lane)));
-    else if (ld_acquire_sys(&own->rows_from[lane]) != ld_acquire_sys(&own->rows_from[P.rank]))
-      atomicOr(&own->error, NVFP4_EP_ERR_SHAPE | (1u << (8 + lane)));
-  }
-  __syncwarp();
-  if (lane == 0) own->epoch = step;
+  wait_dispatch_warp(P, own, __ldcg(&own->epoch) + 1, threadIdx.x);
 }
 
 // Step 5: the expert rows of this step (written by the kernels before this
@@ -277,7 +299,10 @@ __global__ void ep_signal_done_kernel(PeerTable P) {
 // Step 6: every block first waits for all done flags (threads 0..world-1),
 // then thread (t, 8-column group) sums its slots in j order, loading each
 // slot's fp32 row from the window of the rank that computed it: the
-// arithmetic of the single-GPU combine, bit for bit.
+// arithmetic of the single-GPU combine, bit for bit.  (Step 5 stays a launch
+// of its own: raised by every combine block before its wait, the done signal
+// took the combine from 5.6 to 19 us on the critical path, against 3.3 us for
+// the separate signal kernel.)
 template <typename OutT>
 __global__ void __launch_bounds__(256) ep_combine_kernel(PeerTable P, const int32_t *__restrict__ ids,
                                                          const float *__restrict__ w,
@@ -400,7 +425,7 @@ int check_step(const nvfp4_ep_peers *p, int64_t T, int32_t k, int32_t epr) {
 
 int ep_p2p_topk_dispatch(const nvfp4_ep_peers *p, const uint16_t *x, const float *part,
                          int nslices, int64_t T, int k, int renormalize, int epr, int32_t *ids,
-                         float *w, cudaStream_t st) {
+                         float *w, bool wait_all, cudaStream_t st) {
   int rc = check_step(p, T, k, epr);
   if (rc) return rc;
   if (T > 0 && (!x || !part || !ids || !w))
@@ -412,8 +437,8 @@ int ep_p2p_topk_dispatch(const nvfp4_ep_peers *p, const uint16_t *x, const float
   const unsigned blocks = (unsigned)std::max<int64_t>(1, T);
   return check_launch(launch_pdl(ep_topk_dispatch_kernel, dim3(blocks), dim3(256), 0, st,
                                  make_table(*p), part, nslices, reinterpret_cast<const uint4 *>(x),
-                                 (int)T, k, renormalize, epr, ids, w),
-                      "top-k + dispatch launch");
+                                 (int)T, k, renormalize, epr, ids, w, (int)wait_all),
+                      wait_all ? "top-k + dispatch + wait launch" : "top-k + dispatch launch");
 }
 
 }  // namespace nvfp4

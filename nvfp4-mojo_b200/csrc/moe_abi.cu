@@ -665,7 +665,9 @@ extern "C" int nvfp4_ep_p2p_forward(const nvfp4_moe_desc *d, const nvfp4_moe_wei
   float *tw = reinterpret_cast<float *>(base + L.w);
   const int epr = d->num_experts / p->world, k = d->top_k;
   // Every rank takes every step, also with no tokens: the peers wait on its
-  // flags.  The top-k runs inside the dispatch kernel.
+  // flags.  Seven launches: router logits; top-k + dispatch + the wait for
+  // every rank's dispatch; the expert pass (permutation, gate_up, down); the
+  // done signal; the combine.
   float *part = reinterpret_cast<float *>(base + L.part);
   int nslices = 1;
   if (T > 0) {
@@ -676,9 +678,8 @@ extern "C" int nvfp4_ep_p2p_forward(const nvfp4_moe_desc *d, const nvfp4_moe_wei
     if (rc) return rc;
   }
   if ((rc = ep_p2p_topk_dispatch(p, static_cast<const uint16_t *>(x), part, nslices, T, k,
-                                 d->renormalize, epr, ids, tw, st)))
+                                 d->renormalize, epr, ids, tw, true, st)))
     return rc;
-  if ((rc = nvfp4_ep_p2p_wait_dispatch(p, stream))) return rc;
   void *recv_x = nullptr;
   int32_t *recv_e = nullptr;
   float *out = nullptr;
