@@ -8,7 +8,9 @@
 // read-modify-write that the publishing thread acquires), and publishes them
 // with one st.release.sys of a flag in that window; the owner polls its own flags
 // with ld.acquire.sys (local memory, bounded by time) and every later read
-// of the published rows follows that acquire in the same stream.  All waits
+// of the published rows follows that acquire in the same stream.  With one
+// rank every window is this GPU's own memory and the same releases and
+// acquires are taken at GPU scope.  All waits
 // are on this GPU's memory, all signals are remote stores, so no kernel ever
 // waits on another kernel of its own GPU.  Every kernel here is launched with
 // programmatic dependent launch and executes griddepcontrol.wait before it
@@ -71,14 +73,23 @@ struct PeerTable {
   uint64_t timeout_ns;
 };
 
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+// The control words are ordered at system scope when the windows span GPUs
+// (`sys`: world > 1, peers over NVLink) and at GPU scope when every window is
+// this GPU's own memory (world 1), where that order is all a reader needs.
+__device__ __forceinline__ uint32_t ld_acquire(const uint32_t *p, bool sys) {
   uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  if (sys)
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  else
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
 
-__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_release(uint32_t *p, uint32_t v, bool sys) {
+  if (sys)
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+  else
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 // Eight fp32 from another rank's window: system-scope (volatile) loads, so
@@ -101,11 +112,11 @@ __device__ __forceinline__ uint64_t global_ns() {
 // Polls `flag` until it reaches `step` (wrap-safe).  Bounded twice: by the
 // global timer and, should that timer not advance, by an iteration count
 // (each iteration sleeps >= 64 ns).  Returns false when it gave up.
-__device__ bool wait_flag(const uint32_t *flag, uint32_t step, uint64_t timeout_ns) {
+__device__ bool wait_flag(const uint32_t *flag, uint32_t step, uint64_t timeout_ns, bool sys) {
   const uint64_t t0 = global_ns();
   const uint64_t max_iter = timeout_ns / 64 + 1024;
   for (uint64_t it = 0;; ++it) {
-    if ((int32_t)(ld_acquire_sys(flag) - step) >= 0) return true;
+    if ((int32_t)(ld_acquire(flag, sys) - step) >= 0) return true;
     if (global_ns() - t0 > timeout_ns || it >= max_iter) return false;
     __nanosleep(64);
   }
@@ -154,9 +165,14 @@ __device__ __forceinline__ void dispatch_slot(const PeerTable &P, char *const *s
   }
 }
 
-__device__ __forceinline__ uint32_t atom_add_acq_rel_sys(uint32_t *p, uint32_t v) {
+__device__ __forceinline__ uint32_t atom_add_acq_rel(uint32_t *p, uint32_t v, bool sys) {
   uint32_t old;
-  asm volatile("atom.acq_rel.sys.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  if (sys)
+    asm volatile("atom.acq_rel.sys.global.add.u32 %0, [%1], %2;"
+                 : "=r"(old) : "l"(p), "r"(v) : "memory");
+  else
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;"
+                 : "=r"(old) : "l"(p), "r"(v) : "memory");
   return old;
 }
 
@@ -167,10 +183,11 @@ __device__ __forceinline__ uint32_t atom_add_acq_rel_sys(uint32_t *p, uint32_t v
 // records).
 __device__ __forceinline__ void wait_dispatch_warp(const PeerTable &P, EpCtrl *own, uint32_t step,
                                                    int lane) {
+  const bool sys = P.world > 1;
   if (lane < P.world) {
-    if (!wait_flag(&own->flag_dispatch[lane], step, P.timeout_ns))
+    if (!wait_flag(&own->flag_dispatch[lane], step, P.timeout_ns, sys))
       atomicOr(&own->error, NVFP4_EP_ERR_DISPATCH_TIMEOUT | (1u << (8 + lane)));
-    else if (ld_acquire_sys(&own->rows_from[lane]) != ld_acquire_sys(&own->rows_from[P.rank]))
+    else if (ld_acquire(&own->rows_from[lane], sys) != ld_acquire(&own->rows_from[P.rank], sys))
       atomicOr(&own->error, NVFP4_EP_ERR_SHAPE | (1u << (8 + lane)));
   }
   __syncwarp();
@@ -198,12 +215,13 @@ __device__ __forceinline__ void dispatch_publish(const PeerTable &P, char *const
   __shared__ int s_last;
   __syncthreads();
   if (threadIdx.x == 0) {
-    const bool last = atom_add_acq_rel_sys(&own->blocks_done, 1u) == gridDim.x - 1;
+    const bool sys = P.world > 1;
+    const bool last = atom_add_acq_rel(&own->blocks_done, 1u, sys) == gridDim.x - 1;
     if (last) {
       own->blocks_done = 0;  // the next step's launch starts after this one
       for (int r = 0; r < P.world; ++r) ctrl_of(s_win[r])->rows_from[P.rank] = (uint32_t)R;
       for (int r = 0; r < P.world; ++r)
-        st_release_sys(&ctrl_of(s_win[r])->flag_dispatch[P.rank], step);
+        st_release(&ctrl_of(s_win[r])->flag_dispatch[P.rank], step, sys);
     }
     s_last = last;
   }
@@ -292,8 +310,13 @@ __global__ void ep_signal_done_kernel(PeerTable P) {
   pdl_trigger();
   EpCtrl *own = ctrl_of(win_at(P, P.rank));
   const uint32_t step = __ldcg(&own->epoch);
-  __threadfence_system();
-  if (threadIdx.x < P.world) st_release_sys(&ctrl_of(win_at(P, threadIdx.x))->flag_done[P.rank], step);
+  const bool sys = P.world > 1;
+  if (sys)
+    __threadfence_system();
+  else
+    __threadfence();
+  if (threadIdx.x < P.world)
+    st_release(&ctrl_of(win_at(P, threadIdx.x))->flag_done[P.rank], step, sys);
 }
 
 // Step 6: every block first waits for all done flags (threads 0..world-1),
@@ -319,7 +342,7 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(PeerTable P, const int3
   if (threadIdx.x < kMaxWorld) {
     const int p = threadIdx.x < P.world ? threadIdx.x : 0;
     s_out[threadIdx.x] = reinterpret_cast<const float *>(win_at(P, p) + P.off_out);
-    if (threadIdx.x < P.world && !wait_flag(&own->flag_done[p], step, P.timeout_ns)) {
+    if (threadIdx.x < P.world && !wait_flag(&own->flag_done[p], step, P.timeout_ns, P.world > 1)) {
       atomicOr(&own->error, NVFP4_EP_ERR_DONE_TIMEOUT | (1u << (8 + p)));
       s_ok = 0;
     }
