@@ -135,16 +135,17 @@ __device__ __forceinline__ char *win_at(const PeerTable &P, int r) {
 
 // One warp: slot s (expert e) of this rank.  The row of x[s / k] goes to row
 // rank*R + s of the destination's window, the expert id to the same row of
-// every window (-1 where the slot does not go).
+// every window (-1 where the slot does not go).  Without `rows` only the ids
+// are stored (one rank: the expert pass reads x[s / k] itself).
 __device__ __forceinline__ void dispatch_slot(const PeerTable &P, char *const *s_win, int s, int e,
                                               int R, int k, int epr, const uint4 *__restrict__ x,
-                                              int lane) {
+                                              int lane, bool rows) {
   const int E = epr * P.world, row_v = P.H / 8;  // uint4 per bf16 row
   const int d = (e >= 0 && e < E) ? e / epr : -1;
   const int64_t row = (int64_t)P.rank * R + s;
   if (lane < P.world)
     reinterpret_cast<int32_t *>(s_win[lane] + P.off_expert)[row] = lane == d ? e - d * epr : -1;
-  if (d < 0) return;
+  if (d < 0 || !rows) return;
   const uint4 *src = x + (int64_t)(s / k) * row_v;
   uint4 *dst = reinterpret_cast<uint4 *>(s_win[d] + P.off_x) + row * row_v;
   // All of this lane's loads before any store: the store pointer may alias
@@ -246,7 +247,7 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(PeerTable P, const int
   const int R = T * k;
   const int lane = threadIdx.x & 31;
   for (int s = blockIdx.x * 8 + (threadIdx.x >> 5); s < R; s += gridDim.x * 8)
-    dispatch_slot(P, s_win, s, __ldcg(ids + s), R, k, epr, x, lane);
+    dispatch_slot(P, s_win, s, __ldcg(ids + s), R, k, epr, x, lane, true);
   dispatch_publish(P, s_win, own, step, R, false);
 }
 
@@ -255,7 +256,8 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(PeerTable P, const int
 // the router's own top-k kernel, router_topk.cuh) into the ids / weights of
 // the combine and the block's shared memory, then the block's warps dispatch
 // its k slots (dispatch_slot) and the flag goes up as in ep_dispatch_kernel.
-// With `wait_all` the completing block also runs step 3 (dispatch_publish).
+// With `wait_all` the completing block also runs step 3 (dispatch_publish);
+// without `copy_rows` (one rank) the slots carry only their expert ids.
 // Two kernel boundaries less than top-k, dispatch, wait.
 __global__ void __launch_bounds__(256) ep_topk_dispatch_kernel(PeerTable P, const float *__restrict__ part,
                                                                int nslices,
@@ -263,7 +265,7 @@ __global__ void __launch_bounds__(256) ep_topk_dispatch_kernel(PeerTable P, cons
                                                                int k, int renormalize, int epr,
                                                                int32_t *__restrict__ ids,
                                                                float *__restrict__ w,
-                                                               int wait_all) {
+                                                               int wait_all, int copy_rows) {
   __shared__ char *s_win[kMaxWorld];
   __shared__ int32_t s_ids[32];
   pdl_wait();  // the partial logits, x and the step counter come from earlier kernels
@@ -290,7 +292,7 @@ __global__ void __launch_bounds__(256) ep_topk_dispatch_kernel(PeerTable P, cons
   const int R = T * k;
   if (t < T)
     for (int j = warp; j < k; j += blockDim.x >> 5)
-      dispatch_slot(P, s_win, t * k + j, s_ids[j], R, k, epr, x, lane);
+      dispatch_slot(P, s_win, t * k + j, s_ids[j], R, k, epr, x, lane, copy_rows != 0);
   dispatch_publish(P, s_win, own, step, R, wait_all);
 }
 
@@ -448,19 +450,22 @@ int check_step(const nvfp4_ep_peers *p, int64_t T, int32_t k, int32_t epr) {
 
 int ep_p2p_topk_dispatch(const nvfp4_ep_peers *p, const uint16_t *x, const float *part,
                          int nslices, int64_t T, int k, int renormalize, int epr, int32_t *ids,
-                         float *w, bool wait_all, cudaStream_t st) {
+                         float *w, bool wait_all, bool copy_rows, cudaStream_t st) {
   int rc = check_step(p, T, k, epr);
   if (rc) return rc;
   if (T > 0 && (!x || !part || !ids || !w))
     return fail(NVFP4_ERR_INVALID_ARG, "null activations, logits, ids or weights");
   if (!aligned(x, 16)) return fail(NVFP4_ERR_INVALID_ARG, "x must be 16-byte aligned");
+  if (!copy_rows && p->world != 1)
+    return fail(NVFP4_ERR_INVALID_ARG, "a dispatch without its rows needs world 1");
   if (epr * p->world > 256 || nslices < 1)
     return fail(NVFP4_ERR_INVALID_ARG, "the fused top-k takes at most 256 experts");
   // At least one block, so the flags go up even for an empty step.
   const unsigned blocks = (unsigned)std::max<int64_t>(1, T);
   return check_launch(launch_pdl(ep_topk_dispatch_kernel, dim3(blocks), dim3(256), 0, st,
                                  make_table(*p), part, nslices, reinterpret_cast<const uint4 *>(x),
-                                 (int)T, k, renormalize, epr, ids, w, (int)wait_all),
+                                 (int)T, k, renormalize, epr, ids, w, (int)wait_all,
+                                 (int)copy_rows),
                       wait_all ? "top-k + dispatch + wait launch" : "top-k + dispatch launch");
 }
 

@@ -70,10 +70,12 @@ cudaError_t launch_moe_combine(const void *ys, int ys_dtype, const float *w,
 // the token's softmax top-k (router_topk.cuh) and dispatches its slots into
 // the peers' windows.  Writes ids / weights [T, k] for the combine.  With
 // wait_all the launch also waits for every rank's dispatch (the step of
-// nvfp4_ep_p2p_wait_dispatch).
+// nvfp4_ep_p2p_wait_dispatch); without copy_rows (world 1 only) it stores the
+// slots' expert ids but not their rows, which the expert pass then reads from
+// x (slot s is token s / k).
 int ep_p2p_topk_dispatch(const nvfp4_ep_peers *p, const uint16_t *x, const float *part,
                          int nslices, int64_t T, int k, int renormalize, int epr, int32_t *ids,
-                         float *w, bool wait_all, cudaStream_t st);
+                         float *w, bool wait_all, bool copy_rows, cudaStream_t st);
 cudaError_t launch_ep_plan(const int32_t *ids, int R, int k, int epr, int world, int32_t *counts,
                            int32_t *send_token, int32_t *send_expert, int32_t *slot_pos,
                            cudaStream_t st);

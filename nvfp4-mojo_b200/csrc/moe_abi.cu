@@ -677,15 +677,19 @@ extern "C" int nvfp4_ep_p2p_forward(const nvfp4_moe_desc *d, const nvfp4_moe_wei
                       "router launch");
     if (rc) return rc;
   }
+  // One rank: the expert pass reads the token rows from x (slot s = token
+  // s / k) and the dispatch stores only the slots' expert ids.
+  const bool one_rank = p->world == 1;
   if ((rc = ep_p2p_topk_dispatch(p, static_cast<const uint16_t *>(x), part, nslices, T, k,
-                                 d->renormalize, epr, ids, tw, true, st)))
+                                 d->renormalize, epr, ids, tw, true, !one_rank, st)))
     return rc;
   void *recv_x = nullptr;
   int32_t *recv_e = nullptr;
   float *out = nullptr;
   if ((rc = nvfp4_ep_p2p_rows(p, T, k, &recv_x, &recv_e, &out))) return rc;
-  rc = run_experts(ep_local_desc(*d, p->world), *local, static_cast<const uint16_t *>(recv_x),
-                   nullptr, 1, recv_e, (int64_t)p->world * T * k, out, kF32, base + L.experts, st);
+  rc = run_experts(ep_local_desc(*d, p->world), *local,
+                   static_cast<const uint16_t *>(one_rank ? x : recv_x), nullptr, one_rank ? k : 1,
+                   recv_e, (int64_t)p->world * T * k, out, kF32, base + L.experts, st);
   if (rc) return rc;
   if ((rc = nvfp4_ep_p2p_signal_done(p, stream))) return rc;
   return nvfp4_ep_p2p_combine(p, ids, tw, T, k, epr, residual, y, y_dtype, stream);
